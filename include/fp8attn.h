@@ -1,0 +1,124 @@
+/*
+ * fp8attn -- B200 (sm_100a) FP8 PagedAttention hot path behind a plain C ABI.
+ *
+ * Three entry points replace the three GPU kernels of nano-vLLM's FP8 KV-cache attention path
+ * (Lin-so/my-nano-vllm); the Python signatures they sit behind are kept verbatim by the
+ * `nanovllm_b200` package:
+ *
+ *   fp8attn_store_kvcache  <- store_kvcache          nanovllm/layers/attention.py:33-40
+ *                             (kernel store_kvcache_kernel, :11-31)
+ *   fp8attn_decode         <- fp8_decode_attention   nanovllm/kernels/fp8_attention.py:173-207
+ *                             (kernel fp8_paged_attention_decode_kernel, :88-171)
+ *   fp8attn_prefill        <- fp8_prefill_attention  nanovllm/kernels/fp8_attention.py:314-353
+ *                             (kernel fp8_paged_attention_prefill_kernel, :209-312)
+ *
+ * Conventions
+ *   - All pointers are device pointers; `stream` is a cudaStream_t (NULL = legacy stream).
+ *     Nothing synchronises the stream or reads device memory on the host, so every call can be
+ *     captured into a CUDA graph.
+ *   - bf16 tensors are passed as raw 16-bit patterns, e4m3 caches as bytes.  head_dim must be 128.
+ *   - Paged caches are [num_blocks, block_size, num_kv_heads, 128] e4m3, contiguous; block_size is
+ *     a multiple of 16.  Optional scales are fp32 [num_blocks * block_size, num_kv_heads]; NULL
+ *     means unit scale, which is the reference's behaviour (its cache has no scales).
+ *   - Return value: 0 on success, otherwise an FP8ATTN_E* code; fp8attn_last_error() gives a
+ *     message (thread-local).  Launch errors are reported, device-side problems (a bounded wait
+ *     that timed out, a workspace overflow) are recorded in the workspace's error word
+ *     (int32 at byte offset FP8ATTN_WS_ERROR_OFFSET) and never trap.
+ */
+#ifndef FP8ATTN_H_
+#define FP8ATTN_H_
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define FP8ATTN_API __attribute__((visibility("default")))
+#else
+#define FP8ATTN_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FP8ATTN_OK 0
+#define FP8ATTN_EINVAL 1     /* invalid argument (null pointer, shape, stride, alignment) */
+#define FP8ATTN_EWORKSPACE 2 /* workspace missing or smaller than fp8attn_workspace_bytes() */
+#define FP8ATTN_ECUDA 3      /* CUDA error while preparing or launching */
+
+#define FP8ATTN_WS_ERROR_OFFSET 0
+
+/* Library version (major * 10000 + minor * 100 + patch). */
+FP8ATTN_API int fp8attn_version(void);
+
+/* Message for the last non-zero status returned on this thread. */
+FP8ATTN_API const char* fp8attn_last_error(void);
+
+/*
+ * KV store / quantise.  Replaces store_kvcache (nanovllm/layers/attention.py:33-40).
+ * For every token i < num_tokens with slot = slot_mapping[i] != -1:
+ *   k_cache[slot] = e4m3(key[i]),  v_cache[slot] = e4m3(value[i])      (cache rows of KVH*128)
+ * key/value rows are KVH*128 bf16 values, row i at key + i*key_row_stride (elements).
+ * scaled == 0: round-to-nearest-even cast with finite overflow saturating to +-448; scale arrays
+ *              (if given) receive 1.0.
+ * scaled == 1: per (token, kv head) scale = amax/448 (0 -> 1); bytes = e4m3(clamp(x/scale)).
+ * Slots outside [0, num_slots) are skipped like -1.
+ */
+FP8ATTN_API int fp8attn_store_kvcache(const void* key, int64_t key_row_stride, const void* value,
+                          int64_t value_row_stride, void* k_cache, void* v_cache, float* k_scale,
+                          float* v_scale, const int32_t* slot_mapping, int64_t num_tokens,
+                          int num_kv_heads, int head_dim, int64_t num_slots, int scaled,
+                          void* stream);
+
+/*
+ * Workspace needed by fp8attn_decode (max_seqlen_q = 1) or fp8attn_prefill (its max_seqlen_q)
+ * on the current device.  The workspace must be zero-filled before its first use; every call
+ * leaves its counters at zero again.  One workspace must not be used by two calls that can run
+ * at the same time.
+ */
+FP8ATTN_API int64_t fp8attn_workspace_bytes(int num_seqs, int num_heads, int num_kv_heads, int max_seqlen_q);
+
+/*
+ * Paged decode.  Replaces fp8_decode_attention (nanovllm/kernels/fp8_attention.py:173-207).
+ * q: [num_seqs, num_heads, 128] bf16, rows q_row_stride elements apart; out: contiguous
+ * [num_seqs, num_heads, 128] bf16.  Sequence b attends key positions < context_lens[b] (clamped
+ * to max_num_blocks * block_size) of kv head h / (num_heads / num_kv_heads), position j in
+ * cache block block_tables[b * block_tables_stride + j / block_size].  context_lens[b] <= 0
+ * gives zeros.  Block ids outside [0, num_blocks) mask their positions out.
+ */
+FP8ATTN_API int fp8attn_decode(void* out, const void* q, int64_t q_row_stride, const void* k_cache,
+                   const void* v_cache, const float* k_scale, const float* v_scale,
+                   const int32_t* block_tables, int64_t block_tables_stride, int max_num_blocks,
+                   const int32_t* context_lens, int num_seqs, int num_heads, int num_kv_heads,
+                   int head_dim, int64_t num_blocks, int block_size, float softmax_scale,
+                   void* workspace, int64_t workspace_bytes, void* stream);
+
+/*
+ * Varlen causal prefill / chunked prefill / speculative verify.  Replaces fp8_prefill_attention
+ * (nanovllm/kernels/fp8_attention.py:314-353).
+ * q: [Tq, num_heads, 128] bf16 (rows q_row_stride elements apart); out: contiguous like q.
+ * Sequence s has query rows cu_seqlens_q[s]..cu_seqlens_q[s+1] and nk = cu_seqlens_k[s+1] -
+ * cu_seqlens_k[s] key positions; query row i attends key positions j <= i + (nk - nq).
+ *   block_tables != NULL: k/v are paged caches (as in fp8attn_decode), num_blocks = cache blocks.
+ *   block_tables == NULL: k/v are contiguous [Tk, num_kv_heads, 128] e4m3 with token rows
+ *                         kv_row_stride bytes apart, num_blocks = Tk, key rows from
+ *                         cu_seqlens_k[s]; block_size is ignored.
+ * Short query sequences (speculative verification, 1 + k rows) are served by the split-KV
+ * decode engine inside this call; longer ones by the tensor-core prefill engine.
+ */
+FP8ATTN_API int fp8attn_prefill(void* out, const void* q, int64_t q_row_stride, const void* k, const void* v,
+                    int64_t kv_row_stride, const float* k_scale, const float* v_scale,
+                    const int32_t* block_tables, int64_t block_tables_stride, int max_num_blocks,
+                    const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k, int num_seqs,
+                    int max_seqlen_q, int max_seqlen_k, int num_heads, int num_kv_heads,
+                    int head_dim, int64_t num_blocks, int block_size, float softmax_scale,
+                    void* workspace, int64_t workspace_bytes, void* stream);
+
+/* Tuning knob (process-wide): minimum key positions per split-KV work item, a multiple of 64
+ * (default 256).  Returns the previous value; values < 64 are rejected with -1. */
+FP8ATTN_API int fp8attn_set_decode_min_chunk(int tokens);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FP8ATTN_H_ */

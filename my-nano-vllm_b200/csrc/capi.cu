@@ -1,0 +1,368 @@
+// C-ABI layer: argument validation, TMA descriptor encoding, engine selection and launches.
+// See include/fp8attn.h for the contract of every entry point.
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "../../include/fp8attn.h"
+#include "common.cuh"
+#include "kernels.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+int g_min_chunk = 256;
+
+int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(FP8ATTN_ECUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (fn == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// The paged cache viewed as a 2-D byte tensor [num_blocks * block_size, KVH * 128]; one box is
+// `box_rows` token rows x the 128 bytes of one kv head, 128-byte swizzled.
+int make_cache_map(CUtensorMap* map, const void* cache, int64_t rows, int kvh, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return fail(FP8ATTN_ECUDA, "cuTensorMapEncodeTiled is unavailable");
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(kvh) * fp8attn::kHeadDim,
+                              static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(kvh) * fp8attn::kHeadDim};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(fp8attn::kHeadDim),
+                             static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(cache), dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(FP8ATTN_ECUDA, "cuTensorMapEncodeTiled failed (%d)", int(r));
+  return FP8ATTN_OK;
+}
+
+// Query sequences with at most this many rows go to the split-KV decode engine inside the
+// prefill entry point (speculative verification: 1 + k rows).
+int spec_q_max(int group) {
+  int m = 64 / group;
+  if (m > 16) m = 16;
+  if (m < 1) m = 1;
+  return m;
+}
+
+struct EnginePlan {
+  int nt;
+  int rows;
+  int max_rowgroups;
+};
+
+EnginePlan plan_engine(int group, int max_q) {
+  EnginePlan e;
+  const int r = group * (max_q < 1 ? 1 : max_q);
+  e.nt = r <= 8 ? 1 : 2;
+  e.rows = fp8attn::decode_rows(e.nt);
+  e.max_rowgroups = (r + e.rows - 1) / e.rows;
+  return e;
+}
+
+int box_rows_for(int block_size) {
+  if (block_size % 64 == 0) return 64;
+  if (block_size % 32 == 0) return 32;
+  return 16;
+}
+
+int check_common(int num_seqs, int num_heads, int num_kv_heads, int head_dim) {
+  if (head_dim != fp8attn::kHeadDim)
+    return fail(FP8ATTN_EINVAL, "head_dim must be 128 (got %d)", head_dim);
+  if (num_heads <= 0 || num_kv_heads <= 0 || num_heads % num_kv_heads != 0)
+    return fail(FP8ATTN_EINVAL, "num_heads (%d) must be a positive multiple of num_kv_heads (%d)",
+                num_heads, num_kv_heads);
+  if (num_seqs < 0 || num_seqs > fp8attn::kMaxSeqs)
+    return fail(FP8ATTN_EINVAL, "num_seqs must be in [0, %d] (got %d)", fp8attn::kMaxSeqs,
+                num_seqs);
+  return FP8ATTN_OK;
+}
+
+int check_paged(const void* k, const void* v, const int32_t* bt, int64_t bt_stride,
+                int max_blocks, int64_t num_blocks, int block_size) {
+  if (k == nullptr || v == nullptr || bt == nullptr)
+    return fail(FP8ATTN_EINVAL, "null cache or block_tables pointer");
+  if (!aligned16(k) || !aligned16(v))
+    return fail(FP8ATTN_EINVAL, "caches must be 16-byte aligned");
+  if (block_size <= 0 || block_size % 16 != 0)
+    return fail(FP8ATTN_EINVAL, "block_size must be a positive multiple of 16 (got %d)",
+                block_size);
+  if (max_blocks < 0 || bt_stride < max_blocks)
+    return fail(FP8ATTN_EINVAL, "bad block table geometry (max_num_blocks %d, stride %lld)",
+                max_blocks, static_cast<long long>(bt_stride));
+  if (static_cast<int64_t>(max_blocks) * block_size >= (1 << 24))
+    return fail(FP8ATTN_EINVAL, "max_num_blocks * block_size must be < 2^24");
+  if (num_blocks <= 0 || num_blocks * block_size > INT32_MAX)
+    return fail(FP8ATTN_EINVAL, "num_blocks * block_size must be in (0, 2^31)");
+  return FP8ATTN_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int fp8attn_version(void) { return 100; }
+
+const char* fp8attn_last_error(void) { return g_last_error.c_str(); }
+
+int fp8attn_set_decode_min_chunk(int tokens) {
+  if (tokens < 64 || tokens % 64 != 0) return -1;
+  const int prev = g_min_chunk;
+  g_min_chunk = tokens;
+  return prev;
+}
+
+int fp8attn_store_kvcache(const void* key, int64_t key_row_stride, const void* value,
+                          int64_t value_row_stride, void* k_cache, void* v_cache, float* k_scale,
+                          float* v_scale, const int32_t* slot_mapping, int64_t num_tokens,
+                          int num_kv_heads, int head_dim, int64_t num_slots, int scaled,
+                          void* stream) {
+  if (head_dim != fp8attn::kHeadDim)
+    return fail(FP8ATTN_EINVAL, "head_dim must be 128 (got %d)", head_dim);
+  if (num_tokens < 0 || num_kv_heads <= 0 || num_slots < 0)
+    return fail(FP8ATTN_EINVAL, "bad sizes");
+  if (num_tokens == 0) return FP8ATTN_OK;
+  if (!key || !value || !k_cache || !v_cache || !slot_mapping)
+    return fail(FP8ATTN_EINVAL, "null pointer argument");
+  if (!aligned16(k_cache) || !aligned16(v_cache))
+    return fail(FP8ATTN_EINVAL, "caches must be 16-byte aligned");
+  if ((reinterpret_cast<uintptr_t>(key) & 1) || (reinterpret_cast<uintptr_t>(value) & 1))
+    return fail(FP8ATTN_EINVAL, "key/value must be 2-byte aligned");
+  if ((k_scale == nullptr) != (v_scale == nullptr))
+    return fail(FP8ATTN_EINVAL, "k_scale and v_scale must both be given or both be null");
+  if (scaled && k_scale == nullptr)
+    return fail(FP8ATTN_EINVAL, "scaled mode needs scale arrays");
+  fp8attn::StoreParams p;
+  p.key = static_cast<const uint16_t*>(key);
+  p.key_row_stride = key_row_stride;
+  p.value = static_cast<const uint16_t*>(value);
+  p.value_row_stride = value_row_stride;
+  p.k_cache = static_cast<uint8_t*>(k_cache);
+  p.v_cache = static_cast<uint8_t*>(v_cache);
+  p.k_scale = k_scale;
+  p.v_scale = v_scale;
+  p.slot_mapping = slot_mapping;
+  p.num_tokens = num_tokens;
+  p.num_slots = num_slots;
+  p.num_kv_heads = num_kv_heads;
+  p.scaled = scaled ? 1 : 0;
+  const cudaError_t e = fp8attn::launch_store(p, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "store launch");
+  return FP8ATTN_OK;
+}
+
+int64_t fp8attn_workspace_bytes(int num_seqs, int num_heads, int num_kv_heads,
+                                int max_seqlen_q) {
+  if (num_seqs < 0 || num_heads <= 0 || num_kv_heads <= 0 || num_heads % num_kv_heads) return -1;
+  const int group = num_heads / num_kv_heads;
+  const int mq = max_seqlen_q <= 1 ? 1 : (max_seqlen_q < spec_q_max(group) ? max_seqlen_q
+                                                                           : spec_q_max(group));
+  const EnginePlan e = plan_engine(group, mq);
+  return fp8attn::decode_workspace_bytes(num_seqs, num_kv_heads, e.max_rowgroups, e.rows,
+                                         fp8attn::decode_grid(e.nt));
+}
+
+static int run_decode_engine(fp8attn::DecodeParams& p, const EnginePlan& e, const void* k_cache,
+                             const void* v_cache, void* workspace, int64_t workspace_bytes,
+                             cudaStream_t stream) {
+  const int grid = fp8attn::decode_grid(e.nt);
+  const int64_t need =
+      fp8attn::decode_workspace_bytes(p.num_seqs, p.num_kv_heads, e.max_rowgroups, e.rows, grid);
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(FP8ATTN_EWORKSPACE, "workspace of %lld bytes is smaller than the %lld needed",
+                static_cast<long long>(workspace_bytes), static_cast<long long>(need));
+  if (!aligned16(workspace)) return fail(FP8ATTN_EINVAL, "workspace must be 16-byte aligned");
+  const int64_t pairs = static_cast<int64_t>(p.num_seqs) * p.num_kv_heads * e.max_rowgroups;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  p.ctrl = reinterpret_cast<int*>(ws);
+  p.tickets = reinterpret_cast<int*>(ws + fp8attn::kCtrlInts * 4);
+  p.partials = reinterpret_cast<float*>(ws + fp8attn::kCtrlInts * 4 + (pairs * 4 + 255) / 256 * 256);
+  p.max_items = static_cast<int>(32LL * grid + pairs);
+  p.max_rowgroups = e.max_rowgroups;
+  p.min_chunk = g_min_chunk;
+  p.box_rows = box_rows_for(p.block_size);
+  CUtensorMap tmk, tmv;
+  const int64_t rows = p.num_blocks * p.block_size;
+  int rc = make_cache_map(&tmk, k_cache, rows, p.num_kv_heads, p.box_rows);
+  if (rc) return rc;
+  rc = make_cache_map(&tmv, v_cache, rows, p.num_kv_heads, p.box_rows);
+  if (rc) return rc;
+  const cudaError_t err = fp8attn::launch_decode(p, e.nt, tmk, tmv, stream);
+  if (err != cudaSuccess) return cuda_fail(err, "decode launch");
+  return FP8ATTN_OK;
+}
+
+int fp8attn_decode(void* out, const void* q, int64_t q_row_stride, const void* k_cache,
+                   const void* v_cache, const float* k_scale, const float* v_scale,
+                   const int32_t* block_tables, int64_t block_tables_stride, int max_num_blocks,
+                   const int32_t* context_lens, int num_seqs, int num_heads, int num_kv_heads,
+                   int head_dim, int64_t num_blocks, int block_size, float softmax_scale,
+                   void* workspace, int64_t workspace_bytes, void* stream) {
+  int rc = check_common(num_seqs, num_heads, num_kv_heads, head_dim);
+  if (rc) return rc;
+  if (num_seqs == 0) return FP8ATTN_OK;
+  rc = check_paged(k_cache, v_cache, block_tables, block_tables_stride, max_num_blocks,
+                   num_blocks, block_size);
+  if (rc) return rc;
+  if (!out || !q || !context_lens) return fail(FP8ATTN_EINVAL, "null pointer argument");
+  if (!aligned16(out) || !aligned16(q) || q_row_stride % 8 != 0 ||
+      q_row_stride < static_cast<int64_t>(num_heads) * head_dim)
+    return fail(FP8ATTN_EINVAL, "q/out must be 16-byte aligned with rows of num_heads*128");
+  if ((k_scale == nullptr) != (v_scale == nullptr))
+    return fail(FP8ATTN_EINVAL, "k_scale and v_scale must both be given or both be null");
+  const int group = num_heads / num_kv_heads;
+  const EnginePlan e = plan_engine(group, 1);
+  if (e.max_rowgroups > 127) return fail(FP8ATTN_EINVAL, "too many query heads per kv head");
+  fp8attn::DecodeParams p{};
+  p.out = static_cast<uint16_t*>(out);
+  p.out_row_stride = static_cast<int64_t>(num_heads) * head_dim;
+  p.q = static_cast<const uint16_t*>(q);
+  p.q_row_stride = q_row_stride;
+  p.k_scale = k_scale;
+  p.v_scale = v_scale;
+  p.block_tables = block_tables;
+  p.bt_stride = block_tables_stride;
+  p.max_blocks = max_num_blocks;
+  p.context_lens = context_lens;
+  p.num_seqs = num_seqs;
+  p.num_heads = num_heads;
+  p.num_kv_heads = num_kv_heads;
+  p.group = group;
+  p.block_size = block_size;
+  p.num_blocks = num_blocks;
+  p.spec_mode = 0;
+  p.spec_q_max = 1;
+  p.scale_log2 = softmax_scale * 1.4426950408889634f;
+  return run_decode_engine(p, e, k_cache, v_cache, workspace, workspace_bytes,
+                           static_cast<cudaStream_t>(stream));
+}
+
+int fp8attn_prefill(void* out, const void* q, int64_t q_row_stride, const void* k, const void* v,
+                    int64_t kv_row_stride, const float* k_scale, const float* v_scale,
+                    const int32_t* block_tables, int64_t block_tables_stride, int max_num_blocks,
+                    const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k, int num_seqs,
+                    int max_seqlen_q, int max_seqlen_k, int num_heads, int num_kv_heads,
+                    int head_dim, int64_t num_blocks, int block_size, float softmax_scale,
+                    void* workspace, int64_t workspace_bytes, void* stream) {
+  (void)max_seqlen_k;  // the reference does not use it either (fp8_attention.py:314-353)
+  int rc = check_common(num_seqs, num_heads, num_kv_heads, head_dim);
+  if (rc) return rc;
+  if (num_seqs == 0 || max_seqlen_q <= 0) return FP8ATTN_OK;
+  if (!out || !q || !k || !v || !cu_seqlens_q || !cu_seqlens_k)
+    return fail(FP8ATTN_EINVAL, "null pointer argument");
+  if (!aligned16(out) || !aligned16(q) || q_row_stride % 8 != 0 ||
+      q_row_stride < static_cast<int64_t>(num_heads) * head_dim)
+    return fail(FP8ATTN_EINVAL, "q/out must be 16-byte aligned with rows of num_heads*128");
+  if ((k_scale == nullptr) != (v_scale == nullptr))
+    return fail(FP8ATTN_EINVAL, "k_scale and v_scale must both be given or both be null");
+  const int group = num_heads / num_kv_heads;
+  const bool paged = block_tables != nullptr;
+  if (paged) {
+    rc = check_paged(k, v, block_tables, block_tables_stride, max_num_blocks, num_blocks,
+                     block_size);
+    if (rc) return rc;
+  } else {
+    if (kv_row_stride < static_cast<int64_t>(num_kv_heads) * head_dim || kv_row_stride % 16 != 0 ||
+        !aligned16(k) || !aligned16(v) || num_blocks < 0)
+      return fail(FP8ATTN_EINVAL, "bad contiguous k/v layout");
+  }
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const float scale_log2 = softmax_scale * 1.4426950408889634f;
+  int min_q = 1;
+  if (paged) {
+    // speculative-verify sized sequences: split-KV decode engine
+    const int sq = spec_q_max(group);
+    const int mq = max_seqlen_q < sq ? max_seqlen_q : sq;
+    const EnginePlan e = plan_engine(group, mq);
+    fp8attn::DecodeParams p{};
+    p.out = static_cast<uint16_t*>(out);
+    p.out_row_stride = static_cast<int64_t>(num_heads) * head_dim;
+    p.q = static_cast<const uint16_t*>(q);
+    p.q_row_stride = q_row_stride;
+    p.k_scale = k_scale;
+    p.v_scale = v_scale;
+    p.block_tables = block_tables;
+    p.bt_stride = block_tables_stride;
+    p.max_blocks = max_num_blocks;
+    p.cu_q = cu_seqlens_q;
+    p.cu_k = cu_seqlens_k;
+    p.num_seqs = num_seqs;
+    p.num_heads = num_heads;
+    p.num_kv_heads = num_kv_heads;
+    p.group = group;
+    p.block_size = block_size;
+    p.num_blocks = num_blocks;
+    p.spec_mode = 1;
+    p.spec_q_max = mq;
+    p.scale_log2 = scale_log2;
+    rc = run_decode_engine(p, e, k, v, workspace, workspace_bytes, st);
+    if (rc) return rc;
+    min_q = mq + 1;
+    if (max_seqlen_q < min_q) return FP8ATTN_OK;  // every sequence was short
+  } else if (workspace == nullptr || workspace_bytes < 256) {
+    return fail(FP8ATTN_EWORKSPACE, "workspace missing");
+  }
+  fp8attn::PrefillParams pp{};
+  pp.out = static_cast<uint16_t*>(out);
+  pp.out_row_stride = static_cast<int64_t>(num_heads) * head_dim;
+  pp.q = static_cast<const uint16_t*>(q);
+  pp.q_row_stride = q_row_stride;
+  pp.k = static_cast<const uint8_t*>(k);
+  pp.v = static_cast<const uint8_t*>(v);
+  pp.kv_row_stride = paged ? static_cast<int64_t>(num_kv_heads) * head_dim : kv_row_stride;
+  pp.k_scale = k_scale;
+  pp.v_scale = v_scale;
+  pp.block_tables = block_tables;
+  pp.bt_stride = block_tables_stride;
+  pp.max_blocks = max_num_blocks;
+  pp.cu_q = cu_seqlens_q;
+  pp.cu_k = cu_seqlens_k;
+  pp.num_seqs = num_seqs;
+  pp.max_seqlen_q = max_seqlen_q;
+  pp.num_heads = num_heads;
+  pp.num_kv_heads = num_kv_heads;
+  pp.group = group;
+  pp.block_size = paged ? block_size : 1;
+  pp.num_blocks = num_blocks;
+  pp.min_q = min_q;
+  pp.scale_log2 = scale_log2;
+  pp.err = static_cast<int*>(workspace);
+  const cudaError_t e = fp8attn::launch_prefill(pp, st);
+  if (e != cudaSuccess) return cuda_fail(e, "prefill launch");
+  return FP8ATTN_OK;
+}
+
+}  // extern "C"

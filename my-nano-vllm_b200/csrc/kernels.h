@@ -1,0 +1,103 @@
+// Host-side launch interface between the C-ABI layer (capi.cu) and the kernels.
+#pragma once
+
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+namespace fp8attn {
+
+// ------------------------------------------------------------------ store
+struct StoreParams {
+  const uint16_t* key;  // bf16 [N, KVH, 128], rows `key_row_stride` elements apart
+  int64_t key_row_stride;
+  const uint16_t* value;
+  int64_t value_row_stride;
+  uint8_t* k_cache;  // e4m3 [num_slots, KVH, 128]
+  uint8_t* v_cache;
+  float* k_scale;  // fp32 [num_slots, KVH] or null
+  float* v_scale;
+  const int32_t* slot_mapping;  // [N]
+  int64_t num_tokens;
+  int64_t num_slots;
+  int num_kv_heads;
+  int scaled;  // 0: plain RNE cast (scale 1.0); 1: amax/448 per (token, kv head)
+};
+cudaError_t launch_store(const StoreParams& p, cudaStream_t stream);
+
+// ------------------------------------------------------------------ decode engine
+// Control block at the head of the decode workspace (ints):
+//   [0] sticky device error code, [1] next work item, [2] CTAs finished.
+constexpr int kCtrlInts = 64;  // 256 bytes
+constexpr int kMaxSeqs = 2048;  // per launch (plan lives in shared memory)
+
+struct DecodeParams {
+  uint16_t* out;  // bf16
+  int64_t out_row_stride;  // elements per query token row
+  const uint16_t* q;  // bf16
+  int64_t q_row_stride;
+  const float* k_scale;  // per (slot, kv head) or null
+  const float* v_scale;
+  const int32_t* block_tables;
+  int64_t bt_stride;
+  int max_blocks;
+  const int32_t* context_lens;  // decode mode
+  const int32_t* cu_q;  // spec mode (prefill entry point, short query sequences)
+  const int32_t* cu_k;
+  int num_seqs;
+  int num_heads;
+  int num_kv_heads;
+  int group;  // num_heads / num_kv_heads
+  int block_size;
+  int box_rows;  // TMA box height: 64, 32 or 16 (divides block_size and 64)
+  int64_t num_blocks;
+  int spec_mode;
+  int spec_q_max;  // spec mode: sequences with 1 <= nq <= spec_q_max are handled here
+  int max_rowgroups;
+  int min_chunk;  // minimum tokens per work item (multiple of 64)
+  float scale_log2;  // softmax_scale * log2(e)
+  int* ctrl;
+  int* tickets;  // [num_seqs * num_kv_heads * max_rowgroups], zero between launches
+  float* partials;
+  int max_items;
+};
+
+// Rows (query rows of one kv head) per work item for the two engine widths.
+inline int decode_rows(int nt) { return 8 * nt; }
+int64_t decode_workspace_bytes(int num_seqs, int num_kv_heads, int max_rowgroups, int rows,
+                               int grid);
+// Grid (persistent CTAs) the decode engine uses on the current device for the given width.
+int decode_grid(int nt);
+cudaError_t launch_decode(const DecodeParams& p, int nt, const CUtensorMap& tmk,
+                          const CUtensorMap& tmv, cudaStream_t stream);
+
+// ------------------------------------------------------------------ prefill engine
+struct PrefillParams {
+  uint16_t* out;
+  int64_t out_row_stride;
+  const uint16_t* q;
+  int64_t q_row_stride;
+  const uint8_t* k;  // paged cache [nb, BS, KVH, 128] or contiguous [Tk, KVH, 128]
+  const uint8_t* v;
+  int64_t kv_row_stride;  // bytes between consecutive token rows (contiguous layout)
+  const float* k_scale;
+  const float* v_scale;
+  const int32_t* block_tables;  // null: contiguous layout
+  int64_t bt_stride;
+  int max_blocks;
+  const int32_t* cu_q;
+  const int32_t* cu_k;
+  int num_seqs;
+  int max_seqlen_q;
+  int num_heads;
+  int num_kv_heads;
+  int group;
+  int block_size;
+  int64_t num_blocks;  // paged: blocks in the cache; contiguous: token rows
+  int min_q;  // sequences with nq < min_q are left to the decode engine
+  float scale_log2;
+  int* err;
+};
+cudaError_t launch_prefill(const PrefillParams& p, cudaStream_t stream);
+
+}  // namespace fp8attn

@@ -1,0 +1,86 @@
+"""The C-ABI boundary without a GPU: the library loads, exports every function include/fp8attn.h
+declares, and rejects bad arguments before touching a device."""
+import ctypes
+import subprocess
+
+import pytest
+
+from nanovllm_b200 import _lib
+from nanovllm_b200.build import LIB_PATH
+
+
+def test_library_exports_every_header_symbol():
+    declared = _lib.header_symbols()
+    assert len(declared) >= 7
+    out = subprocess.run(["nm", "-D", "--defined-only", LIB_PATH], capture_output=True,
+                         text=True, check=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if line.strip()}
+    missing = [s for s in declared if s not in exported]
+    assert not missing, missing
+    for s in declared:
+        assert hasattr(_lib.lib, s)
+
+
+def test_library_has_no_hard_cuda_driver_dependency():
+    # the driver is resolved at run time, so the library also loads on GPU-less hosts
+    out = subprocess.run(["ldd", LIB_PATH], capture_output=True, text=True).stdout
+    assert "libcuda.so" not in out
+
+
+def test_version_and_min_chunk_knob():
+    assert _lib.lib.fp8attn_version() >= 100
+    prev = _lib.lib.fp8attn_set_decode_min_chunk(128)
+    assert prev == 256
+    assert _lib.lib.fp8attn_set_decode_min_chunk(100) == -1      # not a multiple of 64
+    assert _lib.lib.fp8attn_set_decode_min_chunk(prev) == 128
+
+
+def _decode_call(**over):
+    a = dict(out=16, q=16, q_row_stride=32 * 128, k=16, v=16, ks=None, vs=None, bt=16,
+             bt_stride=4, max_blocks=4, ctx=16, num_seqs=2, hq=32, kvh=8, d=128, nb=10, bs=256,
+             scale=0.088, ws=16, ws_bytes=1 << 20, stream=None)
+    a.update(over)
+    return _lib.lib.fp8attn_decode(a["out"], a["q"], a["q_row_stride"], a["k"], a["v"], a["ks"],
+                                   a["vs"], a["bt"], a["bt_stride"], a["max_blocks"], a["ctx"],
+                                   a["num_seqs"], a["hq"], a["kvh"], a["d"], a["nb"], a["bs"],
+                                   a["scale"], a["ws"], a["ws_bytes"], a["stream"])
+
+
+@pytest.mark.parametrize("bad,msg", [
+    (dict(d=64), "head_dim"),
+    (dict(hq=30), "multiple"),
+    (dict(bs=24), "block_size"),
+    (dict(bt_stride=2), "block table"),
+    (dict(q=8), "aligned"),
+    (dict(k=None), "null"),
+    (dict(num_seqs=5000), "num_seqs"),
+    (dict(max_blocks=1 << 20, bt_stride=1 << 20), "2^24"),
+    (dict(ks=16), "both"),
+])
+def test_decode_rejects_bad_arguments(bad, msg):
+    rc = _decode_call(**bad)
+    assert rc == _lib.EINVAL
+    assert msg in _lib.lib.fp8attn_last_error().decode()
+
+
+def test_store_rejects_bad_arguments():
+    f = _lib.lib.fp8attn_store_kvcache
+    assert f(16, 1024, 16, 1024, 16, 16, None, None, 16, 4, 8, 64, 100, 0, None) == _lib.EINVAL
+    assert f(16, 1024, 16, 1024, 8, 16, None, None, 16, 4, 8, 128, 100, 0, None) == _lib.EINVAL
+    assert f(16, 1024, 16, 1024, 16, 16, None, None, 16, 4, 8, 128, 100, 1, None) == _lib.EINVAL
+    assert f(16, 1024, 16, 1024, 16, 16, None, None, 16, 0, 8, 128, 100, 0, None) == _lib.OK
+
+
+def test_prefill_rejects_bad_arguments():
+    f = _lib.lib.fp8attn_prefill
+    args = [16, 16, 4096, 16, 16, 1024, None, None, None, 0, 0, 16, 16, 2, 8, 8, 32, 8, 128, 100,
+            1, 0.088, 16, 1 << 20, None]
+    bad = list(args)
+    bad[18] = 96                                   # head_dim
+    assert f(*bad) == _lib.EINVAL
+    bad = list(args)
+    bad[5] = 100                                   # contiguous kv row stride < KVH*128
+    assert f(*bad) == _lib.EINVAL
+    bad = list(args)
+    bad[13] = 0                                    # no sequences: nothing to do
+    assert f(*bad) == _lib.OK

@@ -1,0 +1,142 @@
+"""Decode engine parity: reference golden outputs, the fp32 oracle on the benchmark configs and on
+edge cases (ragged lengths, zero lengths, -1 padding, block sizes 16..256, GQA 1..16, split-KV
+chunking), scaled caches, and CUDA-graph capture."""
+import pytest
+import torch
+
+from helpers import ATOL, RTOL, assert_close, bf16, fp8
+from oracle import attention as oatt
+
+pytestmark = pytest.mark.gpu
+
+
+def _lib():
+    from nanovllm_b200 import _lib
+    return _lib.lib
+
+
+def _decode(case_or_args, **kw):
+    from nanovllm_b200 import fp8_decode_attention
+    out = fp8_decode_attention(*case_or_args, **kw)
+    torch.cuda.synchronize()
+    return out
+
+
+def _no_device_error():
+    from nanovllm_b200.fp8_attention import device_error
+    assert device_error() == 0
+
+
+@pytest.mark.parametrize("name", ["decode_bs32", "decode_bs256", "decode_bs16_g8"])
+def test_decode_matches_reference_golden(golden, name):
+    g = golden(name)
+    args = (bf16(g["q"]).cuda(), fp8(g["k_cache"]).cuda(), fp8(g["v_cache"]).cuda(),
+            torch.from_numpy(g["block_tables"]).cuda(), torch.from_numpy(g["context_lens"]).cuda(),
+            float(g["scale"]))
+    out = _decode(args)
+    assert_close(out, bf16(g["out"]), what=name)
+    _no_device_error()
+
+
+def _oracle_case(c, **kw):
+    return oatt.decode(c.q.cpu(), c.k_cache.cpu(), c.v_cache.cpu(), c.block_tables.cpu(),
+                       c.context_lens.cpu(), c.scale, **kw)
+
+
+def test_decode_config1():
+    from nanovllm_b200 import workloads
+    c = workloads.config1("cuda")
+    out = _decode((c.q, c.k_cache, c.v_cache, c.block_tables, c.context_lens, c.scale))
+    assert_close(out, _oracle_case(c), what="config1")
+    _no_device_error()
+
+
+@pytest.mark.parametrize("min_chunk", [64, 256])
+@pytest.mark.parametrize("bs,hq,kvh", [(16, 4, 4), (32, 8, 2), (64, 16, 1), (256, 32, 8),
+                                       (48, 8, 8), (80, 32, 2), (256, 64, 8)])
+def test_decode_edge_cases(bs, hq, kvh, min_chunk):
+    from nanovllm_b200 import workloads
+    lens = [0, 1, bs - 1, bs, bs + 1, 63, 64, 65, 3 * bs + 17, 700, -5, 1000]
+    c = workloads.decode_case(len(lens), hq, kvh, 0, 0, seed=bs + hq, device="cuda",
+                              block_size=bs, pool_factor=1.3, lens=lens, extra_cols=2)
+    prev = _lib().fp8attn_set_decode_min_chunk(min_chunk)
+    try:
+        out = _decode((c.q, c.k_cache, c.v_cache, c.block_tables, c.context_lens, c.scale))
+    finally:
+        _lib().fp8attn_set_decode_min_chunk(prev)
+    ref = _oracle_case(c)
+    assert_close(out, ref, what=f"bs{bs} hq{hq} kvh{kvh}")
+    assert torch.all(out[0] == 0) and torch.all(out[10] == 0)   # empty contexts give zeros
+    _no_device_error()
+
+
+def test_decode_nan_bytes_beyond_context_are_ignored():
+    # slots past each context hold NaN codes (0x7F): they must not leak into the output
+    from nanovllm_b200 import workloads
+    lens = [5, 70, 300]
+    c = workloads.decode_case(3, 8, 2, 0, 0, seed=9, device="cuda", block_size=64,
+                              lens=lens, pool_factor=1.0)
+    kc = c.k_cache.view(torch.uint8)
+    vc = c.v_cache.view(torch.uint8)
+    for b, n in enumerate(lens):
+        for j in range(n, ((n + 63) // 64) * 64):
+            blk = int(c.block_tables[b, j // 64])
+            kc[blk, j % 64] = 0x7F
+            vc[blk, j % 64] = 0x7F
+    out = _decode((c.q, c.k_cache, c.v_cache, c.block_tables, c.context_lens, c.scale))
+    assert torch.isfinite(out.float()).all()
+    assert_close(out, _oracle_case(c), what="nan-padding")
+
+
+def test_decode_scaled_cache():
+    from nanovllm_b200 import workloads
+    c = workloads.decode_case(6, 16, 4, 1, 900, seed=11, device="cuda", block_size=128)
+    nb, bs, kvh, _ = c.k_cache.shape
+    gen = torch.Generator().manual_seed(5)
+    ks = (torch.rand(nb, bs, kvh, generator=gen) * 0.05 + 0.001).cuda()
+    vs = (torch.rand(nb, bs, kvh, generator=gen) * 0.05 + 0.001).cuda()
+    out = _decode((c.q, c.k_cache, c.v_cache, c.block_tables, c.context_lens, c.scale),
+                  k_scale=ks, v_scale=vs)
+    ref = _oracle_case(c, k_scale=ks.cpu(), v_scale=vs.cpu())
+    assert_close(out, ref, what="scaled")
+
+
+def test_decode_config2_full_size_sampled():
+    # full config-2 launch; the oracle checks a deterministic sample of sequences
+    from nanovllm_b200 import workloads
+    c = workloads.config2("cuda")
+    out = _decode((c.q, c.k_cache, c.v_cache, c.block_tables, c.context_lens, c.scale))
+    idx = list(range(0, 256, 17)) + [255]
+    sub = workloads.DecodeCase(c.q[idx], c.k_cache, c.v_cache, c.block_tables[idx],
+                               c.context_lens[idx])
+    assert_close(out[idx], _oracle_case(sub), what="config2 sample")
+    _no_device_error()
+
+
+def test_decode_cuda_graph_replay():
+    """Captured once, replayed with new lengths / tables: matches eager (graph capture path of
+    ModelRunner.capture_cudagraph, nanovllm/engine/model_runner.py:294-329)."""
+    from nanovllm_b200 import fp8_decode_attention, workloads
+    c = workloads.decode_case(16, 32, 8, 1, 2000, seed=3, device="cuda", block_size=256,
+                              extra_cols=3)
+    static_q = c.q.clone()
+    static_bt = c.block_tables.clone()
+    static_ctx = torch.zeros_like(c.context_lens)
+    fp8_decode_attention(static_q, c.k_cache, c.v_cache, static_bt, static_ctx, c.scale)  # warmup
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        static_out = fp8_decode_attention(static_q, c.k_cache, c.v_cache, static_bt, static_ctx,
+                                          c.scale)
+    for trial in range(3):
+        gen = torch.Generator().manual_seed(trial)
+        ctx = torch.randint(0, 2000, (16,), generator=gen, dtype=torch.int32)
+        ctx[trial] = 0
+        static_ctx.copy_(ctx.cuda())
+        static_q.copy_(torch.randn(16, 32, 128, generator=gen).to(torch.bfloat16).cuda())
+        g.replay()
+        torch.cuda.synchronize()
+        eager = fp8_decode_attention(static_q, c.k_cache, c.v_cache, static_bt, static_ctx, c.scale)
+        torch.cuda.synchronize()
+        assert torch.equal(static_out, eager)
+    _no_device_error()

@@ -1,0 +1,92 @@
+"""The oracle is pinned here: against the reference's own kernels (golden fixtures produced by
+running them under TRITON_INTERPRET=1, see tests/golden/make_golden.py) and against torch's
+bf16 -> float8_e4m3fn cast for every bf16 bit pattern."""
+import numpy as np
+import pytest
+import torch
+
+from helpers import bf16, bits, fp8, u8, assert_close
+from oracle import attention as oatt
+from oracle import e4m3
+from oracle import store as ostore
+
+DECODE_CASES = ["decode_bs32", "decode_bs256", "decode_bs16_g8"]
+PREFILL_CASES = ["prefill_paged", "prefill_paged_small", "prefill_paged_bs256", "prefill_contig"]
+
+
+def test_e4m3_cast_matches_torch_for_all_bf16():
+    allbits = np.arange(1 << 16, dtype=np.uint32).astype(np.uint16)
+    x = torch.from_numpy(allbits.view(np.int16)).view(torch.bfloat16)
+    torch_codes = x.to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+    ours = e4m3.from_bf16_bits(allbits, e4m3.TORCH)
+    xf = x.float().numpy()
+    finite = np.isfinite(xf)
+    assert np.array_equal(ours[finite], torch_codes[finite])
+    # NaN inputs: both produce a NaN code
+    nan_codes = ours[np.isnan(xf)] & 0x7F
+    assert np.all(nan_codes == 0x7F)
+    # satfinite mode agrees wherever |x| <= 464 and saturates beyond
+    sat = e4m3.from_bf16_bits(allbits, e4m3.SATFINITE)
+    small = finite & (np.abs(xf) <= 464)
+    assert np.array_equal(sat[small], torch_codes[small])
+    big = finite & (np.abs(xf) > 464)
+    assert np.all((sat[big] & 0x7F) == 0x7E)
+    assert np.array_equal(sat[big] >> 7, (allbits[big] >> 15).astype(np.uint8))
+
+
+def test_e4m3_widen_matches_torch():
+    codes = np.arange(256, dtype=np.uint8)
+    ours = e4m3.to_f32(codes)
+    ref = u8(codes).view(torch.float8_e4m3fn).float().numpy()
+    assert np.array_equal(np.isnan(ours), np.isnan(ref))
+    ok = ~np.isnan(ref)
+    assert np.array_equal(ours[ok], ref[ok])
+
+
+def test_scaled_quantiser_roundtrip():
+    rng = np.random.default_rng(0)
+    x = torch.from_numpy(rng.standard_normal((64, 128)).astype(np.float32) * 5).to(torch.bfloat16)
+    x[3] = 0
+    codes, scales = e4m3.quant_rows(bits(x))
+    assert scales[3] == 1.0 and np.all(codes[3] == 0)
+    back = e4m3.to_f32(codes) * scales[:, None]
+    amax = x.float().abs().amax(dim=1).numpy()
+    np.testing.assert_allclose(scales[amax > 0], amax[amax > 0] / 448.0, rtol=1e-6)
+    # rounding error of e4m3 is <= 2^-4 relative (plus subnormal quantum)
+    err = np.abs(back - x.float().numpy())
+    assert np.all(err <= np.abs(x.float().numpy()) / 16 + scales[:, None] * 2.0 ** -9 + 1e-30)
+
+
+def test_store_placement_matches_reference(golden):
+    g = golden("store_placement")
+    qkv = g["qkv"]
+    hq, kvh = int(g["hq"]), int(g["kvh"])
+    key = qkv[:, hq:hq + kvh]
+    value = qkv[:, hq + kvh:]
+    nb, bs = g["k_cache"].shape[:2]
+    kc = np.full(g["k_cache"].shape, int(g["init"]), dtype=np.uint8)
+    vc = np.full(g["v_cache"].shape, int(g["init"]), dtype=np.uint8)
+    ostore.store_kvcache(key, value, kc, vc, g["slots"])
+    assert np.array_equal(kc, g["k_cache"])
+    assert np.array_equal(vc, g["v_cache"])
+
+
+@pytest.mark.parametrize("name", DECODE_CASES)
+def test_decode_oracle_matches_reference(golden, name):
+    g = golden(name)
+    out = oatt.decode(bf16(g["q"]), fp8(g["k_cache"]), fp8(g["v_cache"]),
+                      torch.from_numpy(g["block_tables"]), torch.from_numpy(g["context_lens"]),
+                      float(g["scale"]))
+    ref = bf16(g["out"])
+    # same fp32 math up to summation order: agreement to a few bf16 ulps
+    assert_close(out, ref, atol=4e-3, rtol=8e-3, what=name)
+
+
+@pytest.mark.parametrize("name", PREFILL_CASES)
+def test_prefill_oracle_matches_reference(golden, name):
+    g = golden(name)
+    tables = torch.from_numpy(g["block_tables"]) if "block_tables" in g else None
+    out = oatt.prefill(bf16(g["q"]), fp8(g["k"]), fp8(g["v"]), tables,
+                       torch.from_numpy(g["cu_seqlens_q"]), torch.from_numpy(g["cu_seqlens_k"]),
+                       float(g["scale"]))
+    assert_close(out, bf16(g["out"]), atol=4e-3, rtol=8e-3, what=name)
