@@ -275,7 +275,8 @@ def run_ours(args, world, rank, local):
                      "traffic": _traffic("decode_kernel")},
         "e2e": {"value": e2e_val, "unit": "TB/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
-        "gpu_launches": args.steps,
+        "gpu_launches": 2 * args.steps,  # decode + split-KV combine per step
+        "decode_ctas": int(__import__("nanovllm_b200._lib", fromlist=["lib"]).lib.fp8attn_decode_ctas(256, 32, 8, 1)),
         "clocks": clk.summary(),
         "device_error": err,
     }

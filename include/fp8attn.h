@@ -113,8 +113,12 @@ FP8ATTN_API int fp8attn_prefill(void* out, const void* q, int64_t q_row_stride, 
                     int head_dim, int64_t num_blocks, int block_size, float softmax_scale,
                     void* workspace, int64_t workspace_bytes, void* stream);
 
-/* Tuning knob (process-wide): minimum key positions per split-KV work item, a multiple of 64
- * (default 256).  Returns the previous value; values < 64 are rejected with -1. */
+/* Persistent CTAs a decode (max_seqlen_q = 1) or prefill call of this shape launches on the
+ * current device for its split-KV engine (diagnostics and benchmarking). */
+FP8ATTN_API int fp8attn_decode_ctas(int num_seqs, int num_heads, int num_kv_heads, int max_seqlen_q);
+
+/* Tuning knob (process-wide): minimum key positions per split-KV work item, a multiple of 128
+ * (default 128).  Returns the previous value; other values are rejected with -1. */
 FP8ATTN_API int fp8attn_set_decode_min_chunk(int tokens);
 
 #ifdef __cplusplus

@@ -13,7 +13,7 @@
 namespace {
 
 thread_local std::string g_last_error;
-int g_min_chunk = 256;
+int g_min_chunk = 128;
 
 int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
 int fail(int code, const char* fmt, ...) {
@@ -93,9 +93,11 @@ EnginePlan plan_engine(int group, int max_q) {
   return e;
 }
 
+// TMA box height of the decode engine: divides both its 32-token tile and the block size.
 int box_rows_for(int block_size) {
-  if (block_size % 64 == 0) return 64;
-  if (block_size % 32 == 0) return 32;
+  static_assert(fp8attn::kDecodeTile == 128, "box heights below assume 128-token tiles");
+  for (int r = 128; r > 16; r >>= 1)
+    if (block_size % r == 0) return r;
   return 16;
 }
 
@@ -138,8 +140,16 @@ int fp8attn_version(void) { return 100; }
 
 const char* fp8attn_last_error(void) { return g_last_error.c_str(); }
 
+int fp8attn_decode_ctas(int num_seqs, int num_heads, int num_kv_heads, int max_seqlen_q) {
+  if (num_seqs < 0 || num_heads <= 0 || num_kv_heads <= 0 || num_heads % num_kv_heads) return -1;
+  const int group = num_heads / num_kv_heads;
+  const int mq = max_seqlen_q <= 1 ? 1 : (max_seqlen_q < spec_q_max(group) ? max_seqlen_q
+                                                                           : spec_q_max(group));
+  return fp8attn::decode_launch_grid(plan_engine(group, mq).nt, num_seqs);
+}
+
 int fp8attn_set_decode_min_chunk(int tokens) {
-  if (tokens < 64 || tokens % 64 != 0) return -1;
+  if (tokens < fp8attn::kDecodeTile || tokens % fp8attn::kDecodeTile != 0) return -1;
   const int prev = g_min_chunk;
   g_min_chunk = tokens;
   return prev;
@@ -208,9 +218,9 @@ static int run_decode_engine(fp8attn::DecodeParams& p, const EnginePlan& e, cons
   const int64_t pairs = static_cast<int64_t>(p.num_seqs) * p.num_kv_heads * e.max_rowgroups;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   p.ctrl = reinterpret_cast<int*>(ws);
-  p.tickets = reinterpret_cast<int*>(ws + fp8attn::kCtrlInts * 4);
-  p.partials = reinterpret_cast<float*>(ws + fp8attn::kCtrlInts * 4 + (pairs * 4 + 255) / 256 * 256);
-  p.max_items = static_cast<int>(32LL * grid + pairs);
+  p.plan = reinterpret_cast<int*>(ws + fp8attn::kCtrlInts * 4);
+  p.partials = reinterpret_cast<float*>(ws + fp8attn::kCtrlInts * 4 + fp8attn::kPlanInts * 4);
+  p.max_items = static_cast<int>(fp8attn::decode_max_items(pairs, grid));
   p.max_rowgroups = e.max_rowgroups;
   p.min_chunk = g_min_chunk;
   p.box_rows = box_rows_for(p.block_size);

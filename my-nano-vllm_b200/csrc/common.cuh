@@ -76,15 +76,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Bounded wait for the phase with the given parity to complete.  Returns false (and records
-// kDevErrWaitTimeout in *err) when the wall-clock bound is exceeded.
+// kDevErrWaitTimeout in *err) when the wall-clock bound is exceeded.  The clock is read only
+// every 1024 polls: reading %globaltimer is slow, and a wait that completes must not pay for it.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
   if (mbar_try_wait(bar, parity)) return true;
-  const unsigned long long t0 = globaltimer_ns();
-  while (true) {
+  unsigned long long t0 = 0;
+  for (uint32_t polls = 1;; ++polls) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
-      if (err) atomicExch(err, kDevErrWaitTimeout);
-      return false;
+    if ((polls & 1023u) == 0) {
+      const unsigned long long now = globaltimer_ns();
+      if (t0 == 0) {
+        t0 = now;
+      } else if (now - t0 > kWaitLimitNs) {
+        if (err) atomicExch(err, kDevErrWaitTimeout);
+        return false;
+      }
     }
   }
 }
@@ -133,6 +139,18 @@ __device__ __forceinline__ void mma_f16_16816(float (&c)[4], const uint32_t (&a)
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// D += A.B with e4m3 operands (m16n8k32, fp32 accumulate).  Fragment layout (g = lane / 4,
+// t = lane % 4): a0 = A[g][4t..4t+3], a1 = A[g+8][4t..4t+3], a2 = A[g][4t+16..], a3 = A[g+8][4t+16..]
+// (byte i = column +i); b0 = B[4t..4t+3][g], b1 = B[4t+16..4t+19][g]; c as for m16n8k16.
+__device__ __forceinline__ void mma_e4m3_16832(float (&c)[4], const uint32_t (&a)[4], uint32_t b0,
+                                               uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.f32.e4m3.e4m3.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
 __device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
   uint32_t y;
   asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
@@ -152,6 +170,30 @@ __device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t two_bytes) {
   return static_cast<uint32_t>(h.x) | (static_cast<uint32_t>(h.y) << 16);
 }
 
+// f16x2 -> two e4m3 bytes (low half -> low byte), round to nearest even, saturating.
+__device__ __forceinline__ uint32_t f16x2_to_e4m3x2(uint32_t h) {
+  __half2_raw r;
+  r.x = static_cast<unsigned short>(h & 0xFFFFu);
+  r.y = static_cast<unsigned short>(h >> 16);
+  return static_cast<uint32_t>(__nv_cvt_halfraw2_to_fp8x2(r, __NV_SATFINITE, __NV_E4M3));
+}
+
+// Two floats -> two e4m3 bytes (a -> low byte), round to nearest even, saturating.
+__device__ __forceinline__ uint32_t f32x2_to_e4m3x2(float a, float b) {
+  return static_cast<uint32_t>(
+      __nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3));
+}
+
+// x (f16x2) ~= hi + lo with hi, lo e4m3 pairs: hi = e4m3(x), lo = e4m3(x - hi).  The pair carries
+// about 8 significant bits (the residual is at most 2^-4 of x).
+__device__ __forceinline__ void split_f16x2_e4m3(uint32_t x, uint32_t& hi, uint32_t& lo) {
+  hi = f16x2_to_e4m3x2(x);
+  const uint32_t back = e4m3x2_to_f16x2(hi);
+  const __half2 r = __hsub2(*reinterpret_cast<const __half2*>(&x),
+                            *reinterpret_cast<const __half2*>(&back));
+  lo = f16x2_to_e4m3x2(*reinterpret_cast<const uint32_t*>(&r));
+}
+
 // (lo, hi) floats -> f16x2 with lo in the low half; round to nearest even.
 __device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
   __half2 h = __floats2half2_rn(lo, hi);
@@ -165,6 +207,12 @@ __device__ __forceinline__ uint32_t bf16x2_to_f16x2(uint32_t v) {
   return pack_f16x2(lo, hi);
 }
 
+__device__ __forceinline__ float lg2(float x) {
+  float y;
+  asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -174,6 +222,21 @@ __device__ __forceinline__ float ex2(float x) {
 // fp32 -> fp16 -> bf16, the reference output path (.to(tl.float16) stored into bf16).
 __device__ __forceinline__ __nv_bfloat16 out_round(float x) {
   return __float2bfloat16_rn(__half2float(__float2half_rn(x)));
+}
+
+// Read-only global loads that stay where they are written: the compiler may not sink them to
+// their first use, so a load issued early (a prefetch) really overlaps with the work after it.
+__device__ __forceinline__ int ldg_keep(const int* p) {
+  int v;
+  asm volatile("ld.global.nc.s32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ uint4 ldg_keep_v4(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
 }
 
 __device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {

@@ -1,46 +1,53 @@
-// Split-KV paged decode engine (HBM-bound).
+// Split-KV paged decode engine (HBM-bound), on the sm_100a tensor cores.
 //
 // Replaces fp8_paged_attention_decode_kernel (nanovllm/kernels/fp8_attention.py:88-171) and,
 // inside the prefill entry point, serves the short query sequences of speculative verification
 // (1 + k rows per sequence, causal among themselves).
 //
 // Work decomposition.  A work item is (sequence, kv head, row group, chunk of key positions).
-// A row group is up to ROWS = 8*NT query rows that share one kv head (GQA: the group's q heads,
-// times the sequence's query tokens in spec mode), so each K/V byte is loaded from HBM once per
-// row group -- once in total for decode, where all q heads of a kv head fit one group.  Every CTA
-// first computes the same plan from the sequence lengths (chunk size, item prefix sums in shared
-// memory); then a persistent grid pulls items from an atomic counter.  Chunks of one
-// (sequence, kv head, row group) are consecutive items, so the split-KV partial results are
-// combined by whichever CTA finishes the pair's last chunk (atomic ticket), with no second
-// launch and no spinning.
+// A row group is up to R = 8*NT query rows that share one kv head (GQA: the group's q heads,
+// times the sequence's query tokens in spec mode), so each K/V byte is read from HBM once per
+// row group -- once in total for decode.  Every CTA first computes the same plan from the
+// sequence lengths (chunk size, item prefix sums in shared memory), then a persistent grid pulls
+// items from an atomic counter.  Chunks of one (sequence, kv head, row group) are consecutive
+// items; their partial results are combined by whichever CTA finishes the pair's last chunk
+// (atomic ticket): no second launch and no spinning.
 //
-// CTA = 4 consumer warps + 1 producer warp.  The producer walks the items, looks block ids up in
-// block_tables and issues TMA loads of 64-token K and V tiles (128-byte rows, 128B swizzle) into
-// a STAGES-deep ring, plus a 1-D bulk copy of the item's query rows.  Each consumer warp takes
-// 16 of the 64 tokens of a tile:
-//   S^T[16 tok x 8 rows] = K[16 x 128] . Q^T   mma.sync m16n8k16, K dequantised e4m3 -> f16 in
-//                                              registers (exact), Q bf16 -> f16
-//   online softmax per query row (exp2 domain), P^T moved into B-fragment layout by movmatrix
-//   O^T[128 dims x 8 rows] += V^T . P^T        V transposed in registers by byte permutes
-// The contraction index permutations (dims inside QK, output dims inside PV) are chosen so every
-// shared-memory read is a conflict-free 16-byte load; outputs are un-permuted at the store.
+// One CTA per SM, six warps:
+//   warp 4  producer: walks the items, looks block ids up in block_tables, issues TMA loads of
+//           128-token K and V tiles (128-byte rows, 128B swizzle) into a 4-deep ring, and
+//           prepares each item's query rows as e4m3 hi + lo pairs (q scaled by a power of two per
+//           row, about 8 significant bits in total);
+//   warp 5  MMA issuer (one thread), per tile j:
+//             S^T[128 tok x 2R]  = K_j . [Qhi; Qlo]^T          tcgen05.mma kind::f8f6f4 (e4m3)
+//             PV^T[128 dim x 2R] = V_{j-1}^T . [Phi; Plo]^T    (V read MN-major from its tile)
+//           both double-buffered in tensor memory, P double-buffered in shared memory;
+//   warps 0-3 softmax: thread = token row of S^T (and dim row of PV^T): online softmax with the
+//           column max from redux.sync + a 4-warp exchange, P quantised as 256 p = hi + lo e4m3;
+//           the output accumulates in registers, folding in each tile's PV product two tiles
+//           later, so softmax and tensor cores never wait on each other within an item.
+// K and V bytes go to the tensor cores untouched: no per-byte conversion anywhere.
 #include <climits>
 
 #include "common.cuh"
 #include "kernels.h"
+#include "tcgen05.cuh"
 
 namespace fp8attn {
 namespace {
 
-constexpr int kTile = 64;            // tokens per pipeline stage
-constexpr int kConsumerWarps = 4;
-constexpr int kDecodeThreads = (kConsumerWarps + 1) * 32;
-constexpr int kConsumerThreads = kConsumerWarps * 32;
+constexpr int kTile = kDecodeTile;  // key positions per stage
+constexpr int kMaxCtasPerSm = 2;  // the ring is sized so two CTAs share an SM
+constexpr int kProducerWarp = 4;
+constexpr int kMmaWarp = 5;
+constexpr int kThreads = 8 * 32;  // warps 6-7 idle (no role): 2 warps per scheduler, 2 CTAs per SM
+constexpr int kSoftmaxThreads = 128;
 constexpr int kMaxBoxes = kTile / 16;
+constexpr int kItemsPerCta = 16;  // plan target: work items per CTA
 
 enum : int { kFirst = 1, kLast = 2 };
 
-struct StageHeader {
+struct TileHeader {
   int item;  // < 0: no more work
   int seq, kvh, rg;
   int tok0;    // key position of the tile's first row
@@ -48,37 +55,42 @@ struct StageHeader {
   int flags;
   int nchunks;
   int pair_first;  // item id of the pair's chunk 0
-  int nq;
-  int qrow0;  // first query token row of the sequence
-  int rows;   // valid query rows in this row group
+  int pair_stride; // item ids of the pair's chunks are pair_first + c * pair_stride
+  int qrow0;       // first query token row of the sequence
+  int rows;        // valid query rows in this row group
   int qslot;
-  int lim_base;  // causal limit of the row group's token 0: key positions <= lim_base + j
-  int blk[kMaxBoxes];  // physical block of each box (-1: invalid)
-};
-
-template <int NT>
-struct DecodeCfg {
-  static constexpr int ROWS = 8 * NT;
-  static constexpr int STAGES = NT == 1 ? 4 : 3;
+  int lim_base;              // causal limit of the row group's first query token
+  int blk[kMaxBoxes];        // physical block of each box (-1: masked)
+  int slot0[kMaxBoxes];      // cache row of each box's first token
 };
 
 template <int NT>
 struct __align__(1024) DecodeSmem {
-  static constexpr int ROWS = DecodeCfg<NT>::ROWS;
-  static constexpr int STAGES = DecodeCfg<NT>::STAGES;
-  uint8_t k[STAGES][kTile * kHeadDim];  // each stage 1024-aligned (8 KB)
+  static constexpr int R = 8 * NT;  // query rows per item
+  static constexpr int N = 2 * R;   // S / O columns: rows 0..R-1 hi, R..2R-1 lo
+  static constexpr int STAGES = NT == 1 ? 3 : 2;  // two CTAs per SM fit either way
+  uint8_t k[STAGES][kTile * kHeadDim];  // 16 KB each, 1024-aligned
   uint8_t v[STAGES][kTile * kHeadDim];
-  uint16_t qbuf[2][ROWS][kHeadDim];  // bf16 query rows, double-buffered by item
-  float mrg_o[kConsumerWarps][ROWS][kHeadDim + 4];
-  float mrg_m[kConsumerWarps][ROWS];
-  float mrg_l[kConsumerWarps][ROWS];
-  int prefix[kMaxSeqs + 1];  // item prefix sums over sequences
-  int info[kMaxSeqs];        // (L << 7) | rowgroups, per sequence
-  StageHeader hdr[STAGES];
-  uint64_t full[STAGES];
-  uint64_t empty[STAGES];
-  uint64_t qempty[2];
-  int scratch[8];
+  uint8_t q2[2][N * kHeadDim];            // K-major SW128 query operand, by item parity
+  uint8_t p2[2][NT][kTile * 16];          // P^T planes of 16 columns, MN-major, by tile parity
+  float qscale[2][R];                     // per-row score multiplier (scale * log2 e * 2^k)
+  float red[2][4][R];                     // cross-warp row maxima, double-buffered by tile
+  float redl[4][R];                       // cross-warp row sums (epilogue)
+  TileHeader hdr[STAGES];
+  uint64_t kv_full[STAGES];
+  uint64_t kv_empty[STAGES];
+  uint64_t s_full[2];
+  uint64_t s_empty[2];
+  uint64_t p_full[2];
+  uint64_t pv_done[2];
+  uint64_t q_full[2];
+  uint64_t q_empty[2];
+  uint64_t sync128;  // bounded barrier of the 128 softmax threads
+  uint32_t tmem_base;
+  int scratch[16];
+  unsigned long long total_work;
+  // followed in shared memory by int prefix[num_seqs + 1] (item prefix sums over sequences)
+  // and int info[num_seqs] ((L << 7) | rowgroups per sequence), sized per launch
 };
 
 __device__ __forceinline__ int seq_len_clamped(const DecodeParams& p, int b, int* nq_out) {
@@ -97,8 +109,8 @@ __device__ __forceinline__ int seq_len_clamped(const DecodeParams& p, int b, int
   return L;
 }
 
-// Block-wide exclusive scan of one int per thread (all kDecodeThreads threads participate).
-__device__ __forceinline__ int block_exclusive_scan(int v, int* smem8, int* total) {
+// Block-wide exclusive scan of one int per thread.
+__device__ __forceinline__ int block_exclusive_scan(int v, int* smem, int* total) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   int x = v;
 #pragma unroll
@@ -106,12 +118,12 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* smem8, int* tota
     const int y = __shfl_up_sync(0xffffffffu, x, o);
     if (lane >= o) x += y;
   }
-  if (lane == 31) smem8[warp] = x;
+  if (lane == 31) smem[warp] = x;
   __syncthreads();
   int base = 0, tot = 0;
 #pragma unroll
-  for (int w = 0; w < kDecodeThreads / 32; ++w) {
-    const int s = smem8[w];
+  for (int w = 0; w < kThreads / 32; ++w) {
+    const int s = smem[w];
     if (w < warp) base += s;
     tot += s;
   }
@@ -120,13 +132,163 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* smem8, int* tota
   return base + x - v;
 }
 
+// Order-preserving float <-> int maps (for redux.sync max).
+__device__ __forceinline__ int f2ord(float f) {
+  const int i = __float_as_int(f);
+  return i >= 0 ? i : i ^ 0x7FFFFFFF;
+}
+__device__ __forceinline__ float ord2f(int i) { return __int_as_float(i >= 0 ? i : i ^ 0x7FFFFFFF); }
+
+// Producer cursor: the item whose tiles are being issued.  Warp-uniform.
 template <int NT>
-__global__ void __launch_bounds__(kDecodeThreads, NT == 1 ? 2 : 2)
+struct Cursor {
+  int item;  // >= total_items: exhausted
+  int next;  // prefetched id of the following item (lane 0 holds the atomic's result)
+  int b, kvh, rg, c, nchunks, t0, t1, t;
+  int qrow0, rows, lim_base, row0;
+  int pair_first, pair_stride;
+  int nth;           // items started (selects the q buffer)
+  int ebase, myent;  // block-table entries ebase .. ebase+31, one per lane
+  uint4 qraw[4 * NT];  // this lane's slice of the item's q rows (bf16), loaded when the item is
+                     // claimed and consumed one item later, so no load latency is ever waited on
+};
+
+template <int NT>
+__device__ __forceinline__ void cursor_set(Cursor<NT>& P, int item, const DecodeParams& p,
+                                           const int* prefix, const int* info, int total_items,
+                                           int CT, int B) {
+  constexpr int R = DecodeSmem<NT>::R;
+  P.item = item;
+  if (item >= total_items) return;
+  int lo = 0, hi = B - 1;  // largest b with prefix[b] <= item
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (prefix[mid] <= item) lo = mid; else hi = mid - 1;
+  }
+  const int b = lo;
+  const int inf = info[b];
+  const int L = inf >> 7, nrg = inf & 127;
+  const int nchunks = (L + CT - 1) / CT;
+  // items of sequence b: chunk-major, then kv head, then row group, so the CTAs that start
+  // at about the same time read the same token rows (neighbouring heads share DRAM pages)
+  const int r = item - prefix[b];
+  const int npairs = p.num_kv_heads * nrg;
+  const int c = r / npairs;
+  const int pair_local = r - c * npairs;
+  P.b = b;
+  P.kvh = pair_local / nrg;
+  P.rg = pair_local - P.kvh * nrg;
+  P.c = c;
+  P.pair_first = prefix[b] + pair_local;
+  P.pair_stride = npairs;
+  P.nchunks = nchunks;
+  P.t0 = c * CT;
+  P.t1 = min(L, P.t0 + CT);
+  P.t = P.t0;
+  int nq = 1;
+  P.qrow0 = b;
+  P.lim_base = INT_MAX / 2;
+  if (p.spec_mode) {
+    P.qrow0 = __ldg(p.cu_q + b);
+    nq = __ldg(p.cu_q + b + 1) - P.qrow0;
+    const int nk = __ldg(p.cu_k + b + 1) - __ldg(p.cu_k + b);
+    P.lim_base = nk - nq;
+  }
+  P.row0 = P.rg * R;
+  P.rows = min(R, nq * p.group - P.row0);
+  if (p.spec_mode) P.lim_base += P.row0 / p.group;
+  // start the loads the item will need: its first 32 block-table entries and its q rows
+  const int lane = threadIdx.x & 31;
+  P.ebase = P.t0 / p.block_size;
+  const int idx = P.ebase + lane;
+  P.myent = idx < p.max_blocks
+                ? ldg_keep(p.block_tables + static_cast<int64_t>(b) * p.bt_stride + idx) : -1;
+  const int G = p.group;
+#pragma unroll
+  for (int pass = 0; pass < NT; ++pass) {
+    const int rq = pass * 8 + (lane >> 2);
+    if (rq < P.rows) {
+      const int rr = P.row0 + rq;
+      const int j = rr / G, h = P.kvh * G + (rr - j * G);
+      const uint4* src = reinterpret_cast<const uint4*>(
+          p.q + static_cast<int64_t>(P.qrow0 + j) * p.q_row_stride + static_cast<int64_t>(h) * kHeadDim + 32 * (lane & 3));
+#pragma unroll
+      for (int i = 0; i < 4; ++i) P.qraw[4 * pass + i] = ldg_keep_v4(src + i);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) P.qraw[4 * pass + i] = make_uint4(0, 0, 0, 0);
+    }
+  }
+}
+
+// The item's query rows -> K-major SW128 [hi rows | lo rows] operand + per-row multipliers.
+// Lane l handles row (l >> 2) (+ 8 per pass) and dims 32 (l & 3) .. +32, from P.qraw.
+template <int NT>
+__device__ __forceinline__ void prepare_q(const Cursor<NT>& P, int slot, const DecodeParams& p,
+                                          DecodeSmem<NT>& sm, int lane) {
+  constexpr int R = DecodeSmem<NT>::R;
+  const int quarter = lane & 3;
+#pragma unroll
+  for (int pass = 0; pass < NT; ++pass) {
+    const int r = pass * 8 + (lane >> 2);
+    float q[32];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint4 w = P.qraw[4 * pass + i];
+      const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        q[8 * i + 2 * k] = __uint_as_float(ww[k] << 16);
+        q[8 * i + 2 * k + 1] = __uint_as_float(ww[k] & 0xFFFF0000u);
+      }
+    }
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(q[i]));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    int ex = 0;  // |q| / 2^(ex-7) < 256 for the row's largest element
+    if (amax > 0.f && amax < INFINITY) ex = ((__float_as_uint(amax) >> 23) & 0xFF) - 127;
+    ex = max(-100, min(ex, 120));
+    const float inv_s = __uint_as_float(static_cast<uint32_t>(127 + 7 - ex) << 23);
+    const float s_row = __uint_as_float(static_cast<uint32_t>(127 - 7 + ex) << 23);
+    uint32_t hi[8], lo[8];
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      const float x0 = q[4 * w] * inv_s, x1 = q[4 * w + 1] * inv_s;
+      const float x2 = q[4 * w + 2] * inv_s, x3 = q[4 * w + 3] * inv_s;
+      const uint32_t h01 = f32x2_to_e4m3x2(x0, x1), h23 = f32x2_to_e4m3x2(x2, x3);
+      const uint32_t r01 = e4m3x2_to_f16x2(h01), r23 = e4m3x2_to_f16x2(h23);
+      const __half2 b01 = *reinterpret_cast<const __half2*>(&r01);
+      const __half2 b23 = *reinterpret_cast<const __half2*>(&r23);
+      const uint32_t l01 = f32x2_to_e4m3x2(x0 - __low2float(b01), x1 - __high2float(b01));
+      const uint32_t l23 = f32x2_to_e4m3x2(x2 - __low2float(b23), x3 - __high2float(b23));
+      hi[w] = h01 | (h23 << 16);
+      lo[w] = l01 | (l23 << 16);
+    }
+    // rows r (hi) and R + r (lo), 16-byte chunks 2*quarter and 2*quarter + 1, 128B swizzle
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int chunk = 2 * quarter + half;
+      const int rh = r, rl = R + r;
+      *reinterpret_cast<uint4*>(&sm.q2[slot][rh * 128 + ((chunk ^ (rh & 7)) << 4)]) =
+          make_uint4(hi[4 * half], hi[4 * half + 1], hi[4 * half + 2], hi[4 * half + 3]);
+      *reinterpret_cast<uint4*>(&sm.q2[slot][rl * 128 + ((chunk ^ (rl & 7)) << 4)]) =
+          make_uint4(lo[4 * half], lo[4 * half + 1], lo[4 * half + 2], lo[4 * half + 3]);
+    }
+    if (quarter == 0) sm.qscale[slot][r] = s_row * p.scale_log2;
+  }
+}
+
+template <int NT>
+__global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
     decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                   const DecodeParams p) {
   using Smem = DecodeSmem<NT>;
-  constexpr int ROWS = Smem::ROWS;
-  constexpr int STAGES = Smem::STAGES;
+  constexpr int R = Smem::R;
+  constexpr int N = Smem::N;
+  constexpr int kStages = Smem::STAGES;
+  constexpr uint32_t kTmemCols = NT == 1 ? 64 : 128;  // S x2 and PV x2, N columns each
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -135,520 +297,503 @@ __global__ void __launch_bounds__(kDecodeThreads, NT == 1 ? 2 : 2)
   const int warp = tid >> 5, lane = tid & 31;
   const int G = p.group;
   const int B = p.num_seqs;
+  int* prefix = reinterpret_cast<int*>(&sm + 1);
+  int* info = prefix + (B + 1);
 
   if (tid == 0) {
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&sm.full[s], 1);
-      mbar_init(&sm.empty[s], kConsumerWarps);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&sm.kv_full[s], 1);
+      mbar_init(&sm.kv_empty[s], 1);
     }
-    mbar_init(&sm.qempty[0], kConsumerWarps);
-    mbar_init(&sm.qempty[1], kConsumerWarps);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sm.s_full[i], 1);
+      mbar_init(&sm.s_empty[i], kSoftmaxThreads);
+      mbar_init(&sm.q_full[i], 32);
+      mbar_init(&sm.q_empty[i], kSoftmaxThreads);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sm.p_full[i], kSoftmaxThreads);
+      mbar_init(&sm.pv_done[i], 1);
+    }
+    mbar_init(&sm.sync128, kSoftmaxThreads);
     fence_mbar_init();
+    sm.total_work = 0;
   }
-  if (warp == kConsumerWarps && lane == 0) {
+  if (warp == kProducerWarp && lane == 0) {
     prefetch_tensormap(&tmk);
     prefetch_tensormap(&tmv);
   }
+  if (warp == kMmaWarp) {
+    tc::tmem_alloc(&sm.tmem_base, kTmemCols);
+    tc::tmem_relinquish();
+  }
 
   // ---------------------------------------------------------------- plan (every CTA, same result)
-  // Each thread owns a contiguous run of sequences.
-  const int per = (B + kDecodeThreads - 1) / kDecodeThreads;
+  const int per = (B + kThreads - 1) / kThreads;
   const int s0 = min(B, tid * per), s1 = min(B, s0 + per);
-  const int max_rows_pass = ROWS;
   long long my_work = 0;
   for (int b = s0; b < s1; ++b) {
     int nq;
     const int L = seq_len_clamped(p, b, &nq);
-    const int rows = nq * G;
-    const int rg = L > 0 ? (rows + max_rows_pass - 1) / max_rows_pass : 0;
-    sm.info[b] = (L << 7) | rg;
+    const int rg = L > 0 ? (nq * G + R - 1) / R : 0;
+    info[b] = (L << 7) | rg;
     my_work += static_cast<long long>(L) * rg;
   }
-  // total key-position passes (x kv heads) -> chunk size targeting ~32 items per CTA
-  __shared__ unsigned long long s_total;
-  if (tid == 0) s_total = 0;
+  tc::fence_before_sync();
   __syncthreads();
-  if (my_work) atomicAdd(&s_total, static_cast<unsigned long long>(my_work));
+  tc::fence_after_sync();
+  if (my_work) atomicAdd(&sm.total_work, static_cast<unsigned long long>(my_work));
   __syncthreads();
-  const unsigned long long total_work = s_total * static_cast<unsigned long long>(p.num_kv_heads);
-  const unsigned long long target = 32ull * gridDim.x;
+  const uint32_t tmem = sm.tmem_base;
+  const unsigned long long total_work =
+      sm.total_work * static_cast<unsigned long long>(p.num_kv_heads);
+  const unsigned long long target = static_cast<unsigned long long>(kItemsPerCta) * gridDim.x;
   long long ct = static_cast<long long>((total_work + target - 1) / target);
-  ct = (ct + kTile - 1) / kTile * kTile;
   if (ct < p.min_chunk) ct = p.min_chunk;
+  ct = (ct + kTile - 1) / kTile * kTile;
   const int CT = static_cast<int>(ct > (1 << 24) ? (1 << 24) : ct);
 
   int my_items = 0;
   for (int b = s0; b < s1; ++b) {
-    const int inf = sm.info[b];
-    const int L = inf >> 7, rg = inf & 127;
-    my_items += ((L + CT - 1) / CT) * p.num_kv_heads * rg;
+    const int inf = info[b];
+    my_items += (((inf >> 7) + CT - 1) / CT) * p.num_kv_heads * (inf & 127);
   }
   int total_items;
   const int base = block_exclusive_scan(my_items, sm.scratch, &total_items);
   {
     int acc = base;
     for (int b = s0; b < s1; ++b) {
-      sm.prefix[b] = acc;
-      const int inf = sm.info[b];
-      const int L = inf >> 7, rg = inf & 127;
-      acc += ((L + CT - 1) / CT) * p.num_kv_heads * rg;
+      prefix[b] = acc;
+      const int inf = info[b];
+      acc += (((inf >> 7) + CT - 1) / CT) * p.num_kv_heads * (inf & 127);
     }
-    if (tid == kDecodeThreads - 1) sm.prefix[B] = total_items;
+    if (tid == kThreads - 1) prefix[B] = total_items;
   }
   __syncthreads();
+  if (blockIdx.x == 0) {  // the combine kernel reads the same plan after this launch
+    for (int b = tid; b <= B; b += kThreads) p.plan[2 + b] = prefix[b];
+    if (tid == 0) {
+      p.plan[0] = CT;
+      p.plan[1] = total_items;
+    }
+  }
   // partial results are indexed by item id; a workspace sized by decode_workspace_bytes always
-  // has room, anything else is reported instead of overrunning it
-  const bool fits = total_items <= p.max_items;
+  // has room, and a TMA box must fit its stage: anything else is reported, never overrun
+  const bool fits = total_items <= p.max_items && p.box_rows >= 16 && p.box_rows <= kTile &&
+                    kTile % p.box_rows == 0;
   if (!fits && tid == 0 && blockIdx.x == 0) atomicExch(p.ctrl, kDevErrWorkspace);
 
-  if (!fits) {
-    // nothing to do
-  } else if (warp == kConsumerWarps) {
-    // ============================================================ producer warp
-    int stage = 0;
-    uint32_t phase = 0;
-    int nth = 0;  // items taken by this CTA
-    int item = 0;
-    if (lane == 0) item = atomicAdd(p.ctrl + 1, 1);
-    item = __shfl_sync(0xffffffffu, item, 0);
-    bool ok = true;
-    while (ok && item < total_items) {
-      int nxt = 0;
-      if (lane == 0) nxt = atomicAdd(p.ctrl + 1, 1);
-      // locate the sequence: largest b with prefix[b] <= item
-      int lo = 0, hi = B - 1;
-      while (lo < hi) {
-        const int mid = (lo + hi + 1) >> 1;
-        if (sm.prefix[mid] <= item) lo = mid; else hi = mid - 1;
-      }
-      const int b = lo;
-      const int inf = sm.info[b];
-      const int L = inf >> 7, nrg = inf & 127;
-      const int nchunks = (L + CT - 1) / CT;
-      const int r = item - sm.prefix[b];
-      const int pair_local = r / nchunks;
-      const int c = r - pair_local * nchunks;
-      const int kvh = pair_local / nrg;
-      const int rg = pair_local - kvh * nrg;
-      int nq = 1, qrow0 = b, lim_base = INT_MAX / 2;
-      if (p.spec_mode) {
-        qrow0 = __ldg(p.cu_q + b);
-        nq = __ldg(p.cu_q + b + 1) - qrow0;
-        const int nk = __ldg(p.cu_k + b + 1) - __ldg(p.cu_k + b);
-        lim_base = nk - nq;
-      }
-      const int rows_total = nq * G;
-      const int row0 = rg * ROWS;
-      const int rows = min(ROWS, rows_total - row0);
-      const int t0 = c * CT;
-      const int t1 = min(L, t0 + CT);
-      const int qslot = nth & 1;
-      const uint32_t qbytes = static_cast<uint32_t>(rows) * kHeadDim * 2;
-
-      // the item's query rows go into qbuf[qslot] once the consumers released it
-      if (!mbar_wait(&sm.qempty[qslot], ((nth >> 1) & 1) ^ 1, p.ctrl)) { ok = false; break; }
-
-      int ebase = INT_MIN / 2, myent = -1;
-      const int64_t bt_row = static_cast<int64_t>(b) * p.bt_stride;
-      for (int t = t0; t < t1 && ok; t += kTile) {
-        if (!mbar_wait(&sm.empty[stage], phase ^ 1, p.ctrl)) { ok = false; break; }
-        const int nvalid = min(kTile, t1 - t);
-        const int nbox = (nvalid + p.box_rows - 1) / p.box_rows;
-        int blks[kMaxBoxes];
-#pragma unroll
-        for (int j = 0; j < kMaxBoxes; ++j) {
-          blks[j] = -1;
-          if (j < nbox) {
-            const int pos = t + j * p.box_rows;
-            const int e = pos / p.block_size;
-            if (e < ebase || e >= ebase + 32) {
-              ebase = e;
-              const int idx = ebase + lane;
-              myent = idx < p.max_blocks ? __ldg(p.block_tables + bt_row + idx) : -1;
-            }
-            int blk = __shfl_sync(0xffffffffu, myent, e - ebase);
-            if (blk < 0 || blk >= p.num_blocks) blk = -1;
-            blks[j] = blk;
-          }
-        }
-        if (lane == 0) {
-          StageHeader& h = sm.hdr[stage];
-          h.item = item;
-          h.seq = b;
-          h.kvh = kvh;
-          h.rg = rg;
-          h.tok0 = t;
-          h.nvalid = nvalid;
-          h.flags = (t == t0 ? kFirst : 0) | (t + kTile >= t1 ? kLast : 0);
-          h.nchunks = nchunks;
-          h.pair_first = item - c;
-          h.nq = nq;
-          h.qrow0 = qrow0;
-          h.rows = rows;
-          h.qslot = qslot;
-          h.lim_base = lim_base + (p.spec_mode ? row0 / G : 0);
-#pragma unroll
-          for (int j = 0; j < kMaxBoxes; ++j) h.blk[j] = blks[j];
-          uint32_t bytes = 0;
-#pragma unroll
-          for (int j = 0; j < kMaxBoxes; ++j)
-            if (blks[j] >= 0) bytes += 2u * p.box_rows * kHeadDim;
-          if (t == t0) bytes += qbytes;
-          mbar_arrive_expect_tx(&sm.full[stage], bytes);
-#pragma unroll
-          for (int j = 0; j < kMaxBoxes; ++j) {
-            if (blks[j] >= 0) {
-              const int pos = t + j * p.box_rows;
-              const int y = blks[j] * p.block_size + (pos % p.block_size);
-              const int x = kvh * kHeadDim;
-              tma_load_2d(&sm.k[stage][j * p.box_rows * kHeadDim], &tmk, &sm.full[stage], x, y);
-              tma_load_2d(&sm.v[stage][j * p.box_rows * kHeadDim], &tmv, &sm.full[stage], x, y);
-            }
-          }
-          if (t == t0) {
-            // query rows row0 .. row0+rows-1: row r is (token r / G, head kvh*G + r % G); rows
-            // of one token are contiguous in q
-            int r = row0;
-            while (r < row0 + rows) {
-              const int j = r / G;
-              const int g = r - j * G;
-              const int run = min(G - g, row0 + rows - r);
-              const uint16_t* src = p.q + static_cast<int64_t>(qrow0 + j) * p.q_row_stride +
-                                    static_cast<int64_t>(kvh * G + g) * kHeadDim;
-              bulk_load(&sm.qbuf[qslot][r - row0][0], src, run * kHeadDim * 2, &sm.full[stage]);
-              r += run;
-            }
-          }
-        }
-        __syncwarp();
-        if (++stage == STAGES) { stage = 0; phase ^= 1; }
-      }
-      ++nth;
-      item = __shfl_sync(0xffffffffu, nxt, 0);
+  // zero the outputs of routed sequences without key positions (reference: acc / max(s, 1e-10))
+  for (int b = blockIdx.x; b < B; b += gridDim.x) {
+    if ((info[b] >> 7) != 0) continue;
+    int nq = 1, qrow0 = b;
+    if (p.spec_mode) {
+      qrow0 = __ldg(p.cu_q + b);
+      nq = __ldg(p.cu_q + b + 1) - qrow0;
+      if (nq < 1 || nq > p.spec_q_max) continue;
     }
-    // termination marker
-    if (ok && mbar_wait(&sm.empty[stage], phase ^ 1, p.ctrl)) {
-      if (lane == 0) {
-        sm.hdr[stage].item = -1;
-        mbar_arrive(&sm.full[stage]);
-      }
-    } else if (lane == 0) {
-      // timed out: still release the consumers so they can leave
-      sm.hdr[stage].item = -1;
-      mbar_arrive(&sm.full[stage]);
-    }
-  } else {
-    // ============================================================ consumer warps
-    const int g = lane >> 2, t = lane & 3;
-    // zero outputs of routed sequences that have no key positions (reference: acc/max(s,1e-10))
-    for (int b = blockIdx.x; b < B; b += gridDim.x) {
-      const int inf = sm.info[b];
-      if ((inf >> 7) != 0) continue;
-      int nq = 1, qrow0 = b;
-      if (p.spec_mode) {
-        qrow0 = __ldg(p.cu_q + b);
-        nq = __ldg(p.cu_q + b + 1) - qrow0;
-        if (nq < 1 || nq > p.spec_q_max) continue;
-      }
-      const int per_row = p.num_heads * kHeadDim / 8;  // uint4 per token row
-      for (int j = 0; j < nq; ++j) {
-        uint4* dst = reinterpret_cast<uint4*>(p.out + static_cast<int64_t>(qrow0 + j) * p.out_row_stride);
-        for (int i = tid; i < per_row; i += kConsumerThreads) dst[i] = make_uint4(0, 0, 0, 0);
-      }
-    }
-
-    uint32_t qf[NT][2][4][2];  // Q B-fragments [n-tile][chunk half][word][b0b1 / b2b3]
-    float o[8][NT][4];         // O^T accumulators [m-tile][n-tile][c0..c3]
-    float m_run[NT][2], l_run[NT][2];
-    int lim[NT][2];
-
-    int stage = 0;
-    uint32_t phase = 0;
-    while (true) {
-      if (!mbar_wait(&sm.full[stage], phase, p.ctrl)) break;
-      const StageHeader h = sm.hdr[stage];
-      if (h.item < 0) break;
-      const uint32_t kbase = smem_u32(&sm.k[stage][0]);
-      const uint32_t vbase = smem_u32(&sm.v[stage][0]);
-
-      if (h.flags & kFirst) {
-        // query fragments: n-tile nt row (8nt + g), physical dims [32t, 32t + 32)
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-          const int row = 8 * nt + g;
-#pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {
-            uint4 a = make_uint4(0, 0, 0, 0), bq = make_uint4(0, 0, 0, 0);
-            if (row < h.rows) {
-              const uint4* src = reinterpret_cast<const uint4*>(&sm.qbuf[h.qslot][row][16 * (2 * t + hh)]);
-              a = src[0];
-              bq = src[1];
-            }
-            const uint32_t wv[8] = {a.x, a.y, a.z, a.w, bq.x, bq.y, bq.z, bq.w};
-#pragma unroll
-            for (int w = 0; w < 4; ++w) {
-              qf[nt][hh][w][0] = bf16x2_to_f16x2(wv[2 * w]);      // dims 4w+0, 4w+1
-              qf[nt][hh][w][1] = bf16x2_to_f16x2(wv[2 * w + 1]);  // dims 4w+2, 4w+3
-            }
-          }
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int col = 8 * nt + 2 * t + e;
-            lim[nt][e] = col < h.rows ? (p.spec_mode ? h.lim_base + (col + (h.rg * ROWS) % G) / G
-                                                      : INT_MAX)
-                                      : -1;
-            m_run[nt][e] = -INFINITY;
-            l_run[nt][e] = 0.f;
-          }
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&sm.qempty[h.qslot]);
-#pragma unroll
-        for (int mt = 0; mt < 8; ++mt)
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-            for (int i = 0; i < 4; ++i) o[mt][nt][i] = 0.f;
-      }
-
-      const int slice0 = warp * 16;  // my 16 rows of the tile
-      if (slice0 < h.nvalid) {
-        // ------------------------------------------------ S^T = K . Q^T
-        float s[NT][4];
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
-        const int rk = slice0 + g;
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          const int cchunk = 2 * t + hh;
-          const uint4 k0 = ld_shared_v4(kbase + rk * 128 + ((cchunk ^ g) << 4));
-          const uint4 k1 = ld_shared_v4(kbase + (rk + 8) * 128 + ((cchunk ^ g) << 4));
-          const uint32_t w0[4] = {k0.x, k0.y, k0.z, k0.w};
-          const uint32_t w1[4] = {k1.x, k1.y, k1.z, k1.w};
-#pragma unroll
-          for (int w = 0; w < 4; ++w) {
-            uint32_t a[4];
-            a[0] = e4m3x2_to_f16x2(w0[w]);        // row g,   dims 4w+0..1
-            a[1] = e4m3x2_to_f16x2(w1[w]);        // row g+8, dims 4w+0..1
-            a[2] = e4m3x2_to_f16x2(w0[w] >> 16);  // row g,   dims 4w+2..3
-            a[3] = e4m3x2_to_f16x2(w1[w] >> 16);  // row g+8, dims 4w+2..3
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt) mma_f16_16816(s[nt], a, qf[nt][hh][w][0], qf[nt][hh][w][1]);
-          }
-        }
-        // ------------------------------------------------ scales, masks, online softmax
-        const int box_lo = (slice0 + g) / p.box_rows, box_hi = (slice0 + g + 8) / p.box_rows;
-        const bool vlo = (slice0 + g) < h.nvalid && h.blk[box_lo] >= 0;
-        const bool vhi = (slice0 + g + 8) < h.nvalid && h.blk[box_hi] >= 0;
-        const int pos_lo = h.tok0 + slice0 + g, pos_hi = pos_lo + 8;
-        float ks_lo = 1.f, ks_hi = 1.f;
-        if (p.k_scale != nullptr) {
-          if (vlo) ks_lo = __ldg(p.k_scale + (static_cast<int64_t>(h.blk[box_lo]) * p.block_size + pos_lo % p.block_size) * p.num_kv_heads + h.kvh);
-          if (vhi) ks_hi = __ldg(p.k_scale + (static_cast<int64_t>(h.blk[box_hi]) * p.block_size + pos_hi % p.block_size) * p.num_kv_heads + h.kvh);
-        }
-        float pf[NT][4];
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            float xl = s[nt][e] * ks_lo * p.scale_log2;
-            float xh = s[nt][2 + e] * ks_hi * p.scale_log2;
-            if (!(vlo && pos_lo <= lim[nt][e])) xl = -INFINITY;
-            if (!(vhi && pos_hi <= lim[nt][e])) xh = -INFINITY;
-            float mx = fmaxf(xl, xh);
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-            const float m_new = fmaxf(m_run[nt][e], mx);
-            const float m_use = m_new == -INFINITY ? 0.f : m_new;
-            const float alpha = ex2(m_run[nt][e] - m_use);
-            const float pl = ex2(xl - m_use), ph = ex2(xh - m_use);
-            l_run[nt][e] = l_run[nt][e] * alpha + pl + ph;
-            m_run[nt][e] = m_new;
-            pf[nt][e] = pl;
-            pf[nt][2 + e] = ph;
-#pragma unroll
-            for (int mt = 0; mt < 8; ++mt) {
-              o[mt][nt][e] *= alpha;
-              o[mt][nt][2 + e] *= alpha;
-            }
-          }
-        }
-        // P^T as B fragments (tokens 2t,2t+1 | 2t+8,2t+9 for row g)
-        uint32_t pb[NT][2];
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-          pb[nt][0] = movmatrix_trans(pack_f16x2(pf[nt][0], pf[nt][1]));
-          pb[nt][1] = movmatrix_trans(pack_f16x2(pf[nt][2], pf[nt][3]));
-        }
-        // ------------------------------------------------ O^T += V^T . P^T
-        const int vt[4] = {slice0 + 2 * t, slice0 + 2 * t + 1, slice0 + 2 * t + 8, slice0 + 2 * t + 9};
-        uint4 vw[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          vw[i] = ld_shared_v4(vbase + vt[i] * 128 + ((g ^ (vt[i] & 7)) << 4));
-          const bool ok = vt[i] < h.nvalid && h.blk[vt[i] / p.box_rows] >= 0;
-          if (!ok) vw[i] = make_uint4(0, 0, 0, 0);  // masked rows may hold any bytes (NaN codes)
-        }
-        uint32_t vsc[2] = {0x3C003C00u, 0x3C003C00u};  // f16x2 scales (1.0) for tokens (2t,2t+1), (2t+8,2t+9)
-        if (p.v_scale != nullptr) {
-          float f[4];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            f[i] = 0.f;
-            const int bi = vt[i] / p.box_rows;
-            if (vt[i] < h.nvalid && h.blk[bi] >= 0) {
-              const int pos = h.tok0 + vt[i];
-              f[i] = __ldg(p.v_scale + (static_cast<int64_t>(h.blk[bi]) * p.block_size + pos % p.block_size) * p.num_kv_heads + h.kvh);
-            }
-          }
-          vsc[0] = pack_f16x2(f[0], f[1]);
-          vsc[1] = pack_f16x2(f[2], f[3]);
-        }
-        const uint32_t W[4][4] = {{vw[0].x, vw[0].y, vw[0].z, vw[0].w},
-                                  {vw[1].x, vw[1].y, vw[1].z, vw[1].w},
-                                  {vw[2].x, vw[2].y, vw[2].z, vw[2].w},
-                                  {vw[3].x, vw[3].y, vw[3].z, vw[3].w}};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          // 4x4 byte transpose: T[j] = dim (16g + 4i + j) of tokens (2t, 2t+1, 2t+8, 2t+9)
-          const uint32_t x0 = prmt(W[0][i], W[1][i], 0x5140);
-          const uint32_t x1 = prmt(W[0][i], W[1][i], 0x7362);
-          const uint32_t y0 = prmt(W[2][i], W[3][i], 0x5140);
-          const uint32_t y1 = prmt(W[2][i], W[3][i], 0x7362);
-          const uint32_t T0 = prmt(x0, y0, 0x5410), T1 = prmt(x0, y0, 0x7632);
-          const uint32_t T2 = prmt(x1, y1, 0x5410), T3 = prmt(x1, y1, 0x7632);
-          uint32_t a0[4] = {e4m3x2_to_f16x2(T0), e4m3x2_to_f16x2(T1), e4m3x2_to_f16x2(T0 >> 16),
-                            e4m3x2_to_f16x2(T1 >> 16)};
-          uint32_t a1[4] = {e4m3x2_to_f16x2(T2), e4m3x2_to_f16x2(T3), e4m3x2_to_f16x2(T2 >> 16),
-                            e4m3x2_to_f16x2(T3 >> 16)};
-          if (p.v_scale != nullptr) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const uint32_t sc = (j < 2) ? vsc[0] : vsc[1];
-              __half2 x = *reinterpret_cast<__half2*>(&a0[j]);
-              __half2 y = *reinterpret_cast<__half2*>(&a1[j]);
-              const __half2 s2 = *reinterpret_cast<const __half2*>(&sc);
-              x = __hmul2(x, s2);
-              y = __hmul2(y, s2);
-              a0[j] = *reinterpret_cast<uint32_t*>(&x);
-              a1[j] = *reinterpret_cast<uint32_t*>(&y);
-            }
-          }
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt) {
-            mma_f16_16816(o[2 * i][nt], a0, pb[nt][0], pb[nt][1]);
-            mma_f16_16816(o[2 * i + 1][nt], a1, pb[nt][0], pb[nt][1]);
-          }
-        }
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.empty[stage]);
-      if (++stage == STAGES) { stage = 0; phase ^= 1; }
-
-      if (h.flags & kLast) {
-        // ------------------------------------------------ merge the 4 warps' partial states
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            float l = l_run[nt][e];
-            l += __shfl_xor_sync(0xffffffffu, l, 4);
-            l += __shfl_xor_sync(0xffffffffu, l, 8);
-            l += __shfl_xor_sync(0xffffffffu, l, 16);
-            if (g == 0) {
-              sm.mrg_m[warp][8 * nt + 2 * t + e] = m_run[nt][e];
-              sm.mrg_l[warp][8 * nt + 2 * t + e] = l;
-            }
-          }
-#pragma unroll
-        for (int mt = 0; mt < 8; ++mt)
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              // m-tile mt = 2*ii + jh, row g (+8 if i >= 2) -> dim 16g + 4ii + 2jh + jl
-              // stored at k*8 + g (k = dim % 16, g = dim / 16): conflict-free for these writes
-              // and for the per-thread reads below
-              const int ii = mt >> 1, jh = mt & 1, jl = i >> 1;
-              const int kk = 4 * ii + 2 * jh + jl;
-              const int col = 8 * nt + 2 * t + (i & 1);
-              sm.mrg_o[warp][col][kk * 8 + g] = o[mt][nt][i];
-            }
-        named_barrier(1, kConsumerThreads);
-        const int d = tid;  // consumer thread = permuted dim slot; real dim below
-        const int dim_real = 16 * (d & 7) + (d >> 3);
-        const bool direct = h.nchunks == 1;
-        for (int col = 0; col < h.rows; ++col) {
-          float M = -INFINITY;
-#pragma unroll
-          for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, sm.mrg_m[w][col]);
-          const float Mu = M == -INFINITY ? 0.f : M;
-          float L = 0.f, O = 0.f;
-#pragma unroll
-          for (int w = 0; w < kConsumerWarps; ++w) {
-            const float wt = ex2(sm.mrg_m[w][col] - Mu);
-            L += wt * sm.mrg_l[w][col];
-            O += wt * sm.mrg_o[w][col][d];
-          }
-          if (direct) {
-            const int r = h.rg * ROWS + col;
-            const int j = r / G, hh = h.kvh * G + (r - j * G);
-            __nv_bfloat16 v = out_round(O / fmaxf(L, 1e-10f));
-            p.out[static_cast<int64_t>(h.qrow0 + j) * p.out_row_stride + hh * kHeadDim + dim_real] =
-                *reinterpret_cast<uint16_t*>(&v);
-          } else {
-            float* part = p.partials + (static_cast<int64_t>(h.item) * ROWS + col) * (kHeadDim + 2);
-            part[d] = O;
-            if (d == 0) {
-              part[kHeadDim] = M;
-              part[kHeadDim + 1] = L;
-            }
-          }
-        }
-        if (!direct) {
-          __threadfence();
-          named_barrier(1, kConsumerThreads);
-          int* ticket = p.tickets + (static_cast<int64_t>(h.seq) * p.num_kv_heads + h.kvh) * p.max_rowgroups + h.rg;
-          if (tid == 0) {
-            const int prev = atomicAdd(ticket, 1);
-            const int last = prev == h.nchunks - 1;
-            if (last) atomicExch(ticket, 0);
-            sm.scratch[0] = last;
-          }
-          named_barrier(1, kConsumerThreads);
-          if (sm.scratch[0]) {
-            __threadfence();
-            for (int col = 0; col < h.rows; ++col) {
-              float M = -INFINITY;
-              for (int c = 0; c < h.nchunks; ++c) {
-                const float* part = p.partials + (static_cast<int64_t>(h.pair_first + c) * ROWS + col) * (kHeadDim + 2);
-                M = fmaxf(M, __ldcg(part + kHeadDim));
-              }
-              const float Mu = M == -INFINITY ? 0.f : M;
-              float L = 0.f, O = 0.f;
-              for (int c = 0; c < h.nchunks; ++c) {
-                const float* part = p.partials + (static_cast<int64_t>(h.pair_first + c) * ROWS + col) * (kHeadDim + 2);
-                const float wt = ex2(__ldcg(part + kHeadDim) - Mu);
-                L += wt * __ldcg(part + kHeadDim + 1);
-                O += wt * __ldcg(part + d);
-              }
-              const int r = h.rg * ROWS + col;
-              const int j = r / G, hh = h.kvh * G + (r - j * G);
-              __nv_bfloat16 v = out_round(O / fmaxf(L, 1e-10f));
-              p.out[static_cast<int64_t>(h.qrow0 + j) * p.out_row_stride + hh * kHeadDim + dim_real] =
-                  *reinterpret_cast<uint16_t*>(&v);
-            }
-          }
-        }
-        // merge buffers are rewritten by the next item only after everyone read them
-        named_barrier(1, kConsumerThreads);
-      }
+    const int per_row = p.num_heads * kHeadDim / 8;  // uint4 per token row
+    for (int j = 0; j < nq; ++j) {
+      uint4* dst = reinterpret_cast<uint4*>(p.out + static_cast<int64_t>(qrow0 + j) * p.out_row_stride);
+      for (int i = tid; i < per_row; i += kThreads) dst[i] = make_uint4(0, 0, 0, 0);
     }
   }
 
-  // ---------------------------------------------------------------- last CTA out resets counters
+  if (fits && warp == kProducerWarp) {
+    // ============================================================ producer
+    // P: the item whose tiles are being issued; Pn: the next item, claimed and prefetching
+    Cursor<NT> P, Pn;
+    P.nth = 0;
+    P.next = 0;
+    {
+      int ids[2] = {0, 0};
+      if (lane == 0) {
+        ids[0] = atomicAdd(p.ctrl + 1, 1);
+        ids[1] = atomicAdd(p.ctrl + 1, 1);
+        Pn.next = atomicAdd(p.ctrl + 1, 1);
+      }
+      ids[0] = __shfl_sync(0xffffffffu, ids[0], 0);
+      ids[1] = __shfl_sync(0xffffffffu, ids[1], 0);
+      cursor_set<NT>(P, ids[0], p, prefix, info, total_items, CT, B);
+      cursor_set<NT>(Pn, ids[1], p, prefix, info, total_items, CT, B);
+    }
+    int stage = 0;
+    uint32_t phase = 0;
+    const int box_rows = p.box_rows;
+    while (true) {
+      if (P.item >= total_items) {
+        if (mbar_wait(&sm.kv_empty[stage], phase ^ 1, p.ctrl) && lane == 0) {
+          sm.hdr[stage].item = -1;
+          mbar_arrive(&sm.kv_full[stage]);
+        }
+        break;
+      }
+      const int slot = P.nth & 1;
+      if (P.t == P.t0) {
+        if (!mbar_wait(&sm.q_empty[slot], ((P.nth >> 1) & 1) ^ 1, p.ctrl)) break;
+        prepare_q<NT>(P, slot, p, sm, lane);
+        fence_proxy_async_smem();
+        mbar_arrive(&sm.q_full[slot]);
+      }
+      if (!mbar_wait(&sm.kv_empty[stage], phase ^ 1, p.ctrl)) break;
+      const int t = P.t;
+      const int nvalid = min(kTile, P.t1 - t);
+      const int nbox = (nvalid + box_rows - 1) / box_rows;
+      const int64_t bt_row = static_cast<int64_t>(P.b) * p.bt_stride;
+      int blks[kMaxBoxes], slots[kMaxBoxes];
+#pragma unroll
+      for (int j = 0; j < kMaxBoxes; ++j) {
+        blks[j] = -1;
+        slots[j] = 0;
+        if (j < nbox) {
+          const int pos = t + j * box_rows;
+          const int e = pos / p.block_size;
+          if (e < P.ebase || e >= P.ebase + 32) {
+            P.ebase = e;
+            const int idx = e + lane;
+            P.myent = idx < p.max_blocks ? __ldg(p.block_tables + bt_row + idx) : -1;
+          }
+          int blk = __shfl_sync(0xffffffffu, P.myent, e - P.ebase);
+          if (blk < 0 || blk >= p.num_blocks) blk = -1;
+          blks[j] = blk;
+          slots[j] = blk < 0 ? 0 : blk * p.block_size + (pos - e * p.block_size);
+        }
+      }
+      if (lane == 0) {
+        TileHeader& h = sm.hdr[stage];
+        h.item = P.item;
+        h.seq = P.b;
+        h.kvh = P.kvh;
+        h.rg = P.rg;
+        h.tok0 = t;
+        h.nvalid = nvalid;
+        h.flags = (t == P.t0 ? kFirst : 0) | (t + kTile >= P.t1 ? kLast : 0);
+        h.nchunks = P.nchunks;
+        h.pair_first = P.pair_first;
+        h.pair_stride = P.pair_stride;
+        h.qrow0 = P.qrow0;
+        h.rows = P.rows;
+        h.qslot = slot;
+        h.lim_base = P.lim_base;
+#pragma unroll
+        for (int j = 0; j < kMaxBoxes; ++j) {
+          h.blk[j] = blks[j];
+          h.slot0[j] = slots[j];
+        }
+        uint32_t bytes = 0;
+#pragma unroll
+        for (int j = 0; j < kMaxBoxes; ++j)
+          if (blks[j] >= 0) bytes += 2u * box_rows * kHeadDim;
+        mbar_arrive_expect_tx(&sm.kv_full[stage], bytes);
+      }
+      __syncwarp();
+      if (lane < 2) {  // lane 0 loads the K boxes, lane 1 the V boxes, side by side
+        const CUtensorMap* map = lane == 0 ? &tmk : &tmv;
+        uint8_t* dst = lane == 0 ? &sm.k[stage][0] : &sm.v[stage][0];
+#pragma unroll
+        for (int j = 0; j < kMaxBoxes; ++j)
+          if (blks[j] >= 0)
+            tma_load_2d(dst + j * box_rows * kHeadDim, map, &sm.kv_full[stage], P.kvh * kHeadDim, slots[j]);
+      }
+      __syncwarp();
+      if (++stage == kStages) { stage = 0; phase ^= 1; }
+      P.t += kTile;
+      if (P.t >= P.t1) {
+        const int nth = P.nth + 1;
+        const int nxt = __shfl_sync(0xffffffffu, Pn.next, 0);
+        P = Pn;
+        P.nth = nth;
+        if (lane == 0) Pn.next = atomicAdd(p.ctrl + 1, 1);
+        if (P.item < total_items) cursor_set<NT>(Pn, nxt, p, prefix, info, total_items, CT, B);
+        else Pn.item = total_items;
+      }
+    }
+  } else if (fits && warp == kMmaWarp) {
+    // ============================================================ MMA issuer (lane 0)
+    // tile j: S_j into S buffer j%2, then PV_{j-1} (or PV_j at once when j ends its item) into
+    // PV buffer (tile % 2); each PV is a fresh product (its first MMA does not accumulate)
+    if (lane == 0) {
+      const uint32_t idesc_s = tc::idesc_e4m3(128, N, false, false);
+      const uint32_t idesc_pv = tc::idesc_e4m3(128, 16, true, true);
+      int stage = 0, j = 0;
+      uint32_t phase = 0;
+      int qcount[2] = {0, 0};
+      bool pend = false;  // a tile whose PV is still to be issued
+      int pend_stage = 0;
+      auto issue_pv = [&](int st, int tile) -> bool {
+        const int b = tile & 1;
+        if (!mbar_wait(&sm.p_full[b], (tile >> 1) & 1, p.ctrl)) return false;
+        tc::fence_after_sync();
+        const uint32_t va = smem_u32(&sm.v[st][0]);
+#pragma unroll
+        for (int plane = 0; plane < NT; ++plane) {
+          const uint32_t pa = smem_u32(&sm.p2[b][plane][0]);
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks) {
+            const uint64_t ad = tc::smem_desc(va + ks * 32 * 128, 0, 1024, tc::kSw128);
+            const uint64_t bd = tc::smem_desc(pa + ks * 32 * 16, 128, 2048, tc::kSwNone);
+            tc::mma_f8(tmem + (2 + b) * N + 16 * plane, ad, bd, idesc_pv, ks > 0 ? 1u : 0u);
+          }
+        }
+        tc::commit(&sm.kv_empty[st]);
+        tc::commit(&sm.pv_done[b]);
+        return true;
+      };
+      while (true) {
+        if (!mbar_wait(&sm.kv_full[stage], phase, p.ctrl)) break;
+        const TileHeader& h = sm.hdr[stage];
+        if (h.item < 0) break;
+        const int first = h.flags & kFirst;
+        const int last = h.flags & kLast;
+        const int slot = h.qslot;
+        if (first) {
+          if (!mbar_wait(&sm.q_full[slot], qcount[slot] & 1, p.ctrl)) break;
+          qcount[slot]++;
+        }
+        const int sb = j & 1;
+        if (!mbar_wait(&sm.s_empty[sb], ((j >> 1) & 1) ^ 1, p.ctrl)) break;
+        tc::fence_after_sync();
+        const uint32_t ka = smem_u32(&sm.k[stage][0]);
+        const uint32_t qa = smem_u32(&sm.q2[slot][0]);
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks) {
+          const uint64_t ad = tc::smem_desc(ka + ks * 32, 16, 1024, tc::kSw128);
+          const uint64_t bd = tc::smem_desc(qa + ks * 32, 16, 1024, tc::kSw128);
+          tc::mma_f8(tmem + sb * N, ad, bd, idesc_s, ks > 0 ? 1u : 0u);
+        }
+        tc::commit(&sm.s_full[sb]);
+        if (pend && !issue_pv(pend_stage, j - 1)) break;
+        pend = true;
+        pend_stage = stage;
+        if (last) {  // the item's epilogue waits on this PV: issue it now, not after the next S
+          if (!issue_pv(stage, j)) break;
+          pend = false;
+        }
+        ++j;
+        if (++stage == kStages) { stage = 0; phase ^= 1; }
+      }
+      if (pend) issue_pv(pend_stage, j - 1);
+    }
+    __syncwarp();
+  } else if (fits && warp < 4) {
+    // ============================================================ softmax warps 0-3
+    // thread r: token row r of S^T and dim row r of the PV products.  O lives in registers:
+    // at tile j the product PV_{j-2} (done by then, its P buffer is needed again) is folded in,
+    // rescaled from its tile's reference max; the item's last two products are folded in the
+    // epilogue.  m_hist keeps the reference max of the last two tiles.
+    const int r = tid;
+    const uint32_t lane_base = static_cast<uint32_t>(32 * warp) << 16;
+    const bool kscaled = p.k_scale != nullptr;
+    const bool vscaled = p.v_scale != nullptr;
+    const int box_shift = 31 - __clz(p.box_rows);
+    float cs[R], m_run[R], l_part[R], o_acc[R], m_o[R], m_hist[2][R];
+    int lim[R];
+    int stage = 0, j = 0, sync_uses = 0, item_first_tile = 0;
+    uint32_t phase = 0;
+    int qcount[2] = {0, 0};
+    auto sync = [&]() -> bool {
+      mbar_arrive(&sm.sync128);
+      return mbar_wait(&sm.sync128, (sync_uses++) & 1, p.ctrl);
+    };
+    // fold the finished product of tile t (buffer t % 2) into o_acc
+    auto fold = [&](int t) {
+      const int b = t & 1;
+      float pv[N];
+#pragma unroll
+      for (int c = 0; c < N; c += 16) {
+        float v16[16];
+        tc::ld16(tmem + lane_base + (2 + b) * N + c, v16);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) pv[c + i] = v16[i];
+      }
+      tc::wait_ld();
+#pragma unroll
+      for (int q = 0; q < R; ++q) {
+        const float mr = b ? m_hist[1][q] : m_hist[0][q];
+        const float f = t == item_first_tile ? 0.f : ex2(m_o[q] - mr);
+        o_acc[q] = o_acc[q] * f + (pv[q] + pv[R + q]);
+        m_o[q] = mr;
+      }
+    };
+    auto wait_pv = [&](int t) -> bool {
+      const int b = t & 1;
+      if (!mbar_wait(&sm.pv_done[b], (t >> 1) & 1, p.ctrl)) return false;
+      tc::fence_after_sync();
+      return true;
+    };
+    while (true) {
+      if (!mbar_wait(&sm.kv_full[stage], phase, p.ctrl)) break;
+      const TileHeader& h = sm.hdr[stage];
+      const int item = h.item;
+      if (item < 0) break;
+      // everything this tile needs from its header, read now: once P is handed over, the PV
+      // completes, the stage is released and the producer rewrites the header
+      const int flags = h.flags, nvalid = h.nvalid, tok0 = h.tok0, slot = h.qslot;
+      const int rows = h.rows, nchunks = h.nchunks, rg = h.rg, seq = h.seq, kvh = h.kvh;
+      const int qrow0 = h.qrow0, pair_first = h.pair_first, pair_stride = h.pair_stride;
+      const int lim_base = h.lim_base;
+      const int box = r >> box_shift;
+      const int bb = h.blk[box];
+      const int slot0 = h.slot0[box];
+      const bool valid = r < nvalid && bb >= 0;
+      if (flags & kFirst) {
+        if (!mbar_wait(&sm.q_full[slot], qcount[slot] & 1, p.ctrl)) break;
+        qcount[slot]++;
+        const int row_off = (rg * R) % G;
+        item_first_tile = j;
+#pragma unroll
+        for (int q = 0; q < R; ++q) {
+          cs[q] = sm.qscale[slot][q];
+          lim[q] = q < rows ? (p.spec_mode ? lim_base + (q + row_off) / G : INT_MAX) : -1;
+          m_run[q] = -INFINITY;
+          l_part[q] = 0.f;
+          o_acc[q] = 0.f;
+          m_o[q] = 0.f;
+        }
+      }
+      float ks = 1.f, lv = 0.f;
+      if ((kscaled || vscaled) && valid) {
+        const int64_t idx = (static_cast<int64_t>(slot0) + (r & (p.box_rows - 1))) * p.num_kv_heads + kvh;
+        if (kscaled) ks = __ldg(p.k_scale + idx);
+        if (vscaled) lv = lg2(__ldg(p.v_scale + idx));
+      }
+      // ---------------------------------------------------- scores of this token row
+      const int sb = j & 1;
+      if (!mbar_wait(&sm.s_full[sb], (j >> 1) & 1, p.ctrl)) break;
+      tc::fence_after_sync();
+      float x[N];
+#pragma unroll
+      for (int c = 0; c < N; c += 16) {
+        float v16[16];
+        tc::ld16(tmem + lane_base + sb * N + c, v16);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) x[c + i] = v16[i];
+      }
+      tc::wait_ld();
+      tc::fence_before_sync();
+      mbar_arrive(&sm.s_empty[sb]);
+      const int pos = tok0 + r;
+      float xx[R], xo[R];
+#pragma unroll
+      for (int q = 0; q < R; ++q) {
+        float s = (x[q] + x[R + q]) * cs[q] * ks;
+        if (!(valid && pos <= lim[q])) s = -INFINITY;
+        xx[q] = s;
+        xo[q] = s + lv;
+        const int wm = __reduce_max_sync(0xffffffffu, f2ord(xo[q]));
+        if (lane == 0) sm.red[sb][warp][q] = ord2f(wm);
+      }
+      if (!sync()) break;
+      uint32_t phi[R / 4], plo[R / 4];
+      float m_use_t[R];
+#pragma unroll
+      for (int q = 0; q < R; ++q) {
+        const float tmax = fmaxf(fmaxf(sm.red[sb][0][q], sm.red[sb][1][q]),
+                                 fmaxf(sm.red[sb][2][q], sm.red[sb][3][q]));
+        const float m_new = fmaxf(m_run[q], tmax);
+        const float m_use = m_new == -INFINITY ? 0.f : m_new;
+        const float alpha = ex2(m_run[q] - m_use);
+        m_run[q] = m_new;
+        m_use_t[q] = m_use;
+        const float po = ex2(xo[q] - m_use);
+        l_part[q] = l_part[q] * alpha + 256.f * (vscaled ? ex2(xx[q] - m_use) : po);
+        xo[q] = 256.f * po;  // P is quantised as 256 p (l carries the same factor)
+      }
+#pragma unroll
+      for (int w = 0; w < R / 4; ++w) {
+        const uint32_t a = pack_f16x2(xo[4 * w], xo[4 * w + 1]);
+        const uint32_t b = pack_f16x2(xo[4 * w + 2], xo[4 * w + 3]);
+        uint32_t ah, al, bh, bl;
+        split_f16x2_e4m3(a, ah, al);
+        split_f16x2_e4m3(b, bh, bl);
+        phi[w] = ah | (bh << 16);
+        plo[w] = al | (bl << 16);
+      }
+      // P buffer sb was last read by PV_{j-2}: wait for it, and fold it if it is this item's
+      if (j >= 2) {
+        if (!wait_pv(j - 2)) break;
+        if (j - 2 >= item_first_tile) fold(j - 2);
+      }
+#pragma unroll
+      for (int q = 0; q < R; ++q) {
+        if (sb) m_hist[1][q] = m_use_t[q];
+        else m_hist[0][q] = m_use_t[q];
+      }
+      // P^T row r: R == 8: [hi 0..7 | lo 0..7]; R == 16: plane 0 = hi 0..15, plane 1 = lo 0..15
+      if (R == 8) {
+        *reinterpret_cast<uint4*>(&sm.p2[sb][0][r * 16]) = make_uint4(phi[0], phi[1], plo[0], plo[1]);
+      } else {
+        *reinterpret_cast<uint4*>(&sm.p2[sb][0][r * 16]) =
+            make_uint4(phi[0], phi[1], phi[R / 4 - 2], phi[R / 4 - 1]);
+        *reinterpret_cast<uint4*>(&sm.p2[sb][NT - 1][r * 16]) =
+            make_uint4(plo[0], plo[1], plo[R / 4 - 2], plo[R / 4 - 1]);
+      }
+      if (!valid) {  // masked rows may hold any bytes (NaN codes): zero V's row
+        uint4* vrow = reinterpret_cast<uint4*>(&sm.v[stage][r * 128]);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) vrow[i] = make_uint4(0, 0, 0, 0);
+      }
+      fence_proxy_async_smem();
+      tc::fence_before_sync();
+      mbar_arrive(&sm.p_full[sb]);
+
+      if (flags & kLast) {
+        // ------------------------------------------------ epilogue of the item
+        if (j - 1 >= item_first_tile) {
+          if (!wait_pv(j - 1)) break;
+          fold(j - 1);
+        }
+        if (!wait_pv(j)) break;
+        fold(j);
+        tc::fence_before_sync();
+#pragma unroll
+        for (int q = 0; q < R; ++q) {
+          float l = l_part[q];
+#pragma unroll
+          for (int off = 16; off > 0; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
+          if (lane == 0) sm.redl[warp][q] = l;
+        }
+        if (!sync()) break;
+        float lsum[R];
+#pragma unroll
+        for (int q = 0; q < R; ++q)
+          lsum[q] = sm.redl[0][q] + sm.redl[1][q] + sm.redl[2][q] + sm.redl[3][q];
+        const int d = r;  // output dim
+        if (nchunks == 1) {
+#pragma unroll
+          for (int q = 0; q < R; ++q) {
+            if (q >= rows) break;
+            const int rr = rg * R + q;
+            const int jj = rr / G, hh = kvh * G + (rr - jj * G);
+            __nv_bfloat16 v = out_round(o_acc[q] / fmaxf(lsum[q], 1e-10f));
+            p.out[static_cast<int64_t>(qrow0 + jj) * p.out_row_stride + hh * kHeadDim + d] =
+                *reinterpret_cast<uint16_t*>(&v);
+          }
+        } else {
+#pragma unroll
+          for (int q = 0; q < R; ++q) {
+            if (q >= rows) break;
+            float* part = p.partials + (static_cast<int64_t>(item) * R + q) * (kHeadDim + 4);
+            part[d] = o_acc[q];
+            if (d == 0) {
+              // a chunk whose rows saw no key position carries no weight in the combine
+              part[kHeadDim] = lsum[q] > 0.f ? m_o[q] : -INFINITY;
+              part[kHeadDim + 1] = lsum[q];
+            }
+          }
+        }
+        mbar_arrive(&sm.q_empty[slot]);
+      }
+      ++j;
+      if (++stage == kStages) { stage = 0; phase ^= 1; }
+    }
+  }
+
+  // ---------------------------------------------------------------- teardown
+  tc::fence_before_sync();
   __syncthreads();
+  tc::fence_after_sync();
+  if (warp == kMmaWarp) tc::tmem_dealloc(tmem, kTmemCols);
   if (tid == 0) {
     __threadfence();
     const int done = atomicAdd(p.ctrl + 2, 1);
@@ -659,51 +804,138 @@ __global__ void __launch_bounds__(kDecodeThreads, NT == 1 ? 2 : 2)
   }
 }
 
+// Combines the split-KV partials of every (sequence, kv head, row group) with more than one
+// chunk, using the plan the decode kernel published.  One CTA per pair (grid-strided); thread =
+// output dim.  Partial rows hold O (unnormalised, 128 floats), then the running max (log2 units)
+// and the row sum.
 template <int NT>
-size_t decode_smem_bytes() {
-  return sizeof(DecodeSmem<NT>) + 1024;  // + alignment slack
+__global__ void __launch_bounds__(kHeadDim)
+    combine_kernel(const DecodeParams p) {
+  constexpr int R = 8 * NT;
+  const int G = p.group;
+  const int CT = p.plan[0];
+  const int64_t npairs = static_cast<int64_t>(p.num_seqs) * p.num_kv_heads * p.max_rowgroups;
+  const int d = threadIdx.x;
+  for (int64_t pi = blockIdx.x; pi < npairs; pi += gridDim.x) {
+    const int b = static_cast<int>(pi / (p.num_kv_heads * p.max_rowgroups));
+    const int rem = static_cast<int>(pi - static_cast<int64_t>(b) * p.num_kv_heads * p.max_rowgroups);
+    const int kvh = rem / p.max_rowgroups, rg = rem - kvh * p.max_rowgroups;
+    int nq;
+    const int L = seq_len_clamped(p, b, &nq);
+    if (L <= 0) continue;
+    const int nrg = (nq * G + R - 1) / R;
+    const int nchunks = (L + CT - 1) / CT;
+    if (rg >= nrg || nchunks <= 1) continue;
+    const int qrow0 = p.spec_mode ? __ldg(p.cu_q + b) : b;
+    const int rows = min(R, nq * G - rg * R);
+    const int64_t first = p.plan[2 + b] + kvh * nrg + rg;
+    const int64_t stride = static_cast<int64_t>(p.num_kv_heads) * nrg;
+    for (int q = 0; q < rows; ++q) {
+      float M = -INFINITY;
+      for (int c = 0; c < nchunks; ++c)
+        M = fmaxf(M, p.partials[((first + c * stride) * R + q) * (kHeadDim + 4) + kHeadDim]);
+      const float Mu = M == -INFINITY ? 0.f : M;
+      float L2 = 0.f, O = 0.f;
+#pragma unroll 4
+      for (int c = 0; c < nchunks; ++c) {
+        const float* part = p.partials + ((first + c * stride) * R + q) * (kHeadDim + 4);
+        const float wt = ex2(part[kHeadDim] - Mu);
+        L2 += wt * part[kHeadDim + 1];
+        O += wt * part[d];
+      }
+      const int rr = rg * R + q;
+      const int jj = rr / G, hh = kvh * G + (rr - jj * G);
+      __nv_bfloat16 v = out_round(O / fmaxf(L2, 1e-10f));
+      p.out[static_cast<int64_t>(qrow0 + jj) * p.out_row_stride + hh * kHeadDim + d] =
+          *reinterpret_cast<uint16_t*>(&v);
+    }
+  }
 }
 
-template <int NT>
-int decode_grid_impl() {
+int sm_count() {
   static int cached[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 64 && cached[dev]) return cached[dev];
-  int sms = 0, occ = 0;
+  if (dev >= 0 && dev < 64 && cached[dev]) return cached[dev];
+  int sms = 0;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const size_t smem = decode_smem_bytes<NT>();
-  cudaFuncSetAttribute(decode_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                       static_cast<int>(smem));
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_kernel<NT>, kDecodeThreads, smem);
-  if (occ < 1) occ = 1;
-  const int grid = sms * occ;
-  if (dev < 64) cached[dev] = grid;
-  return grid;
+  if (sms < 1) sms = 1;
+  if (dev >= 0 && dev < 64) cached[dev] = sms;
+  return sms;
+}
+
+template <int NT>
+size_t decode_smem_bytes(int num_seqs) {
+  // + alignment slack, + the per-launch plan arrays (prefix[B + 1], info[B])
+  return sizeof(DecodeSmem<NT>) + 1024 + static_cast<size_t>(2 * num_seqs + 1) * sizeof(int);
+}
+
+// Persistent grid for this launch: as many CTAs as fit on every SM (at most kMaxCtasPerSm; tensor
+// memory per CTA is at most 128 columns, so it never limits).
+template <int NT>
+int decode_grid_for(int num_seqs) {
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    cudaFuncSetAttribute(decode_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(decode_smem_bytes<NT>(kMaxSeqs)));
+    // all of the unified L1/shared storage as shared memory: two CTAs' rings must fit
+    cudaFuncSetAttribute(decode_kernel<NT>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    configured[dev] = true;
+  }
+  // The occupancy calculator reports 1 for every kernel that allocates tensor memory, so the
+  // CTAs per SM are counted from the resources themselves: shared memory (with the per-block
+  // reservation) and registers.  Tensor memory (at most 128 of 512 columns per CTA) never limits.
+  // Were fewer CTAs resident, the extra ones would find the work counter exhausted and leave.
+  int smem_sm = 0, resv = 0;
+  cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+  cudaDeviceGetAttribute(&resv, cudaDevAttrReservedSharedMemoryPerBlock, dev);
+  cudaFuncAttributes fa;
+  cudaFuncGetAttributes(&fa, decode_kernel<NT>);
+  const int per_cta_smem = static_cast<int>(decode_smem_bytes<NT>(num_seqs)) + resv;
+  int occ = per_cta_smem > 0 ? smem_sm / per_cta_smem : 1;
+  const int by_regs = fa.numRegs > 0 ? 65536 / (fa.numRegs * kThreads) : 1;
+  occ = occ < by_regs ? occ : by_regs;
+  occ = occ < 1 ? 1 : (occ > kMaxCtasPerSm ? kMaxCtasPerSm : occ);
+  return sm_count() * occ;
 }
 
 }  // namespace
 
-int decode_grid(int nt) { return nt == 1 ? decode_grid_impl<1>() : decode_grid_impl<2>(); }
+int decode_grid(int nt) {
+  (void)nt;
+  return sm_count() * kMaxCtasPerSm;  // upper bound of any launch's grid (workspace sizing)
+}
+
+int decode_launch_grid(int nt, int num_seqs) {
+  return nt == 1 ? decode_grid_for<1>(num_seqs) : decode_grid_for<2>(num_seqs);
+}
+
+int64_t decode_max_items(int64_t pairs, int grid) {
+  return static_cast<int64_t>(kItemsPerCta) * grid + pairs;
+}
 
 int64_t decode_workspace_bytes(int num_seqs, int num_kv_heads, int max_rowgroups, int rows,
                                int grid) {
   const int64_t pairs = static_cast<int64_t>(num_seqs) * num_kv_heads * max_rowgroups;
-  const int64_t max_items = 32LL * grid + pairs;
-  int64_t bytes = kCtrlInts * 4;
-  bytes += (pairs * 4 + 255) / 256 * 256;
-  bytes += max_items * rows * (kHeadDim + 2) * 4;
+  int64_t bytes = kCtrlInts * 4 + kPlanInts * 4;
+  bytes += decode_max_items(pairs, grid) * rows * (kHeadDim + 4) * 4;
   return bytes;
 }
 
 cudaError_t launch_decode(const DecodeParams& p, int nt, const CUtensorMap& tmk,
                           const CUtensorMap& tmv, cudaStream_t stream) {
+  const int64_t pairs = static_cast<int64_t>(p.num_seqs) * p.num_kv_heads * p.max_rowgroups;
+  const int cgrid = static_cast<int>(pairs < 8LL * sm_count() ? pairs : 8LL * sm_count());
   if (nt == 1) {
-    const int grid = decode_grid_impl<1>();
-    decode_kernel<1><<<grid, kDecodeThreads, decode_smem_bytes<1>(), stream>>>(tmk, tmv, p);
+    const int grid = decode_grid_for<1>(p.num_seqs);
+    decode_kernel<1><<<grid, kThreads, decode_smem_bytes<1>(p.num_seqs), stream>>>(tmk, tmv, p);
+    if (cgrid > 0) combine_kernel<1><<<cgrid, kHeadDim, 0, stream>>>(p);
   } else {
-    const int grid = decode_grid_impl<2>();
-    decode_kernel<2><<<grid, kDecodeThreads, decode_smem_bytes<2>(), stream>>>(tmk, tmv, p);
+    const int grid = decode_grid_for<2>(p.num_seqs);
+    decode_kernel<2><<<grid, kThreads, decode_smem_bytes<2>(p.num_seqs), stream>>>(tmk, tmv, p);
+    if (cgrid > 0) combine_kernel<2><<<cgrid, kHeadDim, 0, stream>>>(p);
   }
   return cudaGetLastError();
 }

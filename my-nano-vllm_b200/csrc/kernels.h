@@ -30,6 +30,10 @@ cudaError_t launch_store(const StoreParams& p, cudaStream_t stream);
 //   [0] sticky device error code, [1] next work item, [2] CTAs finished.
 constexpr int kCtrlInts = 64;  // 256 bytes
 constexpr int kMaxSeqs = 2048;  // per launch (plan lives in shared memory)
+// Plan published by the decode kernel for its combine kernel, right after the control block:
+// [0] chunk size, [1] item count, [2 + b] item prefix of sequence b (b = 0 .. num_seqs).
+constexpr int kPlanInts = kMaxSeqs + 8;
+constexpr int kDecodeTile = 128;  // key positions per decode pipeline stage
 
 struct DecodeParams {
   uint16_t* out;  // bf16
@@ -49,7 +53,7 @@ struct DecodeParams {
   int num_kv_heads;
   int group;  // num_heads / num_kv_heads
   int block_size;
-  int box_rows;  // TMA box height: 64, 32 or 16 (divides block_size and 64)
+  int box_rows;  // TMA box height: 128, 64, 32 or 16 (divides block_size and kDecodeTile)
   int64_t num_blocks;
   int spec_mode;
   int spec_q_max;  // spec mode: sequences with 1 <= nq <= spec_q_max are handled here
@@ -57,7 +61,7 @@ struct DecodeParams {
   int min_chunk;  // minimum tokens per work item (multiple of 64)
   float scale_log2;  // softmax_scale * log2(e)
   int* ctrl;
-  int* tickets;  // [num_seqs * num_kv_heads * max_rowgroups], zero between launches
+  int* plan;      // kPlanInts ints, written by the decode kernel, read by its combine kernel
   float* partials;
   int max_items;
 };
@@ -66,8 +70,11 @@ struct DecodeParams {
 inline int decode_rows(int nt) { return 8 * nt; }
 int64_t decode_workspace_bytes(int num_seqs, int num_kv_heads, int max_rowgroups, int rows,
                                int grid);
+int64_t decode_max_items(int64_t pairs, int grid);
 // Grid (persistent CTAs) the decode engine uses on the current device for the given width.
 int decode_grid(int nt);
+// Grid an actual launch uses (persistent CTAs resident at once) for this batch size.
+int decode_launch_grid(int nt, int num_seqs);
 cudaError_t launch_decode(const DecodeParams& p, int nt, const CUtensorMap& tmk,
                           const CUtensorMap& tmv, cudaStream_t stream);
 

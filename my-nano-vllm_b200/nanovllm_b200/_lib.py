@@ -37,6 +37,8 @@ def _load() -> ctypes.CDLL:
     lib.fp8attn_store_kvcache.restype = i32
     lib.fp8attn_store_kvcache.argtypes = [vp, i64, vp, i64, vp, vp, vp, vp, vp, i64, i32, i32,
                                           i64, i32, vp]
+    lib.fp8attn_decode_ctas.restype = i32
+    lib.fp8attn_decode_ctas.argtypes = [i32, i32, i32, i32]
     lib.fp8attn_workspace_bytes.restype = i64
     lib.fp8attn_workspace_bytes.argtypes = [i32, i32, i32, i32]
     lib.fp8attn_decode.restype = i32

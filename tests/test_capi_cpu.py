@@ -29,10 +29,10 @@ def test_library_has_no_hard_cuda_driver_dependency():
 
 def test_version_and_min_chunk_knob():
     assert _lib.lib.fp8attn_version() >= 100
-    prev = _lib.lib.fp8attn_set_decode_min_chunk(128)
-    assert prev == 256
-    assert _lib.lib.fp8attn_set_decode_min_chunk(100) == -1      # not a multiple of 64
-    assert _lib.lib.fp8attn_set_decode_min_chunk(prev) == 128
+    prev = _lib.lib.fp8attn_set_decode_min_chunk(256)
+    assert prev == 128
+    assert _lib.lib.fp8attn_set_decode_min_chunk(192) == -1      # not a multiple of 128
+    assert _lib.lib.fp8attn_set_decode_min_chunk(prev) == 256
 
 
 def _decode_call(**over):

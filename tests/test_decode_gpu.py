@@ -51,7 +51,7 @@ def test_decode_config1():
     _no_device_error()
 
 
-@pytest.mark.parametrize("min_chunk", [64, 256])
+@pytest.mark.parametrize("min_chunk", [128, 512])
 @pytest.mark.parametrize("bs,hq,kvh", [(16, 4, 4), (32, 8, 2), (64, 16, 1), (256, 32, 8),
                                        (48, 8, 8), (80, 32, 2), (256, 64, 8)])
 def test_decode_edge_cases(bs, hq, kvh, min_chunk):
