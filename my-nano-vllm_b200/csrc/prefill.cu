@@ -1,11 +1,588 @@
-// Varlen causal prefill engine (placeholder until the tcgen05 engine lands).
+// Varlen causal prefill / chunked-prefill engine on the sm_100a tensor cores.
+//
+// Replaces fp8_paged_attention_prefill_kernel (nanovllm/kernels/fp8_attention.py:209-312) for
+// query sequences too long for the split-KV decode engine (which the prefill entry point uses for
+// speculative-verify sized sequences).  Same contract: sequence s has query rows
+// cu_q[s]..cu_q[s+1] and nk = cu_k[s+1] - cu_k[s] key positions; query row i attends key
+// positions j <= i + (nk - nq) (:267-268, :297-298); K/V come from the paged cache through
+// block_tables (first max_num_blocks columns visited, :281) or from contiguous [Tk, KVH, 128]
+// rows starting at cu_k[s] (:254-263); rows with no visible key give 0 (:311).
+//
+// One CTA = one (q tile of 128 rows, q head, sequence).  Six warps:
+//   warps 0-3 softmax, thread = query row: converts its q row to e4m3 hi + lo (power-of-two row
+//             scale) at the start, then per key tile reads its row of S from tensor memory twice
+//             (max, then p), quantises P = 16 * 2^(s - m) as e4m3 hi + lo, and finally divides
+//             the tensor-memory O row by its sum.  O is rescaled only when a row maximum grows by
+//             more than 2^4 (P stays <= 256, inside e4m3's range);
+//   warp 4    TMA producer: 128-token K and V tiles (128-byte rows, 128B swizzle) into a 3-deep
+//             ring; key tiles past the causal limit of the q tile's last row are never loaded;
+//   warp 5    MMA issuer (one thread):
+//               S  = [Qhi; Qlo] . K^T   two accumulating kind::f8f6f4 chains, M = N = 128
+//               O += [Phi; Plo] . V     V is read MN-major straight from its TMA tile
+//             S double-buffered in tensor memory, P double-buffered in shared memory.
+#include <climits>
+
 #include "common.cuh"
 #include "kernels.h"
+#include "tcgen05.cuh"
 
 namespace fp8attn {
-cudaError_t launch_prefill(const PrefillParams& p, cudaStream_t stream) {
-  (void)p;
-  (void)stream;
-  return cudaErrorNotSupported;
+namespace {
+
+constexpr int kBM = 128;      // query rows per CTA
+constexpr int kBN = 128;      // key positions per tile
+constexpr int kStages = 3;
+constexpr int kThreads = 6 * 32;
+constexpr int kProducerWarp = 4;
+constexpr int kMmaWarp = 5;
+constexpr int kMaxBoxes = kBN / 16;
+constexpr float kRescaleLog2 = 4.f;  // lazy rescale threshold (log2 units)
+constexpr float kPScale = 16.f;      // P is quantised as 16 * 2^(s - m_ref) <= 16 * 2^4
+
+struct PrefillTile {
+  int j0;                     // first key position of the tile
+  int blk[kMaxBoxes];         // paged: physical block of each box (-1: masked)
+};
+
+struct __align__(1024) PrefillSmem {
+  uint8_t qhi[kBM * 128];               // A operand of S: K-major SW128
+  uint8_t qlo[kBM * 128];
+  uint8_t k[kStages][kBN * 128];
+  uint8_t v[kStages][kBN * 128];
+  uint8_t phi[2][kBM * 128];            // A operand of PV, by tile parity
+  uint8_t plo[2][kBM * 128];
+  PrefillTile tile[kStages];
+  uint64_t kv_full[kStages];
+  uint64_t kv_empty[kStages];
+  uint64_t q_full;
+  uint64_t s_full[2];
+  uint64_t s_empty[2];
+  uint64_t p_full[2];
+  uint64_t pv_done[2];
+  uint32_t tmem_base;
+};
+
+// Tensor-memory columns: S buffers at [0, 128) and [128, 256), O at [256, 384).
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColS0 = 0, kColO = 256;
+
+struct SeqInfo {
+  int q_begin, nq, k_begin, nk;
+  int vis;        // key positions that can be read (paged: capped by the table width)
+  int ntiles;     // key tiles this q tile needs
+};
+
+__device__ __forceinline__ bool seq_info(const PrefillParams& p, int s, int qt, SeqInfo& si) {
+  si.q_begin = __ldg(p.cu_q + s);
+  si.nq = __ldg(p.cu_q + s + 1) - si.q_begin;
+  si.k_begin = __ldg(p.cu_k + s);
+  si.nk = __ldg(p.cu_k + s + 1) - si.k_begin;
+  if (si.nq < p.min_q || qt * kBM >= si.nq) return false;
+  si.vis = si.nk;
+  if (p.block_tables != nullptr) si.vis = min(si.vis, p.max_blocks * p.block_size);
+  if (si.vis < 0) si.vis = 0;
+  const int q_last = min(si.nq, qt * kBM + kBM) - 1;
+  const int lim = q_last + (si.nk - si.nq);  // largest key position any row of the tile sees
+  const int kv_end = min(si.vis, lim + 1);
+  si.ntiles = kv_end > 0 ? (kv_end + kBN - 1) / kBN : 0;
+  return true;
 }
+
+// Power-of-two scale so that |x| / s < 256 for the largest element (same rule as the decode
+// engine's query rows); returns 1/s and writes s.
+__device__ __forceinline__ float pow2_inv_scale(float amax, float* s) {
+  int ex = 0;
+  if (amax > 0.f && amax < INFINITY) ex = ((__float_as_uint(amax) >> 23) & 0xFF) - 127;
+  ex = max(-100, min(ex, 120));
+  *s = __uint_as_float(static_cast<uint32_t>(127 - 7 + ex) << 23);
+  return __uint_as_float(static_cast<uint32_t>(127 + 7 - ex) << 23);
+}
+
+// 16 floats -> e4m3 hi (16 bytes) and lo (16 bytes) such that x ~= hi + lo.
+__device__ __forceinline__ void split16(const float* x, uint4& hi, uint4& lo) {
+  uint32_t h[4], l[4];
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+    const float x0 = x[4 * w], x1 = x[4 * w + 1], x2 = x[4 * w + 2], x3 = x[4 * w + 3];
+    const uint32_t h01 = f32x2_to_e4m3x2(x0, x1), h23 = f32x2_to_e4m3x2(x2, x3);
+    const uint32_t r01 = e4m3x2_to_f16x2(h01), r23 = e4m3x2_to_f16x2(h23);
+    const __half2 b01 = *reinterpret_cast<const __half2*>(&r01);
+    const __half2 b23 = *reinterpret_cast<const __half2*>(&r23);
+    const uint32_t l01 = f32x2_to_e4m3x2(x0 - __low2float(b01), x1 - __high2float(b01));
+    const uint32_t l23 = f32x2_to_e4m3x2(x2 - __low2float(b23), x3 - __high2float(b23));
+    h[w] = h01 | (h23 << 16);
+    l[w] = l01 | (l23 << 16);
+  }
+  hi = make_uint4(h[0], h[1], h[2], h[3]);
+  lo = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
+// 32x32b.x32: thread reads 32 consecutive columns of its lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  float a[16], b[16];
+  tc::ld16(taddr, a);
+  tc::ld16(taddr + 16, b);
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    v[i] = a[i];
+    v[16 + i] = b[i];
+  }
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    prefill_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
+                   const PrefillParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  PrefillSmem& sm = *reinterpret_cast<PrefillSmem*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // heavy tiles first: later q tiles see more keys
+  const int qt = static_cast<int>(gridDim.x) - 1 - static_cast<int>(blockIdx.x);
+  const int h = blockIdx.y, s = blockIdx.z;
+  SeqInfo si;
+  if (!seq_info(p, s, qt, si)) return;  // uniform across the CTA
+  const int G = p.group;
+  const int kvh = h / G;
+  const int q0 = qt * kBM;
+  const int rows = min(kBM, si.nq - q0);
+
+  if (tid == 0) {
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&sm.kv_full[i], 1);
+      mbar_init(&sm.kv_empty[i], 1);
+    }
+    mbar_init(&sm.q_full, 128);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sm.s_full[i], 1);
+      mbar_init(&sm.s_empty[i], 128);
+      mbar_init(&sm.p_full[i], 128);
+      mbar_init(&sm.pv_done[i], 1);
+    }
+    fence_mbar_init();
+  }
+  if (warp == kProducerWarp && lane == 0) {
+    prefetch_tensormap(&tmk);
+    prefetch_tensormap(&tmv);
+  }
+  if (warp == kMmaWarp) {
+    tc::tmem_alloc(&sm.tmem_base, kTmemCols);
+    tc::tmem_relinquish();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = sm.tmem_base;
+  const int ntiles = si.ntiles;
+
+  if (warp == kProducerWarp) {
+    // ============================================================ TMA producer
+    const bool paged = p.block_tables != nullptr;
+    const int bs = p.block_size;
+    const int box_rows = paged ? (bs % 128 == 0 ? 128 : bs % 64 == 0 ? 64 : bs % 32 == 0 ? 32 : 16)
+                               : kBN;
+    const int nbox = kBN / box_rows;
+    const int64_t bt_row = static_cast<int64_t>(s) * p.bt_stride;
+    int ebase = INT_MIN / 2, myent = -1;
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int j = 0; j < ntiles; ++j) {
+      const int j0 = j * kBN;
+      int blks[kMaxBoxes];
+      if (paged) {
+#pragma unroll
+        for (int b = 0; b < kMaxBoxes; ++b) {
+          blks[b] = -1;
+          if (b < nbox) {
+            const int pos = j0 + b * box_rows;
+            const int e = pos / bs;
+            if (e < ebase || e >= ebase + 32) {
+              ebase = e;
+              const int idx = e + lane;
+              myent = idx < p.max_blocks ? ldg_keep(p.block_tables + bt_row + idx) : -1;
+            }
+            int blk = __shfl_sync(0xffffffffu, myent, e - ebase);
+            if (blk < 0 || blk >= p.num_blocks || pos >= si.vis) blk = -1;
+            blks[b] = blk;
+          }
+        }
+      }
+      if (!mbar_wait(&sm.kv_empty[stage], phase ^ 1, p.err)) break;
+      if (lane == 0) {
+        PrefillTile& t = sm.tile[stage];
+        t.j0 = j0;
+        uint32_t bytes = 0;
+#pragma unroll
+        for (int b = 0; b < kMaxBoxes; ++b) {
+          t.blk[b] = paged ? blks[b] : 0;
+          if (b < nbox && (!paged || blks[b] >= 0)) bytes += 2u * box_rows * 128;
+        }
+        mbar_arrive_expect_tx(&sm.kv_full[stage], bytes);
+      }
+      __syncwarp();
+      if (lane < 2) {  // lane 0: K boxes, lane 1: V boxes
+        const CUtensorMap* map = lane == 0 ? &tmk : &tmv;
+        uint8_t* dst = lane == 0 ? &sm.k[stage][0] : &sm.v[stage][0];
+        for (int b = 0; b < nbox; ++b) {
+          int y;
+          if (paged) {
+            if (blks[b] < 0) continue;
+            const int pos = j0 + b * box_rows;
+            y = blks[b] * bs + (pos - (pos / bs) * bs);
+          } else {
+            y = si.k_begin + j0 + b * box_rows;  // rows past the tensor end read as zeros
+          }
+          tma_load_2d(dst + b * box_rows * 128, map, &sm.kv_full[stage], kvh * 128, y);
+        }
+      }
+      __syncwarp();
+      if (++stage == kStages) { stage = 0; phase ^= 1; }
+    }
+  } else if (warp == kMmaWarp) {
+    // ============================================================ MMA issuer
+    if (lane == 0 && ntiles > 0) {
+      const uint32_t idesc_s = tc::idesc_e4m3(128, 128, false, false);
+      const uint32_t idesc_pv = tc::idesc_e4m3(128, 128, false, true);
+      const uint32_t qh = smem_u32(sm.qhi), ql = smem_u32(sm.qlo);
+      bool ok = mbar_wait(&sm.q_full, 0, p.err);
+      int stage = 0;
+      uint32_t phase = 0;
+      int prev_stage = 0;
+      auto issue_pv = [&](int jt, int st) -> bool {
+        const int b = jt & 1;
+        if (!mbar_wait(&sm.p_full[b], (jt >> 1) & 1, p.err)) return false;
+        tc::fence_after_sync();
+        const uint32_t va = smem_u32(&sm.v[st][0]);
+        const uint32_t pa[2] = {smem_u32(&sm.phi[b][0]), smem_u32(&sm.plo[b][0])};
+#pragma unroll
+        for (int plane = 0; plane < 2; ++plane)
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks) {
+            const uint64_t ad = tc::smem_desc(pa[plane] + ks * 32, 16, 1024, tc::kSw128);
+            const uint64_t bd = tc::smem_desc(va + ks * 32 * 128, 0, 1024, tc::kSw128);
+            tc::mma_f8(tmem + kColO, ad, bd, idesc_pv, (jt > 0 || plane > 0 || ks > 0) ? 1u : 0u);
+          }
+        tc::commit(&sm.kv_empty[st]);
+        tc::commit(&sm.pv_done[b]);
+        return true;
+      };
+      for (int j = 0; ok && j < ntiles; ++j) {
+        if (!mbar_wait(&sm.kv_full[stage], phase, p.err)) break;
+        const int sb = j & 1;
+        if (!mbar_wait(&sm.s_empty[sb], ((j >> 1) & 1) ^ 1, p.err)) break;
+        tc::fence_after_sync();
+        const uint32_t ka = smem_u32(&sm.k[stage][0]);
+#pragma unroll
+        for (int plane = 0; plane < 2; ++plane)
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks) {
+            const uint64_t ad = tc::smem_desc((plane ? ql : qh) + ks * 32, 16, 1024, tc::kSw128);
+            const uint64_t bd = tc::smem_desc(ka + ks * 32, 16, 1024, tc::kSw128);
+            tc::mma_f8(tmem + kColS0 + sb * 128, ad, bd, idesc_s, (plane > 0 || ks > 0) ? 1u : 0u);
+          }
+        tc::commit(&sm.s_full[sb]);
+        if (j > 0 && !issue_pv(j - 1, prev_stage)) { ok = false; break; }
+        prev_stage = stage;
+        if (++stage == kStages) { stage = 0; phase ^= 1; }
+      }
+      if (ok) issue_pv(ntiles - 1, prev_stage);
+    }
+    __syncwarp();
+  } else {
+    // ============================================================ softmax warps 0-3
+    const int r = tid;               // query row within the tile
+    const bool row_ok = r < rows;
+    const int qi = q0 + r;           // query index within the sequence
+    const int lim = qi + (si.nk - si.nq);  // largest visible key position of this row
+    const uint32_t lane_base = static_cast<uint32_t>(32 * warp) << 16;
+    // ---- query row -> e4m3 hi / lo, 128B-swizzled K-major rows
+    float cs;
+    {
+      uint4 w[16];  // the row as packed bf16 pairs
+      if (row_ok) {
+        const uint4* src = reinterpret_cast<const uint4*>(
+            p.q + static_cast<int64_t>(si.q_begin + qi) * p.q_row_stride + static_cast<int64_t>(h) * 128);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) w[i] = __ldg(src + i);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) w[i] = make_uint4(0, 0, 0, 0);
+      }
+      auto widen = [&](int i, float (&x)[8]) {
+        const uint32_t ww[4] = {w[i].x, w[i].y, w[i].z, w[i].w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          x[2 * k] = __uint_as_float(ww[k] << 16);
+          x[2 * k + 1] = __uint_as_float(ww[k] & 0xFFFF0000u);
+        }
+      };
+      float amax = 0.f;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        float x[8];
+        widen(i, x);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) amax = fmaxf(amax, fabsf(x[k]));
+      }
+      float srow;
+      const float inv = pow2_inv_scale(amax, &srow);
+      cs = srow * p.scale_log2;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {  // 16 dims per 16-byte chunk
+        float x[16], a[8], b[8];
+        widen(2 * c, a);
+        widen(2 * c + 1, b);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          x[k] = a[k] * inv;
+          x[8 + k] = b[k] * inv;
+        }
+        uint4 hv, lv;
+        split16(x, hv, lv);
+        const int off = r * 128 + ((c ^ (r & 7)) << 4);
+        *reinterpret_cast<uint4*>(&sm.qhi[off]) = hv;
+        *reinterpret_cast<uint4*>(&sm.qlo[off]) = lv;
+      }
+    }
+    fence_proxy_async_smem();
+    mbar_arrive(&sm.q_full);
+
+    const bool kscaled = p.k_scale != nullptr;
+    const bool vscaled = p.v_scale != nullptr;
+    const bool paged = p.block_tables != nullptr;
+    const int bs = p.block_size;
+    const int box_rows = paged ? (bs % 128 == 0 ? 128 : bs % 64 == 0 ? 64 : bs % 32 == 0 ? 32 : 16) : kBN;
+    float m_ref = -INFINITY;  // reference max of O and l (log2 units)
+    float l = 0.f;
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int j = 0; j < ntiles; ++j) {
+      if (!mbar_wait(&sm.kv_full[stage], phase, p.err)) { ok = false; break; }
+      const int j0 = sm.tile[stage].j0;
+      // key columns of this tile that can be valid at all (visible, inside this sequence)
+      const int col_end = min(kBN, si.vis - j0);
+      bool full = row_ok && j0 + kBN - 1 <= lim && col_end == kBN;
+      uint32_t boxmask = 0xFFu;  // paged: boxes whose block is valid
+      if (paged) {
+        boxmask = 0;
+#pragma unroll
+        for (int b = 0; b < kMaxBoxes; ++b)
+          if (b * box_rows < kBN && sm.tile[stage].blk[b] >= 0) boxmask |= 1u << b;
+        if (boxmask != (1u << (kBN / box_rows)) - 1u) full = false;
+      }
+      const int box_shift = 31 - __clz(box_rows);
+      auto col_valid = [&](int c) -> bool {
+        const int kv = j0 + c;
+        return row_ok && c < col_end && kv <= lim && ((boxmask >> (c >> box_shift)) & 1u);
+      };
+      // per-key scales for the scaled cache format: this tile's key row c belongs to the thread
+      // with r == c; they are read per column below from global memory
+      const int sb = j & 1;
+      if (!mbar_wait(&sm.s_full[sb], (j >> 1) & 1, p.err)) { ok = false; break; }
+      tc::fence_after_sync();
+      const uint32_t sc = tmem + lane_base + kColS0 + sb * 128;
+      // ---- pass 1: row maximum
+      float tmax = -INFINITY;
+#pragma unroll
+      for (int c0 = 0; c0 < kBN; c0 += 32) {
+        float v[32];
+        tmem_ld32(sc + c0, v);
+        tc::wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          float x = v[i] * cs;
+          if (kscaled && col_valid(c0 + i)) {
+            const int c = c0 + i;
+            const int64_t slot = paged ? static_cast<int64_t>(sm.tile[stage].blk[c >> box_shift]) * bs +
+                                             ((j0 + c) - ((j0 + c) / bs) * bs)
+                                       : static_cast<int64_t>(si.k_begin + j0 + c);
+            x *= __ldg(p.k_scale + slot * p.num_kv_heads + kvh);
+          }
+          if (!full && !col_valid(c0 + i)) x = -INFINITY;
+          tmax = fmaxf(tmax, x);
+        }
+      }
+      // ---- lazy rescale: move the reference max only when it grows by more than 2^4
+      float alpha = 1.f;
+      if (tmax > m_ref + kRescaleLog2) {
+        const float m_new = tmax;
+        alpha = m_ref == -INFINITY ? 0.f : ex2(m_ref - m_new);
+        m_ref = m_new;
+        l *= alpha;
+      }
+      const bool need_rescale = __any_sync(0xffffffffu, alpha != 1.f) && j > 0;
+      // O is quiescent once the previous tile's PV is done; P buffer sb was last read by PV(j-2)
+      // each warp rescales its own rows; a warp that waits here for PV(j-1) waits on the phase
+      // the other warps meet at tile j+1, and PV(j+1) cannot complete before this warp's P(j+1)
+      if (need_rescale) {
+        if (!mbar_wait(&sm.pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, p.err)) { ok = false; break; }
+        tc::fence_after_sync();
+        const uint32_t oc = tmem + lane_base + kColO;
+#pragma unroll
+        for (int c0 = 0; c0 < 128; c0 += 16) {
+          float o16[16];
+          tc::ld16(oc + c0, o16);
+          tc::wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) o16[i] *= alpha;
+          tc::st16(oc + c0, o16);
+        }
+        tc::wait_st();
+      }
+      if (j >= 2) {
+        if (!mbar_wait(&sm.pv_done[sb], ((j - 2) >> 1) & 1, p.err)) { ok = false; break; }
+      }
+      // ---- pass 2: P = 16 * 2^(s - m_ref) as e4m3 hi + lo, row sum
+      const float m_use = m_ref == -INFINITY ? 0.f : m_ref;
+#pragma unroll
+      for (int c0 = 0; c0 < kBN; c0 += 32) {
+        float v[32];
+        tmem_ld32(sc + c0, v);
+        tc::wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int c = c0 + i;
+          float x = v[i] * cs;
+          float pv = 0.f;
+          if (full || col_valid(c)) {
+            float ks = 1.f, vs = 1.f;
+            if (kscaled) {
+              const int64_t slot = paged ? static_cast<int64_t>(sm.tile[stage].blk[c >> box_shift]) * bs +
+                                               ((j0 + c) - ((j0 + c) / bs) * bs)
+                                         : static_cast<int64_t>(si.k_begin + j0 + c);
+              ks = __ldg(p.k_scale + slot * p.num_kv_heads + kvh);
+              vs = __ldg(p.v_scale + slot * p.num_kv_heads + kvh);
+            }
+            const float e = ex2(x * ks - m_use);
+            l += kPScale * e;
+            pv = kPScale * e * vs;
+          }
+          v[i] = pv;
+        }
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          uint4 hv, lv;
+          split16(&v[16 * half], hv, lv);
+          const int c = (c0 >> 4) + half;  // 16-byte chunk index within the 128-byte row
+          const int off = r * 128 + ((c ^ (r & 7)) << 4);
+          *reinterpret_cast<uint4*>(&sm.phi[sb][off]) = hv;
+          *reinterpret_cast<uint4*>(&sm.plo[sb][off]) = lv;
+        }
+      }
+      tc::fence_before_sync();
+      mbar_arrive(&sm.s_empty[sb]);
+      // V rows of keys outside the sequence (or in masked blocks) may hold any bytes: zero them
+      {
+        const int kr = r;  // this thread also owns key row kr of the tile
+        const bool kv_ok = kr < col_end && ((boxmask >> (kr >> box_shift)) & 1u);
+        if (!kv_ok) {
+          uint4* vrow = reinterpret_cast<uint4*>(&sm.v[stage][kr * 128]);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) vrow[i] = make_uint4(0, 0, 0, 0);
+        }
+      }
+      fence_proxy_async_smem();
+      tc::fence_before_sync();
+      mbar_arrive(&sm.p_full[sb]);
+      if (++stage == kStages) { stage = 0; phase ^= 1; }
+    }
+    // ---- epilogue: O / l -> fp16 -> bf16 (the reference's output path)
+    if (row_ok) {
+      uint16_t* dst = p.out + static_cast<int64_t>(si.q_begin + qi) * p.out_row_stride + h * 128;
+      if (ntiles == 0 || !ok) {
+        for (int i = 0; i < 16; ++i) reinterpret_cast<uint4*>(dst)[i] = make_uint4(0, 0, 0, 0);
+      }
+    }
+    if (ntiles > 0 && ok) {
+      const int jl = ntiles - 1;
+      if (mbar_wait(&sm.pv_done[jl & 1], (jl >> 1) & 1, p.err)) {
+        tc::fence_after_sync();
+        const uint32_t oc = tmem + lane_base + kColO;
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+#pragma unroll
+        for (int c0 = 0; c0 < 128; c0 += 16) {
+          float o16[16];
+          tc::ld16(oc + c0, o16);
+          tc::wait_ld();
+          if (row_ok) {
+            uint32_t pk[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              __nv_bfloat16 a = out_round(o16[2 * i] * inv), b = out_round(o16[2 * i + 1] * inv);
+              pk[i] = static_cast<uint32_t>(*reinterpret_cast<uint16_t*>(&a)) |
+                      (static_cast<uint32_t>(*reinterpret_cast<uint16_t*>(&b)) << 16);
+            }
+            uint4* dst = reinterpret_cast<uint4*>(
+                p.out + static_cast<int64_t>(si.q_begin + qi) * p.out_row_stride + h * 128 + c0);
+            dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+          }
+        }
+      }
+    }
+  }
+
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  if (warp == kMmaWarp) tc::tmem_dealloc(tmem, kTmemCols);
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (fn == nullptr) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
+
+bool make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t row_bytes, int kvh,
+              int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return false;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(kvh) * 128, static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_bytes)};
+  const cuuint32_t box[2] = {128, static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+cudaError_t launch_prefill(const PrefillParams& p, cudaStream_t stream) {
+  const bool paged = p.block_tables != nullptr;
+  const int box_rows = paged ? (p.block_size % 128 == 0 ? 128 : p.block_size % 64 == 0 ? 64
+                                : p.block_size % 32 == 0 ? 32 : 16)
+                             : kBN;
+  const int64_t rows = paged ? p.num_blocks * p.block_size : p.num_blocks;
+  CUtensorMap tmk, tmv;
+  if (!make_map(&tmk, p.k, rows, p.kv_row_stride, p.num_kv_heads, box_rows) ||
+      !make_map(&tmv, p.v, rows, p.kv_row_stride, p.num_kv_heads, box_rows))
+    return cudaErrorInvalidValue;
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const size_t smem = sizeof(PrefillSmem) + 1024;
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(smem));
+    configured[dev] = true;
+  }
+  const dim3 grid((p.max_seqlen_q + kBM - 1) / kBM, p.num_heads, p.num_seqs);
+  prefill_kernel<<<grid, kThreads, smem, stream>>>(tmk, tmv, p);
+  return cudaGetLastError();
+}
+
 }  // namespace fp8attn

@@ -1,0 +1,153 @@
+"""Prefill entry point parity: reference golden outputs (paged and contiguous layouts, long and
+speculative-verify sized query sequences), the fp32 oracle on benchmark configs 3 and 4 at full
+size, and edge cases (query tiles straddling 128 rows, nk < nq, empty sequences, block sizes
+16..256, GQA 1..8, NaN bytes outside the context, scaled caches)."""
+import pytest
+import torch
+
+from helpers import assert_close, bf16, fp8
+from oracle import attention as oatt
+
+pytestmark = pytest.mark.gpu
+
+
+def _prefill(q, k, v, bt, cq, ck, mq, mk, scale, **kw):
+    from nanovllm_b200 import fp8_prefill_attention
+    out = fp8_prefill_attention(q, k, v, block_tables=bt, cu_seqlens_q=cq, cu_seqlens_k=ck,
+                                max_seqlen_q=mq, max_seqlen_k=mk, softmax_scale=scale, **kw)
+    torch.cuda.synchronize()
+    return out
+
+
+def _no_device_error():
+    from nanovllm_b200.fp8_attention import device_error
+    assert device_error() == 0
+
+
+def _oracle(c, rows=None, **kw):
+    return oatt.prefill(c.q.cpu(), c.k.cpu(), c.v.cpu(),
+                        None if c.block_tables is None else c.block_tables.cpu(),
+                        c.cu_seqlens_q.cpu(), c.cu_seqlens_k.cpu(), c.scale, **kw)
+
+
+@pytest.mark.parametrize("name", ["prefill_paged", "prefill_paged_small", "prefill_paged_bs256",
+                                  "prefill_contig"])
+def test_prefill_matches_reference_golden(golden, name):
+    g = golden(name)
+    cq, ck = torch.from_numpy(g["cu_seqlens_q"]), torch.from_numpy(g["cu_seqlens_k"])
+    bt = torch.from_numpy(g["block_tables"]).cuda() if "block_tables" in g else None
+    nq = (cq[1:] - cq[:-1]).max().item()
+    nk = (ck[1:] - ck[:-1]).max().item()
+    out = _prefill(bf16(g["q"]).cuda(), fp8(g["k"]).cuda(), fp8(g["v"]).cuda(), bt, cq.cuda(),
+                   ck.cuda(), nq, nk, float(g["scale"]))
+    assert_close(out, bf16(g["out"]), what=name)
+    _no_device_error()
+
+
+def _store_new_rows(c):
+    from nanovllm_b200 import store_kvcache
+    store_kvcache(c.new_k, c.new_v, c.k, c.v, c.slot_mapping)
+    torch.cuda.synchronize()
+
+
+def test_prefill_config3_full_size():
+    from nanovllm_b200 import workloads
+    c = workloads.config3("cuda")
+    _store_new_rows(c)
+    out = _prefill(c.q, c.k, c.v, c.block_tables, c.cu_seqlens_q, c.cu_seqlens_k, c.max_seqlen_q,
+                   c.max_seqlen_k, c.scale)
+    assert_close(out, _oracle(c), what="config3")
+    _no_device_error()
+
+
+def test_prefill_config4_mixed_spec_and_fresh():
+    from nanovllm_b200 import workloads
+    c = workloads.config4("cuda")
+    _store_new_rows(c)
+    out = _prefill(c.q, c.k, c.v, c.block_tables, c.cu_seqlens_q, c.cu_seqlens_k, c.max_seqlen_q,
+                   c.max_seqlen_k, c.scale)
+    # the oracle on a sample: 24 spec-verify sequences and both fresh 512-token chunks
+    cq = c.cu_seqlens_q.cpu()
+    pick = list(range(0, 192, 8)) + [192, 193]
+    rows = torch.cat([torch.arange(int(cq[s]), int(cq[s + 1])) for s in pick])
+    from nanovllm_b200.workloads import PrefillCase
+    ck = c.cu_seqlens_k.cpu()
+    nqs = [int(cq[s + 1] - cq[s]) for s in pick]
+    nks = [int(ck[s + 1] - ck[s]) for s in pick]
+    sub = PrefillCase(q=c.q[rows.cuda()], k=c.k, v=c.v, block_tables=c.block_tables[pick],
+                      cu_seqlens_q=torch.tensor([0] + torch.tensor(nqs).cumsum(0).tolist(), dtype=torch.int32),
+                      cu_seqlens_k=torch.tensor([0] + torch.tensor(nks).cumsum(0).tolist(), dtype=torch.int32),
+                      max_seqlen_q=max(nqs), max_seqlen_k=max(nks))
+    assert_close(out[rows.cuda()], _oracle(sub), what="config4 sample")
+    _no_device_error()
+
+
+@pytest.mark.parametrize("bs", [16, 32, 64, 256])
+@pytest.mark.parametrize("hq,kvh", [(4, 4), (8, 2), (16, 2)])
+def test_prefill_paged_edge_cases(bs, hq, kvh):
+    from nanovllm_b200 import workloads
+    nqs = [127, 128, 129, 1, 300, 0, 40, 9]
+    pre = [0, 3, 200, 77, 1000, 5, 0, 130]
+    c = workloads.prefill_case(nqs, pre, hq, kvh, seed=bs + hq, device="cuda", block_size=bs,
+                               pool_factor=1.2)
+    _store_new_rows(c)
+    out = _prefill(c.q, c.k, c.v, c.block_tables, c.cu_seqlens_q, c.cu_seqlens_k, c.max_seqlen_q,
+                   c.max_seqlen_k, c.scale)
+    assert_close(out, _oracle(c), what=f"paged bs{bs} hq{hq} kvh{kvh}")
+    _no_device_error()
+
+
+@pytest.mark.parametrize("hq,kvh", [(4, 4), (8, 1)])
+def test_prefill_contiguous_edge_cases(hq, kvh):
+    from nanovllm_b200 import workloads
+    nqs = [130, 1, 64, 257, 3]
+    pre = [0, 10, 100, 0, 2]
+    c = workloads.prefill_case(nqs, pre, hq, kvh, seed=7 + hq, device="cuda", paged=False)
+    out = _prefill(c.q, c.k, c.v, None, c.cu_seqlens_q, c.cu_seqlens_k, c.max_seqlen_q,
+                   c.max_seqlen_k, c.scale)
+    assert_close(out, _oracle(c), what=f"contig hq{hq} kvh{kvh}")
+    _no_device_error()
+
+
+def test_prefill_rows_without_keys_and_nan_padding():
+    # nk < nq: the first rows see no key and give 0 (reference :311); cache bytes outside every
+    # sequence are NaN codes that must not leak
+    from nanovllm_b200 import workloads
+    from nanovllm_b200.workloads import PrefillCase
+    c = workloads.prefill_case([200, 150], [60, 0], 8, 2, seed=21, device="cuda", block_size=64,
+                               pool_factor=1.0)
+    _store_new_rows(c)
+    kc, vc = c.k.view(torch.uint8), c.v.view(torch.uint8)
+    ck = c.cu_seqlens_k.cpu()
+    for s in range(2):
+        n = int(ck[s + 1] - ck[s])
+        for j in range(n, ((n + 63) // 64) * 64):
+            blk = int(c.block_tables[s, j // 64])
+            kc[blk, j % 64] = 0x7F
+            vc[blk, j % 64] = 0x7F
+    # shrink sequence 1's keys below its queries: rows 0..39 then see nothing
+    ck2 = ck.clone()
+    ck2[2] = ck2[1] + 110
+    c2 = PrefillCase(q=c.q, k=c.k, v=c.v, block_tables=c.block_tables, cu_seqlens_q=c.cu_seqlens_q,
+                     cu_seqlens_k=ck2.cuda(), max_seqlen_q=200, max_seqlen_k=260)
+    out = _prefill(c2.q, c2.k, c2.v, c2.block_tables, c2.cu_seqlens_q, c2.cu_seqlens_k, 200, 260,
+                   c2.scale)
+    assert torch.isfinite(out.float()).all()
+    ref = _oracle(c2)
+    assert_close(out, ref, what="nk<nq + nan padding")
+    assert torch.all(out[200:240] == 0)
+    _no_device_error()
+
+
+def test_prefill_scaled_cache():
+    from nanovllm_b200 import workloads
+    c = workloads.prefill_case([150, 20, 4], [100, 300, 50], 8, 2, seed=31, device="cuda",
+                               block_size=128)
+    nb, bs, kvh, _ = c.k.shape
+    gen = torch.Generator().manual_seed(8)
+    ks = (torch.rand(nb, bs, kvh, generator=gen) * 0.05 + 0.001).cuda()
+    vs = (torch.rand(nb, bs, kvh, generator=gen) * 0.05 + 0.001).cuda()
+    out = _prefill(c.q, c.k, c.v, c.block_tables, c.cu_seqlens_q, c.cu_seqlens_k, c.max_seqlen_q,
+                   c.max_seqlen_k, c.scale, k_scale=ks, v_scale=vs)
+    assert_close(out, _oracle(c, k_scale=ks.cpu(), v_scale=vs.cpu()), what="prefill scaled")
+    _no_device_error()
