@@ -52,6 +52,11 @@ struct __align__(1024) PrefillSmem {
   uint8_t phi[2][kBM * 128];            // A operand of PV, by tile parity
   uint8_t plo[2][kBM * 128];
   PrefillTile tile[kStages];
+  // general-path column table of the S buffer's tile (thread r fills column r): key and value
+  // scales, and a validity bit per column
+  float colk[2][kBN];
+  float colv[2][kBN];
+  uint32_t colok[2][kBN / 32];
   uint64_t kv_full[kStages];
   uint64_t kv_empty[kStages];
   uint64_t q_full;
@@ -347,7 +352,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_arrive(&sm.q_full);
 
     const bool kscaled = p.k_scale != nullptr;
-    const bool vscaled = p.v_scale != nullptr;
     const bool paged = p.block_tables != nullptr;
     const int bs = p.block_size;
     const int box_rows = paged ? (bs % 128 == 0 ? 128 : bs % 64 == 0 ? 64 : bs % 32 == 0 ? 32 : 16) : kBN;
@@ -361,47 +365,61 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int j0 = sm.tile[stage].j0;
       // key columns of this tile that can be valid at all (visible, inside this sequence)
       const int col_end = min(kBN, si.vis - j0);
-      bool full = row_ok && j0 + kBN - 1 <= lim && col_end == kBN;
       uint32_t boxmask = 0xFFu;  // paged: boxes whose block is valid
       if (paged) {
         boxmask = 0;
 #pragma unroll
         for (int b = 0; b < kMaxBoxes; ++b)
           if (b * box_rows < kBN && sm.tile[stage].blk[b] >= 0) boxmask |= 1u << b;
-        if (boxmask != (1u << (kBN / box_rows)) - 1u) full = false;
       }
       const int box_shift = 31 - __clz(box_rows);
-      auto col_valid = [&](int c) -> bool {
-        const int kv = j0 + c;
-        return row_ok && c < col_end && kv <= lim && ((boxmask >> (c >> box_shift)) & 1u);
-      };
-      // per-key scales for the scaled cache format: this tile's key row c belongs to the thread
-      // with r == c; they are read per column below from global memory
+      // columns [0, vlim) of this tile are visible to this row.  A tile with a masked block, or
+      // any tile of a scaled cache, takes the general path through the column table (uniform
+      // across the four softmax warps)
+      const int vlim = row_ok ? max(0, min(col_end, lim - j0 + 1)) : 0;
+      const bool general = kscaled || !(p.scale_log2 > 0.f) || boxmask != (1u << (kBN / box_rows)) - 1u;
       const int sb = j & 1;
       if (!mbar_wait(&sm.s_full[sb], (j >> 1) & 1, p.err)) { ok = false; break; }
       tc::fence_after_sync();
+      if (general) {
+        // S(j) complete => every softmax thread finished tile j-2, the last reader of table sb
+        const int c = r;
+        const bool cok = c < col_end && ((boxmask >> (c >> box_shift)) & 1u);
+        float ks = 1.f, vs = 1.f;
+        if (kscaled && cok) {
+          const int kv = j0 + c;
+          const int64_t slot = paged ? static_cast<int64_t>(sm.tile[stage].blk[c >> box_shift]) * bs + (kv % bs)
+                                     : static_cast<int64_t>(si.k_begin) + kv;
+          ks = __ldg(p.k_scale + slot * p.num_kv_heads + kvh);
+          vs = __ldg(p.v_scale + slot * p.num_kv_heads + kvh);
+        }
+        sm.colk[sb][c] = ks;
+        sm.colv[sb][c] = vs;
+        const uint32_t bal = __ballot_sync(0xffffffffu, cok);
+        if (lane == 0) sm.colok[sb][warp] = bal;
+        named_barrier(1, 128);
+      }
       const uint32_t sc = tmem + lane_base + kColS0 + sb * 128;
-      // ---- pass 1: row maximum
+      // ---- pass 1: row maximum (of the raw scores on the fast path: cs > 0 commutes with max)
       float tmax = -INFINITY;
-#pragma unroll
+#pragma unroll 1
       for (int c0 = 0; c0 < kBN; c0 += 32) {
         float v[32];
         tmem_ld32(sc + c0, v);
         tc::wait_ld();
+        if (!general) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          float x = v[i] * cs;
-          if (kscaled && col_valid(c0 + i)) {
-            const int c = c0 + i;
-            const int64_t slot = paged ? static_cast<int64_t>(sm.tile[stage].blk[c >> box_shift]) * bs +
-                                             ((j0 + c) - ((j0 + c) / bs) * bs)
-                                       : static_cast<int64_t>(si.k_begin + j0 + c);
-            x *= __ldg(p.k_scale + slot * p.num_kv_heads + kvh);
+          for (int i = 0; i < 32; ++i) tmax = fmaxf(tmax, c0 + i < vlim ? v[i] : -INFINITY);
+        } else {
+          const uint32_t okw = sm.colok[sb][c0 >> 5];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const bool cok = ((okw >> i) & 1u) && c0 + i < vlim;
+            tmax = fmaxf(tmax, cok ? v[i] * sm.colk[sb][c0 + i] * cs : -INFINITY);
           }
-          if (!full && !col_valid(c0 + i)) x = -INFINITY;
-          tmax = fmaxf(tmax, x);
         }
       }
+      if (!general && tmax != -INFINITY) tmax *= cs;
       // ---- lazy rescale: move the reference max only when it grows by more than 2^4
       float alpha = 1.f;
       if (tmax > m_ref + kRescaleLog2) {
@@ -434,30 +452,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // ---- pass 2: P = 16 * 2^(s - m_ref) as e4m3 hi + lo, row sum
       const float m_use = m_ref == -INFINITY ? 0.f : m_ref;
-#pragma unroll
+#pragma unroll 1
       for (int c0 = 0; c0 < kBN; c0 += 32) {
         float v[32];
         tmem_ld32(sc + c0, v);
         tc::wait_ld();
+        if (!general) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int c = c0 + i;
-          float x = v[i] * cs;
-          float pv = 0.f;
-          if (full || col_valid(c)) {
-            float ks = 1.f, vs = 1.f;
-            if (kscaled) {
-              const int64_t slot = paged ? static_cast<int64_t>(sm.tile[stage].blk[c >> box_shift]) * bs +
-                                               ((j0 + c) - ((j0 + c) / bs) * bs)
-                                         : static_cast<int64_t>(si.k_begin + j0 + c);
-              ks = __ldg(p.k_scale + slot * p.num_kv_heads + kvh);
-              vs = __ldg(p.v_scale + slot * p.num_kv_heads + kvh);
-            }
-            const float e = ex2(x * ks - m_use);
-            l += kPScale * e;
-            pv = kPScale * e * vs;
+          for (int i = 0; i < 32; ++i) {
+            const float e = c0 + i < vlim ? ex2(fmaf(v[i], cs, -m_use)) : 0.f;
+            l += e;
+            v[i] = kPScale * e;
           }
-          v[i] = pv;
+        } else {
+          const uint32_t okw = sm.colok[sb][c0 >> 5];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const bool cok = ((okw >> i) & 1u) && c0 + i < vlim;
+            const float e = cok ? ex2(v[i] * sm.colk[sb][c0 + i] * cs - m_use) : 0.f;
+            l += e;
+            v[i] = kPScale * e * sm.colv[sb][c0 + i];
+          }
         }
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
@@ -498,7 +513,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (mbar_wait(&sm.pv_done[jl & 1], (jl >> 1) & 1, p.err)) {
         tc::fence_after_sync();
         const uint32_t oc = tmem + lane_base + kColO;
-        const float inv = l > 0.f ? 1.f / l : 0.f;
+        const float inv = l > 0.f ? 1.f / (kPScale * l) : 0.f;
 #pragma unroll
         for (int c0 = 0; c0 < 128; c0 += 16) {
           float o16[16];
