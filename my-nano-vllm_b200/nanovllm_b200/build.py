@@ -3,7 +3,9 @@
 The library is self-contained (static cudart, driver entry points resolved at run time), so it
 loads on a machine without a GPU and is shipped beside this file.
 
-    python -m nanovllm_b200.build        # build if any source is newer than the library
+    python my-nano-vllm_b200/nanovllm_b200/build.py   # build if any source is newer than the library
+
+(run as a script: importing the package loads the library it builds)
 """
 from __future__ import annotations
 
