@@ -117,6 +117,35 @@ FP8ATTN_API int fp8attn_prefill(void* out, const void* q, int64_t q_row_stride, 
  * current device for its split-KV engine (diagnostics and benchmarking). */
 FP8ATTN_API int fp8attn_decode_ctas(int num_seqs, int num_heads, int num_kv_heads, int max_seqlen_q);
 
+/*
+ * No counterpart in the reference.  fp8attn_decode without a caller-supplied workspace: the
+ * split-KV scratch is a file-scope device array of FP8ATTN_NOALLOC_SCRATCH_BYTES inside the
+ * library, so a call allocates no device memory (no cudaMalloc / cudaFree, no caching allocator).
+ * For hosts that cannot allocate on the decode path: a C / cgo / ctypes host without a device
+ * allocator of its own, or one that has handed all free HBM to the KV cache (the reference sizes
+ * its cache from mem_get_info, nanovllm/engine/model_runner.py:104-122) and has none left for a
+ * workspace.  Arguments, results and errors are those of fp8attn_decode.
+ *   - Limit: a shape whose workspace (fp8attn_workspace_bytes(num_seqs, num_heads,
+ *     num_kv_heads, 1)) exceeds FP8ATTN_NOALLOC_SCRATCH_BYTES is rejected with
+ *     FP8ATTN_EWORKSPACE (on a 148-SM B200 this admits up to ~3200 (sequence, kv head) pairs
+ *     for GQA groups <= 8; wider groups need fp8attn_decode).
+ *   - Setup: the first call on a device resolves the array's address with cudaGetSymbolAddress
+ *     (which loads the library's module on that device); make it outside any stream capture,
+ *     with the device current.
+ *   - Zero state: the array starts zeroed; its work counters (bytes 4..11) must be zero when a
+ *     launch starts, and every launch leaves them zero.  Device error codes are recorded in its
+ *     first word and are not reported by this call.
+ *   - One scratch per device: calls whose kernels may overlap (other streams, other host threads,
+ *     other processes sharing the context) race on it and give wrong results.  Serialise them.
+ */
+#define FP8ATTN_NOALLOC_SCRATCH_BYTES (32LL << 20)
+FP8ATTN_API int fp8attn_decode_noalloc(void* out, const void* q, int64_t q_row_stride,
+                   const void* k_cache, const void* v_cache, const float* k_scale,
+                   const float* v_scale, const int32_t* block_tables, int64_t block_tables_stride,
+                   int max_num_blocks, const int32_t* context_lens, int num_seqs, int num_heads,
+                   int num_kv_heads, int head_dim, int64_t num_blocks, int block_size,
+                   float softmax_scale, void* stream);
+
 /* Tuning knob (process-wide): minimum key positions per split-KV work item, a multiple of 128
  * (default 128).  Returns the previous value; other values are rejected with -1. */
 FP8ATTN_API int fp8attn_set_decode_min_chunk(int tokens);

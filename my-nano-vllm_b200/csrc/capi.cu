@@ -4,6 +4,7 @@
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 
 #include "../../include/fp8attn.h"
@@ -373,6 +374,64 @@ int fp8attn_prefill(void* out, const void* q, int64_t q_row_stride, const void* 
   const cudaError_t e = fp8attn::launch_prefill(pp, st);
   if (e != cudaSuccess) return cuda_fail(e, "prefill launch");
   return FP8ATTN_OK;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------- decode without allocation
+// The split-KV scratch of fp8attn_decode_noalloc: control words, plan and partials, laid out as
+// a caller workspace.  Zero at module load; the decode kernel returns its counters to zero at
+// the end of every launch.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[FP8ATTN_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[kMaxDevices] = {};
+
+int noalloc_scratch(void** addr) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(FP8ATTN_EINVAL, "device %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_addr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(no-alloc scratch)");
+    g_noalloc_addr[dev] = p;
+  }
+  *addr = g_noalloc_addr[dev];
+  return FP8ATTN_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int fp8attn_decode_noalloc(void* out, const void* q, int64_t q_row_stride, const void* k_cache,
+                           const void* v_cache, const float* k_scale, const float* v_scale,
+                           const int32_t* block_tables, int64_t block_tables_stride,
+                           int max_num_blocks, const int32_t* context_lens, int num_seqs,
+                           int num_heads, int num_kv_heads, int head_dim, int64_t num_blocks,
+                           int block_size, float softmax_scale, void* stream) {
+  int rc = check_common(num_seqs, num_heads, num_kv_heads, head_dim);
+  if (rc) return rc;
+  if (num_seqs == 0) return FP8ATTN_OK;
+  const int64_t need = fp8attn_workspace_bytes(num_seqs, num_heads, num_kv_heads, 1);
+  if (need > FP8ATTN_NOALLOC_SCRATCH_BYTES)
+    return fail(FP8ATTN_EWORKSPACE,
+                "decode of %d sequences x %d kv heads (%d q heads) needs %lld bytes of scratch; "
+                "the static scratch of fp8attn_decode_noalloc holds %lld: use fp8attn_decode "
+                "with a workspace",
+                num_seqs, num_kv_heads, num_heads, static_cast<long long>(need),
+                static_cast<long long>(FP8ATTN_NOALLOC_SCRATCH_BYTES));
+  void* scratch = nullptr;
+  rc = noalloc_scratch(&scratch);
+  if (rc) return rc;
+  return fp8attn_decode(out, q, q_row_stride, k_cache, v_cache, k_scale, v_scale, block_tables,
+                        block_tables_stride, max_num_blocks, context_lens, num_seqs, num_heads,
+                        num_kv_heads, head_dim, num_blocks, block_size, softmax_scale, scratch,
+                        FP8ATTN_NOALLOC_SCRATCH_BYTES, stream);
 }
 
 }  // extern "C"

@@ -13,6 +13,7 @@ from .build import LIB_PATH, INCLUDE
 
 OK, EINVAL, EWORKSPACE, ECUDA = 0, 1, 2, 3
 WS_ERROR_OFFSET = 0
+NOALLOC_SCRATCH_BYTES = 32 << 20  # FP8ATTN_NOALLOC_SCRATCH_BYTES
 
 
 class Fp8AttnError(RuntimeError):
@@ -24,7 +25,7 @@ class Fp8AttnError(RuntimeError):
 def _load() -> ctypes.CDLL:
     if not os.path.exists(LIB_PATH):
         raise ImportError(
-            f"{LIB_PATH} is missing: build it with `python -m nanovllm_b200.build` "
+            f"{LIB_PATH} is missing: build it with `python my-nano-vllm_b200/nanovllm_b200/build.py` "
             "(there is no fallback implementation)")
     lib = ctypes.CDLL(LIB_PATH)
     i32, i64, f32, vp = ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p
@@ -44,6 +45,9 @@ def _load() -> ctypes.CDLL:
     lib.fp8attn_decode.restype = i32
     lib.fp8attn_decode.argtypes = [vp, vp, i64, vp, vp, vp, vp, vp, i64, i32, vp, i32, i32, i32,
                                    i32, i64, i32, f32, vp, i64, vp]
+    lib.fp8attn_decode_noalloc.restype = i32
+    lib.fp8attn_decode_noalloc.argtypes = [vp, vp, i64, vp, vp, vp, vp, vp, i64, i32, vp, i32, i32,
+                                           i32, i32, i64, i32, f32, vp]
     lib.fp8attn_prefill.restype = i32
     lib.fp8attn_prefill.argtypes = [vp, vp, i64, vp, vp, i64, vp, vp, vp, i64, i32, vp, vp, i32,
                                     i32, i32, i32, i32, i32, i64, i32, f32, vp, i64, vp]
