@@ -80,7 +80,8 @@ int spec_q_max(int group) {
 }
 
 struct EnginePlan {
-  int nt;
+  int nt;             // 8-row planes per row group: R = 8 nt rows (1..3)
+  int rv;             // rows the softmax processes per row group (4, or R)
   int rows;
   int max_rowgroups;
 };
@@ -88,8 +89,9 @@ struct EnginePlan {
 EnginePlan plan_engine(int group, int max_q) {
   EnginePlan e;
   const int r = group * (max_q < 1 ? 1 : max_q);
-  e.nt = r <= 8 ? 1 : 2;
+  e.nt = r <= 8 ? 1 : (r <= 16 ? 2 : 3);
   e.rows = fp8attn::decode_rows(e.nt);
+  e.rv = r <= 4 ? 4 : e.rows;
   e.max_rowgroups = (r + e.rows - 1) / e.rows;
   return e;
 }
@@ -146,7 +148,8 @@ int fp8attn_decode_ctas(int num_seqs, int num_heads, int num_kv_heads, int max_s
   const int group = num_heads / num_kv_heads;
   const int mq = max_seqlen_q <= 1 ? 1 : (max_seqlen_q < spec_q_max(group) ? max_seqlen_q
                                                                            : spec_q_max(group));
-  return fp8attn::decode_launch_grid(plan_engine(group, mq).nt, num_seqs);
+  const EnginePlan e = plan_engine(group, mq);
+  return fp8attn::decode_launch_grid(e.nt, e.rv, num_seqs);
 }
 
 int fp8attn_set_decode_min_chunk(int tokens) {
@@ -231,7 +234,7 @@ static int run_decode_engine(fp8attn::DecodeParams& p, const EnginePlan& e, cons
   if (rc) return rc;
   rc = make_cache_map(&tmv, v_cache, rows, p.num_kv_heads, p.box_rows);
   if (rc) return rc;
-  const cudaError_t err = fp8attn::launch_decode(p, e.nt, tmk, tmv, stream);
+  const cudaError_t err = fp8attn::launch_decode(p, e.nt, e.rv, tmk, tmv, stream);
   if (err != cudaSuccess) return cuda_fail(err, "decode launch");
   return FP8ATTN_OK;
 }

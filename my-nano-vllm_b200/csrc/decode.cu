@@ -20,12 +20,14 @@
 //           row, about 8 significant bits in total);
 //   warp 5  MMA issuer (one thread), per tile j:
 //             S^T[128 tok x 2R]  = K_j . [Qhi; Qlo]^T          tcgen05.mma kind::f8f6f4 (e4m3)
-//             PV^T[128 dim x 2R] = V_{j-1}^T . [Phi; Plo]^T    (V read MN-major from its tile)
-//           both double-buffered in tensor memory, P double-buffered in shared memory;
-//   warps 0-3 softmax: thread = token row of S^T (and dim row of PV^T): online softmax with the
-//           column max from redux.sync + a 4-warp exchange, P quantised as 256 p = hi + lo e4m3;
-//           the output accumulates in registers, folding in each tile's PV product two tiles
-//           later, so softmax and tensor cores never wait on each other within an item.
+//             O^T[128 dim x 2R] += V_{j-1}^T . [Phi; Plo]^T    (V read MN-major from its tile)
+//           S double-buffered and O accumulated in tensor memory, P double-buffered in shared
+//           memory;
+//   warps 0-3 softmax: thread = token row of S^T (and dim row of O^T): online softmax with the
+//           column max from redux.sync + a 4-warp exchange.  P = 16 * 2^(s - m_ref) (e4m3 hi +
+//           lo) against a reference max that moves only when a row max grows by more than 2^4;
+//           O is then rescaled in tensor memory (rare), so no per-tile work touches O.  Only the
+//           RV live rows of the row group are processed (4 for the GQA-4 decode).
 // K and V bytes go to the tensor cores untouched: no per-byte conversion anywhere.
 #include <climits>
 
@@ -74,6 +76,9 @@ struct __align__(1024) DecodeSmem {
   uint8_t q2[2][N * kHeadDim];            // K-major SW128 query operand, by item parity
   uint8_t p2[2][NT][kTile * 16];          // P^T planes of 16 columns, MN-major, by tile parity
   float qscale[2][R];                     // per-row score multiplier (scale * log2 e * 2^k)
+  int qlim[2][R];                         // per-row largest visible key position (-1: no row)
+  uint8_t qstage[R * 256];                // raw bf16 query rows of the next item (cp.async)
+  float alpha[4][R];                      // per-warp copy of a tile's rescale factors (rare)
   float red[2][4][R];                     // cross-warp row maxima, double-buffered by tile
   float redl[4][R];                       // cross-warp row sums (epilogue)
   TileHeader hdr[STAGES];
@@ -92,6 +97,12 @@ struct __align__(1024) DecodeSmem {
   // followed in shared memory by int prefix[num_seqs + 1] (item prefix sums over sequences)
   // and int info[num_seqs] ((L << 7) | rowgroups per sequence), sized per launch
 };
+
+// Two CTAs share an SM (228 KB of shared memory, 1 KB reserved per CTA) with the plan arrays of
+// up to 256 sequences (larger batches run one CTA per SM).
+static_assert(sizeof(DecodeSmem<1>) + 2 * 1024 + (2 * 256 + 1) * 4 <= 228 * 1024 / 2, "smem");
+static_assert(sizeof(DecodeSmem<2>) + 2 * 1024 + (2 * 256 + 1) * 4 <= 228 * 1024 / 2, "smem");
+static_assert(sizeof(DecodeSmem<3>) + 2 * 1024 + (2 * 256 + 1) * 4 <= 228 * 1024 / 2, "smem");
 
 __device__ __forceinline__ int seq_len_clamped(const DecodeParams& p, int b, int* nq_out) {
   int L, nq;
@@ -149,10 +160,10 @@ struct Cursor {
   int pair_first, pair_stride;
   int nth;           // items started (selects the q buffer)
   int ebase, myent;  // block-table entries ebase .. ebase+31, one per lane
-  uint4 qraw[4 * NT];  // this lane's slice of the item's q rows (bf16), loaded when the item is
-                     // claimed and consumed one item later, so no load latency is ever waited on
 };
 
+// Claims `item` for the cursor and starts the load of its first 32 block-table entries (one
+// per lane).
 template <int NT>
 __device__ __forceinline__ void cursor_set(Cursor<NT>& P, int item, const DecodeParams& p,
                                            const int* prefix, const int* info, int total_items,
@@ -203,22 +214,29 @@ __device__ __forceinline__ void cursor_set(Cursor<NT>& P, int item, const Decode
   const int idx = P.ebase + lane;
   P.myent = idx < p.max_blocks
                 ? ldg_keep(p.block_tables + static_cast<int64_t>(b) * p.bt_stride + idx) : -1;
+}
+
+// Starts copying the cursor's query rows (bf16) into qstage with cp.async; prepare_q consumes
+// them one item later, so the load latency is never waited on.
+template <int NT>
+__device__ __forceinline__ void stage_q(const Cursor<NT>& P, const DecodeParams& p, uint8_t* qstage) {
+  const int lane = threadIdx.x & 31;
   const int G = p.group;
+  // lane l: row (l >> 2) + 8 pass, dims 32 (l & 3) .. +32 (64 bytes), the slice prepare_q reads
 #pragma unroll
   for (int pass = 0; pass < NT; ++pass) {
     const int rq = pass * 8 + (lane >> 2);
-    if (rq < P.rows) {
-      const int rr = P.row0 + rq;
-      const int j = rr / G, h = P.kvh * G + (rr - j * G);
-      const uint4* src = reinterpret_cast<const uint4*>(
-          p.q + static_cast<int64_t>(P.qrow0 + j) * p.q_row_stride + static_cast<int64_t>(h) * kHeadDim + 32 * (lane & 3));
+    const bool ok = rq < P.rows;
+    const int rr = P.row0 + rq;
+    const int j = rr / G, h = P.kvh * G + (rr - j * G);
+    const uint16_t* src = ok ? p.q + static_cast<int64_t>(P.qrow0 + j) * p.q_row_stride +
+                                   static_cast<int64_t>(h) * kHeadDim + 32 * (lane & 3)
+                             : p.q;
+    const uint32_t dst = smem_u32(qstage + rq * 256 + 64 * (lane & 3));
 #pragma unroll
-      for (int i = 0; i < 4; ++i) P.qraw[4 * pass + i] = ldg_keep_v4(src + i);
-    } else {
-#pragma unroll
-      for (int i = 0; i < 4; ++i) P.qraw[4 * pass + i] = make_uint4(0, 0, 0, 0);
-    }
+    for (int i = 0; i < 4; ++i) cp_async16(dst + 16 * i, src + 8 * i, ok);
   }
+  cp_async_commit();
 }
 
 // The item's query rows -> K-major SW128 [hi rows | lo rows] operand + per-row multipliers.
@@ -228,13 +246,14 @@ __device__ __forceinline__ void prepare_q(const Cursor<NT>& P, int slot, const D
                                           DecodeSmem<NT>& sm, int lane) {
   constexpr int R = DecodeSmem<NT>::R;
   const int quarter = lane & 3;
+  cp_async_wait<0>();  // this item's rows (the only copy in flight)
 #pragma unroll
   for (int pass = 0; pass < NT; ++pass) {
     const int r = pass * 8 + (lane >> 2);
     float q[32];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const uint4 w = P.qraw[4 * pass + i];
+      const uint4 w = *reinterpret_cast<const uint4*>(&sm.qstage[r * 256 + 64 * quarter + 16 * i]);
       const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
@@ -276,11 +295,16 @@ __device__ __forceinline__ void prepare_q(const Cursor<NT>& P, int slot, const D
       *reinterpret_cast<uint4*>(&sm.q2[slot][rl * 128 + ((chunk ^ (rl & 7)) << 4)]) =
           make_uint4(lo[4 * half], lo[4 * half + 1], lo[4 * half + 2], lo[4 * half + 3]);
     }
-    if (quarter == 0) sm.qscale[slot][r] = s_row * p.scale_log2;
+    if (quarter == 0) {
+      sm.qscale[slot][r] = s_row * p.scale_log2;
+      sm.qlim[slot][r] = r < P.rows ? (p.spec_mode ? P.lim_base + (r + P.row0 % p.group) / p.group
+                                                   : INT_MAX)
+                                    : -1;
+    }
   }
 }
 
-template <int NT>
+template <int NT, int RV>
 __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
     decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                   const DecodeParams p) {
@@ -288,7 +312,8 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
   constexpr int R = Smem::R;
   constexpr int N = Smem::N;
   constexpr int kStages = Smem::STAGES;
-  constexpr uint32_t kTmemCols = NT == 1 ? 64 : 128;  // S x2 and PV x2, N columns each
+  static_assert(RV >= 1 && RV <= R && RV % 4 == 0, "live rows");
+  constexpr uint32_t kTmemCols = 3 * N <= 64 ? 64 : (3 * N <= 128 ? 128 : 256);  // S x2, O
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -416,6 +441,7 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
       ids[1] = __shfl_sync(0xffffffffu, ids[1], 0);
       cursor_set<NT>(P, ids[0], p, prefix, info, total_items, CT, B);
       cursor_set<NT>(Pn, ids[1], p, prefix, info, total_items, CT, B);
+      if (P.item < total_items) stage_q<NT>(P, p, sm.qstage);
     }
     int stage = 0;
     uint32_t phase = 0;
@@ -434,6 +460,8 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
         prepare_q<NT>(P, slot, p, sm, lane);
         fence_proxy_async_smem();
         mbar_arrive(&sm.q_full[slot]);
+        // the staging rows were read into registers above (their uses are issued): reuse it
+        if (Pn.item < total_items) stage_q<NT>(Pn, p, sm.qstage);
       }
       if (!mbar_wait(&sm.kv_empty[stage], phase ^ 1, p.ctrl)) break;
       const int t = P.t;
@@ -510,8 +538,8 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
     }
   } else if (fits && warp == kMmaWarp) {
     // ============================================================ MMA issuer (lane 0)
-    // tile j: S_j into S buffer j%2, then PV_{j-1} (or PV_j at once when j ends its item) into
-    // PV buffer (tile % 2); each PV is a fresh product (its first MMA does not accumulate)
+    // tile j: S_j into S buffer j%2, then PV_{j-1} (or PV_j at once when j ends its item),
+    // accumulated into O (an item's first tile starts it afresh)
     if (lane == 0) {
       const uint32_t idesc_s = tc::idesc_e4m3(128, N, false, false);
       const uint32_t idesc_pv = tc::idesc_e4m3(128, 16, true, true);
@@ -519,8 +547,8 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
       uint32_t phase = 0;
       int qcount[2] = {0, 0};
       bool pend = false;  // a tile whose PV is still to be issued
-      int pend_stage = 0;
-      auto issue_pv = [&](int st, int tile) -> bool {
+      int pend_stage = 0, pend_first = 0;
+      auto issue_pv = [&](int st, int tile, int fresh) -> bool {
         const int b = tile & 1;
         if (!mbar_wait(&sm.p_full[b], (tile >> 1) & 1, p.ctrl)) return false;
         tc::fence_after_sync();
@@ -532,7 +560,7 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
           for (int ks = 0; ks < 4; ++ks) {
             const uint64_t ad = tc::smem_desc(va + ks * 32 * 128, 0, 1024, tc::kSw128);
             const uint64_t bd = tc::smem_desc(pa + ks * 32 * 16, 128, 2048, tc::kSwNone);
-            tc::mma_f8(tmem + (2 + b) * N + 16 * plane, ad, bd, idesc_pv, ks > 0 ? 1u : 0u);
+            tc::mma_f8(tmem + 2 * N + 16 * plane, ad, bd, idesc_pv, (ks > 0 || !fresh) ? 1u : 0u);
           }
         }
         tc::commit(&sm.kv_empty[st]);
@@ -562,32 +590,33 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
           tc::mma_f8(tmem + sb * N, ad, bd, idesc_s, ks > 0 ? 1u : 0u);
         }
         tc::commit(&sm.s_full[sb]);
-        if (pend && !issue_pv(pend_stage, j - 1)) break;
+        if (pend && !issue_pv(pend_stage, j - 1, pend_first)) break;
         pend = true;
         pend_stage = stage;
+        pend_first = first;
         if (last) {  // the item's epilogue waits on this PV: issue it now, not after the next S
-          if (!issue_pv(stage, j)) break;
+          if (!issue_pv(stage, j, first)) break;
           pend = false;
         }
         ++j;
         if (++stage == kStages) { stage = 0; phase ^= 1; }
       }
-      if (pend) issue_pv(pend_stage, j - 1);
+      if (pend) issue_pv(pend_stage, j - 1, pend_first);
     }
     __syncwarp();
   } else if (fits && warp < 4) {
     // ============================================================ softmax warps 0-3
-    // thread r: token row r of S^T and dim row r of the PV products.  O lives in registers:
-    // at tile j the product PV_{j-2} (done by then, its P buffer is needed again) is folded in,
-    // rescaled from its tile's reference max; the item's last two products are folded in the
-    // epilogue.  m_hist keeps the reference max of the last two tiles.
+    // thread r: token row r of S^T and dim row r of O^T.  Per row q of the row group (the first
+    // RV are live): m_ref[q] = reference max (log2 units, uniform over the 128 threads), l_part[q]
+    // = this thread's share of the row sum, both relative to m_ref.
     const int r = tid;
     const uint32_t lane_base = static_cast<uint32_t>(32 * warp) << 16;
     const bool kscaled = p.k_scale != nullptr;
     const bool vscaled = p.v_scale != nullptr;
     const int box_shift = 31 - __clz(p.box_rows);
-    float cs[R], m_run[R], l_part[R], o_acc[R], m_o[R], m_hist[2][R];
-    int lim[R];
+    constexpr float kRescaleLog2 = 4.f;  // P = 16 * 2^(s - m_ref) <= 256 < 448 (e4m3 max)
+    constexpr float kPScale = 16.f;
+    float m_ref[RV], l_part[RV];
     int stage = 0, j = 0, sync_uses = 0, item_first_tile = 0;
     uint32_t phase = 0;
     int qcount[2] = {0, 0};
@@ -595,32 +624,13 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
       mbar_arrive(&sm.sync128);
       return mbar_wait(&sm.sync128, (sync_uses++) & 1, p.ctrl);
     };
-    // fold the finished product of tile t (buffer t % 2) into o_acc
-    auto fold = [&](int t) {
-      const int b = t & 1;
-      float pv[N];
-#pragma unroll
-      for (int c = 0; c < N; c += 16) {
-        float v16[16];
-        tc::ld16(tmem + lane_base + (2 + b) * N + c, v16);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) pv[c + i] = v16[i];
-      }
-      tc::wait_ld();
-#pragma unroll
-      for (int q = 0; q < R; ++q) {
-        const float mr = b ? m_hist[1][q] : m_hist[0][q];
-        const float f = t == item_first_tile ? 0.f : ex2(m_o[q] - mr);
-        o_acc[q] = o_acc[q] * f + (pv[q] + pv[R + q]);
-        m_o[q] = mr;
-      }
-    };
     auto wait_pv = [&](int t) -> bool {
       const int b = t & 1;
       if (!mbar_wait(&sm.pv_done[b], (t >> 1) & 1, p.ctrl)) return false;
       tc::fence_after_sync();
       return true;
     };
+    const uint32_t o_tmem = tmem + lane_base + 2 * N;
     while (true) {
       if (!mbar_wait(&sm.kv_full[stage], phase, p.ctrl)) break;
       const TileHeader& h = sm.hdr[stage];
@@ -629,9 +639,8 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
       // everything this tile needs from its header, read now: once P is handed over, the PV
       // completes, the stage is released and the producer rewrites the header
       const int flags = h.flags, nvalid = h.nvalid, tok0 = h.tok0, slot = h.qslot;
-      const int rows = h.rows, nchunks = h.nchunks, rg = h.rg, seq = h.seq, kvh = h.kvh;
-      const int qrow0 = h.qrow0, pair_first = h.pair_first, pair_stride = h.pair_stride;
-      const int lim_base = h.lim_base;
+      const int rows = h.rows, nchunks = h.nchunks, rg = h.rg, kvh = h.kvh;
+      const int qrow0 = h.qrow0;
       const int box = r >> box_shift;
       const int bb = h.blk[box];
       const int slot0 = h.slot0[box];
@@ -639,16 +648,11 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
       if (flags & kFirst) {
         if (!mbar_wait(&sm.q_full[slot], qcount[slot] & 1, p.ctrl)) break;
         qcount[slot]++;
-        const int row_off = (rg * R) % G;
         item_first_tile = j;
 #pragma unroll
-        for (int q = 0; q < R; ++q) {
-          cs[q] = sm.qscale[slot][q];
-          lim[q] = q < rows ? (p.spec_mode ? lim_base + (q + row_off) / G : INT_MAX) : -1;
-          m_run[q] = -INFINITY;
+        for (int q = 0; q < RV; ++q) {
+          m_ref[q] = -INFINITY;
           l_part[q] = 0.f;
-          o_acc[q] = 0.f;
-          m_o[q] = 0.f;
         }
       }
       float ks = 1.f, lv = 0.f;
@@ -673,61 +677,74 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
       tc::fence_before_sync();
       mbar_arrive(&sm.s_empty[sb]);
       const int pos = tok0 + r;
-      float xx[R], xo[R];
+      float xs[RV];  // score (log2 units) + log2 of the value scale: P's exponent
 #pragma unroll
-      for (int q = 0; q < R; ++q) {
-        float s = (x[q] + x[R + q]) * cs[q] * ks;
-        if (!(valid && pos <= lim[q])) s = -INFINITY;
-        xx[q] = s;
-        xo[q] = s + lv;
-        const int wm = __reduce_max_sync(0xffffffffu, f2ord(xo[q]));
+      for (int q = 0; q < RV; ++q) {
+        float sc = (x[q] + x[R + q]) * sm.qscale[slot][q] * ks;
+        if (!(valid && pos <= sm.qlim[slot][q])) sc = -INFINITY;
+        xs[q] = sc + lv;
+        const int wm = __reduce_max_sync(0xffffffffu, f2ord(xs[q]));
         if (lane == 0) sm.red[sb][warp][q] = ord2f(wm);
       }
       if (!sync()) break;
-      uint32_t phi[R / 4], plo[R / 4];
-      float m_use_t[R];
+      // ---------------------------------------------------- reference max, P, row sums
+      // rows whose reference moved: bit q (uniform: every thread reads the same maxima); their
+      // factors go to this warp's alpha row
+      uint32_t resc = 0;
 #pragma unroll
-      for (int q = 0; q < R; ++q) {
+      for (int q = 0; q < RV; ++q) {
         const float tmax = fmaxf(fmaxf(sm.red[sb][0][q], sm.red[sb][1][q]),
                                  fmaxf(sm.red[sb][2][q], sm.red[sb][3][q]));
-        const float m_new = fmaxf(m_run[q], tmax);
-        const float m_use = m_new == -INFINITY ? 0.f : m_new;
-        const float alpha = ex2(m_run[q] - m_use);
-        m_run[q] = m_new;
-        m_use_t[q] = m_use;
-        const float po = ex2(xo[q] - m_use);
-        l_part[q] = l_part[q] * alpha + 256.f * (vscaled ? ex2(xx[q] - m_use) : po);
-        xo[q] = 256.f * po;  // P is quantised as 256 p (l carries the same factor)
+        if (tmax > m_ref[q] + kRescaleLog2) {
+          const float a = m_ref[q] == -INFINITY ? 0.f : ex2(m_ref[q] - tmax);
+          m_ref[q] = tmax;
+          l_part[q] *= a;
+          resc |= 1u << q;
+          if (lane == 0) sm.alpha[warp][q] = a;
+        }
+        const float m_use = m_ref[q] == -INFINITY ? 0.f : m_ref[q];
+        const float pe = kPScale * ex2(xs[q] - m_use);
+        l_part[q] += vscaled ? kPScale * ex2(xs[q] - lv - m_use) : pe;
+        xs[q] = pe;
       }
+      // P^T row r: 2R bytes, hi rows then lo rows, as 16-byte planes of 16 columns
+      uint32_t words[R / 2];
 #pragma unroll
-      for (int w = 0; w < R / 4; ++w) {
-        const uint32_t a = pack_f16x2(xo[4 * w], xo[4 * w + 1]);
-        const uint32_t b = pack_f16x2(xo[4 * w + 2], xo[4 * w + 3]);
+      for (int w = 0; w < R / 2; ++w) words[w] = 0u;
+#pragma unroll
+      for (int w = 0; w < RV / 4; ++w) {
+        const uint32_t a = pack_f16x2(xs[4 * w], xs[4 * w + 1]);
+        const uint32_t b = pack_f16x2(xs[4 * w + 2], xs[4 * w + 3]);
         uint32_t ah, al, bh, bl;
         split_f16x2_e4m3(a, ah, al);
         split_f16x2_e4m3(b, bh, bl);
-        phi[w] = ah | (bh << 16);
-        plo[w] = al | (bl << 16);
+        words[w] = ah | (bh << 16);
+        words[R / 4 + w] = al | (bl << 16);
       }
-      // P buffer sb was last read by PV_{j-2}: wait for it, and fold it if it is this item's
-      if (j >= 2) {
-        if (!wait_pv(j - 2)) break;
-        if (j - 2 >= item_first_tile) fold(j - 2);
-      }
+      // O rescale (rare): O must be quiescent, i.e. the previous tile's PV done
+      if (resc && j > item_first_tile) {
+        __syncwarp();
+        if (!wait_pv(j - 1)) break;
 #pragma unroll
-      for (int q = 0; q < R; ++q) {
-        if (sb) m_hist[1][q] = m_use_t[q];
-        else m_hist[0][q] = m_use_t[q];
+        for (int c = 0; c < N; c += 16) {
+          float o16[16];
+          tc::ld16(o_tmem + c, o16);
+          tc::wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int q = (c + i) % R;
+            if (q < RV && ((resc >> q) & 1u)) o16[i] *= sm.alpha[warp][q];
+          }
+          tc::st16(o_tmem + c, o16);
+        }
+        tc::wait_st();
       }
-      // P^T row r: R == 8: [hi 0..7 | lo 0..7]; R == 16: plane 0 = hi 0..15, plane 1 = lo 0..15
-      if (R == 8) {
-        *reinterpret_cast<uint4*>(&sm.p2[sb][0][r * 16]) = make_uint4(phi[0], phi[1], plo[0], plo[1]);
-      } else {
-        *reinterpret_cast<uint4*>(&sm.p2[sb][0][r * 16]) =
-            make_uint4(phi[0], phi[1], phi[R / 4 - 2], phi[R / 4 - 1]);
-        *reinterpret_cast<uint4*>(&sm.p2[sb][NT - 1][r * 16]) =
-            make_uint4(plo[0], plo[1], plo[R / 4 - 2], plo[R / 4 - 1]);
-      }
+      // P buffer sb was last read by PV_{j-2}
+      if (j >= 2 && !wait_pv(j - 2)) break;
+#pragma unroll
+      for (int plane = 0; plane < NT; ++plane)
+        *reinterpret_cast<uint4*>(&sm.p2[sb][plane][r * 16]) =
+            make_uint4(words[4 * plane], words[4 * plane + 1], words[4 * plane + 2], words[4 * plane + 3]);
       if (!valid) {  // masked rows may hold any bytes (NaN codes): zero V's row
         uint4* vrow = reinterpret_cast<uint4*>(&sm.v[stage][r * 128]);
 #pragma unroll
@@ -739,46 +756,48 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
 
       if (flags & kLast) {
         // ------------------------------------------------ epilogue of the item
-        if (j - 1 >= item_first_tile) {
-          if (!wait_pv(j - 1)) break;
-          fold(j - 1);
-        }
         if (!wait_pv(j)) break;
-        fold(j);
+        float o[RV];
+#pragma unroll
+        for (int q = 0; q < RV; ++q) o[q] = 0.f;
+#pragma unroll
+        for (int c = 0; c < N; c += 16) {
+          float o16[16];
+          tc::ld16(o_tmem + c, o16);
+          tc::wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int q = (c + i) % R;
+            if (q < RV) o[q] += o16[i];
+          }
+        }
         tc::fence_before_sync();
 #pragma unroll
-        for (int q = 0; q < R; ++q) {
+        for (int q = 0; q < RV; ++q) {
           float l = l_part[q];
 #pragma unroll
           for (int off = 16; off > 0; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
           if (lane == 0) sm.redl[warp][q] = l;
         }
         if (!sync()) break;
-        float lsum[R];
-#pragma unroll
-        for (int q = 0; q < R; ++q)
-          lsum[q] = sm.redl[0][q] + sm.redl[1][q] + sm.redl[2][q] + sm.redl[3][q];
         const int d = r;  // output dim
-        if (nchunks == 1) {
 #pragma unroll
-          for (int q = 0; q < R; ++q) {
-            if (q >= rows) break;
+        for (int q = 0; q < RV; ++q) {
+          if (q >= rows) break;
+          const float lsum = sm.redl[0][q] + sm.redl[1][q] + sm.redl[2][q] + sm.redl[3][q];
+          if (nchunks == 1) {
             const int rr = rg * R + q;
             const int jj = rr / G, hh = kvh * G + (rr - jj * G);
-            __nv_bfloat16 v = out_round(o_acc[q] / fmaxf(lsum[q], 1e-10f));
+            __nv_bfloat16 v = out_round(o[q] / fmaxf(lsum, 1e-10f));
             p.out[static_cast<int64_t>(qrow0 + jj) * p.out_row_stride + hh * kHeadDim + d] =
                 *reinterpret_cast<uint16_t*>(&v);
-          }
-        } else {
-#pragma unroll
-          for (int q = 0; q < R; ++q) {
-            if (q >= rows) break;
+          } else {
             float* part = p.partials + (static_cast<int64_t>(item) * R + q) * (kHeadDim + 4);
-            part[d] = o_acc[q];
+            part[d] = o[q];
             if (d == 0) {
               // a chunk whose rows saw no key position carries no weight in the combine
-              part[kHeadDim] = lsum[q] > 0.f ? m_o[q] : -INFINITY;
-              part[kHeadDim + 1] = lsum[q];
+              part[kHeadDim] = lsum > 0.f ? m_ref[q] : -INFINITY;
+              part[kHeadDim + 1] = lsum;
             }
           }
         }
@@ -871,28 +890,28 @@ size_t decode_smem_bytes(int num_seqs) {
 }
 
 // Persistent grid for this launch: as many CTAs as fit on every SM (at most kMaxCtasPerSm; tensor
-// memory per CTA is at most 128 columns, so it never limits).
-template <int NT>
+// memory per CTA is at most 256 columns, so it never limits).
+template <int NT, int RV>
 int decode_grid_for(int num_seqs) {
   static bool configured[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !configured[dev]) {
-    cudaFuncSetAttribute(decode_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaFuncSetAttribute(decode_kernel<NT, RV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          static_cast<int>(decode_smem_bytes<NT>(kMaxSeqs)));
     // all of the unified L1/shared storage as shared memory: two CTAs' rings must fit
-    cudaFuncSetAttribute(decode_kernel<NT>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    cudaFuncSetAttribute(decode_kernel<NT, RV>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     configured[dev] = true;
   }
   // The occupancy calculator reports 1 for every kernel that allocates tensor memory, so the
   // CTAs per SM are counted from the resources themselves: shared memory (with the per-block
-  // reservation) and registers.  Tensor memory (at most 128 of 512 columns per CTA) never limits.
+  // reservation) and registers.  Tensor memory (at most 256 of 512 columns per CTA) never limits.
   // Were fewer CTAs resident, the extra ones would find the work counter exhausted and leave.
   int smem_sm = 0, resv = 0;
   cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
   cudaDeviceGetAttribute(&resv, cudaDevAttrReservedSharedMemoryPerBlock, dev);
   cudaFuncAttributes fa;
-  cudaFuncGetAttributes(&fa, decode_kernel<NT>);
+  cudaFuncGetAttributes(&fa, decode_kernel<NT, RV>);
   const int per_cta_smem = static_cast<int>(decode_smem_bytes<NT>(num_seqs)) + resv;
   int occ = per_cta_smem > 0 ? smem_sm / per_cta_smem : 1;
   const int by_regs = fa.numRegs > 0 ? 65536 / (fa.numRegs * kThreads) : 1;
@@ -908,8 +927,12 @@ int decode_grid(int nt) {
   return sm_count() * kMaxCtasPerSm;  // upper bound of any launch's grid (workspace sizing)
 }
 
-int decode_launch_grid(int nt, int num_seqs) {
-  return nt == 1 ? decode_grid_for<1>(num_seqs) : decode_grid_for<2>(num_seqs);
+int decode_launch_grid(int nt, int rv, int num_seqs) {
+  switch (nt) {
+    case 1: return rv <= 4 ? decode_grid_for<1, 4>(num_seqs) : decode_grid_for<1, 8>(num_seqs);
+    case 2: return decode_grid_for<2, 16>(num_seqs);
+    default: return decode_grid_for<3, 24>(num_seqs);
+  }
 }
 
 int64_t decode_max_items(int64_t pairs, int grid) {
@@ -924,18 +947,27 @@ int64_t decode_workspace_bytes(int num_seqs, int num_kv_heads, int max_rowgroups
   return bytes;
 }
 
-cudaError_t launch_decode(const DecodeParams& p, int nt, const CUtensorMap& tmk,
+namespace {
+template <int NT, int RV>
+void launch_variant(const DecodeParams& p, const CUtensorMap& tmk, const CUtensorMap& tmv,
+                    int cgrid, cudaStream_t stream) {
+  const int grid = decode_grid_for<NT, RV>(p.num_seqs);
+  decode_kernel<NT, RV><<<grid, kThreads, decode_smem_bytes<NT>(p.num_seqs), stream>>>(tmk, tmv, p);
+  if (cgrid > 0) combine_kernel<NT><<<cgrid, kHeadDim, 0, stream>>>(p);
+}
+}  // namespace
+
+cudaError_t launch_decode(const DecodeParams& p, int nt, int rv, const CUtensorMap& tmk,
                           const CUtensorMap& tmv, cudaStream_t stream) {
   const int64_t pairs = static_cast<int64_t>(p.num_seqs) * p.num_kv_heads * p.max_rowgroups;
   const int cgrid = static_cast<int>(pairs < 8LL * sm_count() ? pairs : 8LL * sm_count());
-  if (nt == 1) {
-    const int grid = decode_grid_for<1>(p.num_seqs);
-    decode_kernel<1><<<grid, kThreads, decode_smem_bytes<1>(p.num_seqs), stream>>>(tmk, tmv, p);
-    if (cgrid > 0) combine_kernel<1><<<cgrid, kHeadDim, 0, stream>>>(p);
-  } else {
-    const int grid = decode_grid_for<2>(p.num_seqs);
-    decode_kernel<2><<<grid, kThreads, decode_smem_bytes<2>(p.num_seqs), stream>>>(tmk, tmv, p);
-    if (cgrid > 0) combine_kernel<2><<<cgrid, kHeadDim, 0, stream>>>(p);
+  switch (nt) {
+    case 1:
+      if (rv <= 4) launch_variant<1, 4>(p, tmk, tmv, cgrid, stream);
+      else launch_variant<1, 8>(p, tmk, tmv, cgrid, stream);
+      break;
+    case 2: launch_variant<2, 16>(p, tmk, tmv, cgrid, stream); break;
+    default: launch_variant<3, 24>(p, tmk, tmv, cgrid, stream); break;
   }
   return cudaGetLastError();
 }

@@ -73,9 +73,11 @@ int64_t decode_workspace_bytes(int num_seqs, int num_kv_heads, int max_rowgroups
 int64_t decode_max_items(int64_t pairs, int grid);
 // Grid (persistent CTAs) the decode engine uses on the current device for the given width.
 int decode_grid(int nt);
+// Engine variants: nt = 8-row planes per row group (R = 8 nt rows, 1..3), rv = rows the
+// softmax processes (4 or R).
 // Grid an actual launch uses (persistent CTAs resident at once) for this batch size.
-int decode_launch_grid(int nt, int num_seqs);
-cudaError_t launch_decode(const DecodeParams& p, int nt, const CUtensorMap& tmk,
+int decode_launch_grid(int nt, int rv, int num_seqs);
+cudaError_t launch_decode(const DecodeParams& p, int nt, int rv, const CUtensorMap& tmk,
                           const CUtensorMap& tmv, cudaStream_t stream);
 
 // ------------------------------------------------------------------ prefill engine
