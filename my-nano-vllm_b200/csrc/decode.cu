@@ -9,15 +9,18 @@
 // times the sequence's query tokens in spec mode), so each K/V byte is read from HBM once per
 // row group -- once in total for decode.  Every CTA first computes the same plan from the
 // sequence lengths (chunk size, item prefix sums in shared memory), then a persistent grid pulls
-// items from an atomic counter.  Chunks of one (sequence, kv head, row group) are consecutive
-// items; their partial results are combined by whichever CTA finishes the pair's last chunk
-// (atomic ticket): no second launch and no spinning.
+// items from an atomic counter.  An item whose (sequence, kv head, row group) has more than one
+// chunk writes an unnormalised partial (O, reference max, row sum); combine_kernel, launched
+// after, merges them using the plan CTA 0 publishes.
 //
-// One CTA per SM, six warps:
-//   warp 4  producer: walks the items, looks block ids up in block_tables, issues TMA loads of
-//           128-token K and V tiles (128-byte rows, 128B swizzle) into a 4-deep ring, and
-//           prepares each item's query rows as e4m3 hi + lo pairs (q scaled by a power of two per
-//           row, about 8 significant bits in total);
+// Two CTAs per SM, eight warps each (warps 6-7 have no role; they balance the register file
+// across the four schedulers):
+//   warp 4  producer: walks the items (the next one claimed and its block-table window and query
+//           rows prefetched one item ahead), writes a 16-word tile header one word per lane,
+//           and issues TMA loads of 128-token K and V tiles (128-byte rows, 128B swizzle; one
+//           lane per box) into a 3-deep ring (2-deep for wider row groups); per item it prepares
+//           the query rows as e4m3 hi + lo pairs (q scaled by a power of two per row, about 8
+//           significant bits in total);
 //   warp 5  MMA issuer (one thread), per tile j:
 //             S^T[128 tok x 2R]  = K_j . [Qhi; Qlo]^T          tcgen05.mma kind::f8f6f4 (e4m3)
 //             O^T[128 dim x 2R] += V_{j-1}^T . [Phi; Plo]^T    (V read MN-major from its tile)
@@ -49,21 +52,16 @@ constexpr int kItemsPerCta = 16;  // plan target: work items per CTA
 
 enum : int { kFirst = 1, kLast = 2 };
 
-struct TileHeader {
-  int item;  // < 0: no more work
-  int seq, kvh, rg;
-  int tok0;    // key position of the tile's first row
-  int nvalid;  // rows of the tile inside the chunk
-  int flags;
-  int nchunks;
-  int pair_first;  // item id of the pair's chunk 0
-  int pair_stride; // item ids of the pair's chunks are pair_first + c * pair_stride
-  int qrow0;       // first query token row of the sequence
-  int rows;        // valid query rows in this row group
-  int qslot;
-  int lim_base;              // causal limit of the row group's first query token
-  int blk[kMaxBoxes];        // physical block of each box (-1: masked)
-  int slot0[kMaxBoxes];      // cache row of each box's first token
+// Per-tile header, written by the producer one word per lane: item (< 0: no more work), key
+// position of the tile's first row, rows inside the chunk, flags | q slot << 4, then per box the
+// cache row of its first token (-1: masked block or no box).
+enum : int { kHdrItem = 0, kHdrTok0 = 1, kHdrValid = 2, kHdrFlags = 3, kHdrSlot0 = 4,
+             kHdrWords = 16 };
+static_assert(kHdrSlot0 + kMaxBoxes <= kHdrWords, "header");
+
+// Per-item facts the softmax epilogue needs, by q slot (written with the item's Q operand).
+struct ItemInfo {
+  int kvh, rg, nchunks, qrow0, rows;
 };
 
 template <int NT>
@@ -81,7 +79,8 @@ struct __align__(1024) DecodeSmem {
   float alpha[4][R];                      // per-warp copy of a tile's rescale factors (rare)
   float red[2][4][R];                     // cross-warp row maxima, double-buffered by tile
   float redl[4][R];                       // cross-warp row sums (epilogue)
-  TileHeader hdr[STAGES];
+  alignas(16) int hdr[STAGES][kHdrWords];
+  ItemInfo iinfo[2];
   uint64_t kv_full[STAGES];
   uint64_t kv_empty[STAGES];
   uint64_t s_full[2];
@@ -157,7 +156,6 @@ struct Cursor {
   int next;  // prefetched id of the following item (lane 0 holds the atomic's result)
   int b, kvh, rg, c, nchunks, t0, t1, t;
   int qrow0, rows, lim_base, row0;
-  int pair_first, pair_stride;
   int nth;           // items started (selects the q buffer)
   int ebase, myent;  // block-table entries ebase .. ebase+31, one per lane
 };
@@ -190,8 +188,6 @@ __device__ __forceinline__ void cursor_set(Cursor<NT>& P, int item, const Decode
   P.kvh = pair_local / nrg;
   P.rg = pair_local - P.kvh * nrg;
   P.c = c;
-  P.pair_first = prefix[b] + pair_local;
-  P.pair_stride = npairs;
   P.nchunks = nchunks;
   P.t0 = c * CT;
   P.t1 = min(L, P.t0 + CT);
@@ -446,10 +442,29 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
     int stage = 0;
     uint32_t phase = 0;
     const int box_rows = p.box_rows;
+    const int box_shift = 31 - __clz(box_rows);
+    // lane l: cache row of the current item's box boxbase + l (-1: masked block / past the end),
+    // computed once per 32 boxes from the block-table window the cursor prefetched
+    int myslot = -1, boxbase = 0;
+    auto compute_boxes = [&](int base) {
+      const int e0 = (P.t0 + (base << box_shift)) / p.block_size;
+      if (e0 != P.ebase) {  // beyond the prefetched window (items of more than 32 boxes)
+        P.ebase = e0;
+        const int idx = e0 + lane;
+        P.myent = idx < p.max_blocks
+                      ? __ldg(p.block_tables + static_cast<int64_t>(P.b) * p.bt_stride + idx) : -1;
+      }
+      const int pos = P.t0 + ((base + lane) << box_shift);
+      const int e = pos / p.block_size;
+      const int blk = __shfl_sync(0xffffffffu, P.myent, (e - P.ebase) & 31);
+      myslot = (pos >= P.t1 || blk < 0 || blk >= p.num_blocks) ? -1
+                                                               : blk * p.block_size + (pos - e * p.block_size);
+      boxbase = base;
+    };
     while (true) {
       if (P.item >= total_items) {
         if (mbar_wait(&sm.kv_empty[stage], phase ^ 1, p.ctrl) && lane == 0) {
-          sm.hdr[stage].item = -1;
+          sm.hdr[stage][kHdrItem] = -1;
           mbar_arrive(&sm.kv_full[stage]);
         }
         break;
@@ -458,70 +473,44 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
       if (P.t == P.t0) {
         if (!mbar_wait(&sm.q_empty[slot], ((P.nth >> 1) & 1) ^ 1, p.ctrl)) break;
         prepare_q<NT>(P, slot, p, sm, lane);
+        if (lane < 5) {
+          const int v = lane == 0 ? P.kvh : lane == 1 ? P.rg : lane == 2 ? P.nchunks
+                                    : lane == 3 ? P.qrow0 : P.rows;
+          reinterpret_cast<int*>(&sm.iinfo[slot])[lane] = v;
+        }
         fence_proxy_async_smem();
         mbar_arrive(&sm.q_full[slot]);
         // the staging rows were read into registers above (their uses are issued): reuse it
         if (Pn.item < total_items) stage_q<NT>(Pn, p, sm.qstage);
+        compute_boxes(0);
       }
       if (!mbar_wait(&sm.kv_empty[stage], phase ^ 1, p.ctrl)) break;
       const int t = P.t;
       const int nvalid = min(kTile, P.t1 - t);
-      const int nbox = (nvalid + box_rows - 1) / box_rows;
-      const int64_t bt_row = static_cast<int64_t>(P.b) * p.bt_stride;
-      int blks[kMaxBoxes], slots[kMaxBoxes];
-#pragma unroll
-      for (int j = 0; j < kMaxBoxes; ++j) {
-        blks[j] = -1;
-        slots[j] = 0;
-        if (j < nbox) {
-          const int pos = t + j * box_rows;
-          const int e = pos / p.block_size;
-          if (e < P.ebase || e >= P.ebase + 32) {
-            P.ebase = e;
-            const int idx = e + lane;
-            P.myent = idx < p.max_blocks ? __ldg(p.block_tables + bt_row + idx) : -1;
-          }
-          int blk = __shfl_sync(0xffffffffu, P.myent, e - P.ebase);
-          if (blk < 0 || blk >= p.num_blocks) blk = -1;
-          blks[j] = blk;
-          slots[j] = blk < 0 ? 0 : blk * p.block_size + (pos - e * p.block_size);
-        }
-      }
-      if (lane == 0) {
-        TileHeader& h = sm.hdr[stage];
-        h.item = P.item;
-        h.seq = P.b;
-        h.kvh = P.kvh;
-        h.rg = P.rg;
-        h.tok0 = t;
-        h.nvalid = nvalid;
-        h.flags = (t == P.t0 ? kFirst : 0) | (t + kTile >= P.t1 ? kLast : 0);
-        h.nchunks = P.nchunks;
-        h.pair_first = P.pair_first;
-        h.pair_stride = P.pair_stride;
-        h.qrow0 = P.qrow0;
-        h.rows = P.rows;
-        h.qslot = slot;
-        h.lim_base = P.lim_base;
-#pragma unroll
-        for (int j = 0; j < kMaxBoxes; ++j) {
-          h.blk[j] = blks[j];
-          h.slot0[j] = slots[j];
-        }
-        uint32_t bytes = 0;
-#pragma unroll
-        for (int j = 0; j < kMaxBoxes; ++j)
-          if (blks[j] >= 0) bytes += 2u * box_rows * kHeadDim;
-        mbar_arrive_expect_tx(&sm.kv_full[stage], bytes);
-      }
+      const int nbox = (nvalid + box_rows - 1) >> box_shift;
+      const int ib0 = (t - P.t0) >> box_shift;
+      if (ib0 + nbox > boxbase + 32) compute_boxes(ib0);
+      // header, one word per lane; lane 4 + j carries box j
+      const int jb = lane - kHdrSlot0;
+      const int bslot = __shfl_sync(0xffffffffu, myslot, (ib0 + jb - boxbase) & 31);
+      const bool boxok = jb >= 0 && jb < nbox && bslot >= 0;
+      const uint32_t okmask = __ballot_sync(0xffffffffu, boxok);
+      const int flags = (t == P.t0 ? kFirst : 0) | (t + kTile >= P.t1 ? kLast : 0) | (slot << 4);
+      const int hv = lane == kHdrItem ? P.item : lane == kHdrTok0 ? t : lane == kHdrValid ? nvalid
+                     : lane == kHdrFlags ? flags : (boxok ? bslot : -1);
+      if (lane < kHdrSlot0 + kMaxBoxes) sm.hdr[stage][lane] = hv;
+      if (lane == 0)
+        mbar_arrive_expect_tx(&sm.kv_full[stage], __popc(okmask) * 2u * box_rows * kHeadDim);
       __syncwarp();
-      if (lane < 2) {  // lane 0 loads the K boxes, lane 1 the V boxes, side by side
-        const CUtensorMap* map = lane == 0 ? &tmk : &tmv;
-        uint8_t* dst = lane == 0 ? &sm.k[stage][0] : &sm.v[stage][0];
-#pragma unroll
-        for (int j = 0; j < kMaxBoxes; ++j)
-          if (blks[j] >= 0)
-            tma_load_2d(dst + j * box_rows * kHeadDim, map, &sm.kv_full[stage], P.kvh * kHeadDim, slots[j]);
+      // lane 2j loads K box j, lane 2j + 1 V box j
+      {
+        const int tj = lane >> 1;
+        const int tslot = __shfl_sync(0xffffffffu, hv, (kHdrSlot0 + tj) & 31);
+        if (tj < nbox && tj < kMaxBoxes && tslot >= 0) {
+          const bool is_v = lane & 1;
+          tma_load_2d((is_v ? &sm.v[stage][0] : &sm.k[stage][0]) + tj * box_rows * kHeadDim,
+                      is_v ? &tmv : &tmk, &sm.kv_full[stage], P.kvh * kHeadDim, tslot);
+        }
       }
       __syncwarp();
       if (++stage == kStages) { stage = 0; phase ^= 1; }
@@ -569,11 +558,11 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
       };
       while (true) {
         if (!mbar_wait(&sm.kv_full[stage], phase, p.ctrl)) break;
-        const TileHeader& h = sm.hdr[stage];
-        if (h.item < 0) break;
-        const int first = h.flags & kFirst;
-        const int last = h.flags & kLast;
-        const int slot = h.qslot;
+        if (sm.hdr[stage][kHdrItem] < 0) break;
+        const int hflags = sm.hdr[stage][kHdrFlags];
+        const int first = hflags & kFirst;
+        const int last = hflags & kLast;
+        const int slot = hflags >> 4;
         if (first) {
           if (!mbar_wait(&sm.q_full[slot], qcount[slot] & 1, p.ctrl)) break;
           qcount[slot]++;
@@ -617,6 +606,11 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
     constexpr float kRescaleLog2 = 4.f;  // P = 16 * 2^(s - m_ref) <= 256 < 448 (e4m3 max)
     constexpr float kPScale = 16.f;
     float m_ref[RV], l_part[RV];
+    // up to 8 live rows keep their score multiplier and causal limit in registers
+    constexpr bool kRowRegs = RV <= 8;
+    float cs_r[kRowRegs ? RV : 1];
+    int lim_r[kRowRegs ? RV : 1];
+    int kvh = 0;
     int stage = 0, j = 0, sync_uses = 0, item_first_tile = 0;
     uint32_t phase = 0;
     int qcount[2] = {0, 0};
@@ -633,26 +627,27 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
     const uint32_t o_tmem = tmem + lane_base + 2 * N;
     while (true) {
       if (!mbar_wait(&sm.kv_full[stage], phase, p.ctrl)) break;
-      const TileHeader& h = sm.hdr[stage];
-      const int item = h.item;
-      if (item < 0) break;
       // everything this tile needs from its header, read now: once P is handed over, the PV
       // completes, the stage is released and the producer rewrites the header
-      const int flags = h.flags, nvalid = h.nvalid, tok0 = h.tok0, slot = h.qslot;
-      const int rows = h.rows, nchunks = h.nchunks, rg = h.rg, kvh = h.kvh;
-      const int qrow0 = h.qrow0;
-      const int box = r >> box_shift;
-      const int bb = h.blk[box];
-      const int slot0 = h.slot0[box];
-      const bool valid = r < nvalid && bb >= 0;
+      const int4 hw = *reinterpret_cast<const int4*>(&sm.hdr[stage][0]);
+      const int item = hw.x;
+      if (item < 0) break;
+      const int tok0 = hw.y, nvalid = hw.z, flags = hw.w & 15, slot = hw.w >> 4;
+      const int slot0 = sm.hdr[stage][kHdrSlot0 + (r >> box_shift)];
+      const bool valid = r < nvalid && slot0 >= 0;
       if (flags & kFirst) {
         if (!mbar_wait(&sm.q_full[slot], qcount[slot] & 1, p.ctrl)) break;
         qcount[slot]++;
         item_first_tile = j;
+        kvh = sm.iinfo[slot].kvh;
 #pragma unroll
         for (int q = 0; q < RV; ++q) {
           m_ref[q] = -INFINITY;
           l_part[q] = 0.f;
+          if constexpr (kRowRegs) {
+            cs_r[q] = sm.qscale[slot][q];
+            lim_r[q] = sm.qlim[slot][q];
+          }
         }
       }
       float ks = 1.f, lv = 0.f;
@@ -680,8 +675,10 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
       float xs[RV];  // score (log2 units) + log2 of the value scale: P's exponent
 #pragma unroll
       for (int q = 0; q < RV; ++q) {
-        float sc = (x[q] + x[R + q]) * sm.qscale[slot][q] * ks;
-        if (!(valid && pos <= sm.qlim[slot][q])) sc = -INFINITY;
+        const float csq = kRowRegs ? cs_r[kRowRegs ? q : 0] : sm.qscale[slot][q];
+        const int limq = kRowRegs ? lim_r[kRowRegs ? q : 0] : sm.qlim[slot][q];
+        float sc = (x[q] + x[R + q]) * csq * ks;
+        if (!(valid && pos <= limq)) sc = -INFINITY;
         xs[q] = sc + lv;
         const int wm = __reduce_max_sync(0xffffffffu, f2ord(xs[q]));
         if (lane == 0) sm.red[sb][warp][q] = ord2f(wm);
@@ -780,6 +777,8 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
           if (lane == 0) sm.redl[warp][q] = l;
         }
         if (!sync()) break;
+        const ItemInfo ii = sm.iinfo[slot];
+        const int rows = ii.rows, nchunks = ii.nchunks, rg = ii.rg, qrow0 = ii.qrow0;
         const int d = r;  // output dim
 #pragma unroll
         for (int q = 0; q < RV; ++q) {
