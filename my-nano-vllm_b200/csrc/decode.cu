@@ -78,6 +78,7 @@ struct __align__(1024) DecodeSmem {
   uint8_t qstage[R * 256];                // raw bf16 query rows of the next item (cp.async)
   float alpha[4][R];                      // per-warp copy of a tile's rescale factors (rare)
   float red[2][4][R];                     // cross-warp row maxima, double-buffered by tile
+  alignas(16) int vote[2][4];             // per warp: a score above its row's reference + 2^4
   float redl[4][R];                       // cross-warp row sums (epilogue)
   alignas(16) int hdr[STAGES][kHdrWords];
   ItemInfo iinfo[2];
@@ -673,6 +674,7 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
       mbar_arrive(&sm.s_empty[sb]);
       const int pos = tok0 + r;
       float xs[RV];  // score (log2 units) + log2 of the value scale: P's exponent
+      bool over = false;  // a score the current reference cannot take (P would pass 256)
 #pragma unroll
       for (int q = 0; q < RV; ++q) {
         const float csq = kRowRegs ? cs_r[kRowRegs ? q : 0] : sm.qscale[slot][q];
@@ -680,25 +682,38 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
         float sc = (x[q] + x[R + q]) * csq * ks;
         if (!(valid && pos <= limq)) sc = -INFINITY;
         xs[q] = sc + lv;
-        const int wm = __reduce_max_sync(0xffffffffu, f2ord(xs[q]));
-        if (lane == 0) sm.red[sb][warp][q] = ord2f(wm);
+        over |= xs[q] > m_ref[q] + kRescaleLog2;
       }
+      // one vote per warp; the exact per-row maxima are exchanged only when some warp needs a
+      // new reference (an item's first tile, and rare growth after it)
+      const bool wover = __any_sync(0xffffffffu, over);
+      if (lane == 0) sm.vote[sb][warp] = wover ? 1 : 0;
       if (!sync()) break;
-      // ---------------------------------------------------- reference max, P, row sums
-      // rows whose reference moved: bit q (uniform: every thread reads the same maxima); their
-      // factors go to this warp's alpha row
-      uint32_t resc = 0;
+      const int4 votes = *reinterpret_cast<const int4*>(&sm.vote[sb][0]);
+      uint32_t resc = 0;  // rows whose reference moved (uniform); factors in this warp's alpha row
+      if (votes.x | votes.y | votes.z | votes.w) {
+#pragma unroll
+        for (int q = 0; q < RV; ++q) {
+          const int wm = __reduce_max_sync(0xffffffffu, f2ord(xs[q]));
+          if (lane == 0) sm.red[sb][warp][q] = ord2f(wm);
+        }
+        if (!sync()) break;
+#pragma unroll
+        for (int q = 0; q < RV; ++q) {
+          const float tmax = fmaxf(fmaxf(sm.red[sb][0][q], sm.red[sb][1][q]),
+                                   fmaxf(sm.red[sb][2][q], sm.red[sb][3][q]));
+          if (tmax > m_ref[q] + kRescaleLog2) {
+            const float a = m_ref[q] == -INFINITY ? 0.f : ex2(m_ref[q] - tmax);
+            m_ref[q] = tmax;
+            l_part[q] *= a;
+            resc |= 1u << q;
+            if (lane == 0) sm.alpha[warp][q] = a;
+          }
+        }
+      }
+      // ---------------------------------------------------- P and row sums
 #pragma unroll
       for (int q = 0; q < RV; ++q) {
-        const float tmax = fmaxf(fmaxf(sm.red[sb][0][q], sm.red[sb][1][q]),
-                                 fmaxf(sm.red[sb][2][q], sm.red[sb][3][q]));
-        if (tmax > m_ref[q] + kRescaleLog2) {
-          const float a = m_ref[q] == -INFINITY ? 0.f : ex2(m_ref[q] - tmax);
-          m_ref[q] = tmax;
-          l_part[q] *= a;
-          resc |= 1u << q;
-          if (lane == 0) sm.alpha[warp][q] = a;
-        }
         const float m_use = m_ref[q] == -INFINITY ? 0.f : m_ref[q];
         const float pe = kPScale * ex2(xs[q] - m_use);
         l_part[q] += vscaled ? kPScale * ex2(xs[q] - lv - m_use) : pe;
