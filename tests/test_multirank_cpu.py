@@ -1,0 +1,73 @@
+"""KV-head-group sharding (two gloo ranks on CPU): each rank computes attention for its own kv
+heads with no collective in the path; gathering the per-rank outputs along the head axis gives
+the unsharded result exactly (heads never interact)."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from nanovllm_b200 import shard
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _case(seed):
+    from nanovllm_b200 import workloads
+    return workloads.decode_case(5, 16, 4, 1, 300, seed=seed, block_size=32, pool_factor=1.3)
+
+
+def _rank_main(rank, world, port, results):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from oracle import attention as oatt
+        c = _case(11)
+        kvh = c.k_cache.shape[2]
+        q = shard.shard_q(c.q, kvh, rank, world).contiguous()
+        kc = shard.shard_cache(c.k_cache.view(torch.uint8), rank, world)
+        vc = shard.shard_cache(c.v_cache.view(torch.uint8), rank, world)
+        out = oatt.decode(q, kc, vc, c.block_tables, c.context_lens, c.scale)
+        # the gather is the test's, standing in for the engine's o_proj all-reduce
+        parts = [torch.empty_like(out.float()) for _ in range(world)]
+        dist.all_gather(parts, out.float())
+        if rank == 0:
+            results.put(torch.cat(parts, dim=1))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_kv_head_shards_reassemble_the_unsharded_output():
+    from oracle import attention as oatt
+    world = 2
+    ctx = mp.get_context("spawn")
+    results = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, results)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = results.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    c = _case(11)
+    ref = oatt.decode(c.q, c.k_cache.view(torch.uint8), c.v_cache.view(torch.uint8),
+                      c.block_tables, c.context_lens, c.scale).float()
+    assert torch.equal(got, ref)
+
+
+def test_head_ranges():
+    assert shard.kv_head_range(8, 3, 4) == (6, 8)
+    assert shard.q_head_range(64, 8, 1, 8) == (8, 16)
+    assert shard.q_head_range(32, 8, 0, 2) == (0, 16)
+    with pytest.raises(ValueError):
+        shard.kv_head_range(8, 0, 3)
+    with pytest.raises(ValueError):
+        shard.kv_head_range(8, 2, 2)
