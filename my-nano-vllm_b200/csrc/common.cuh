@@ -194,6 +194,23 @@ __device__ __forceinline__ void split_f16x2_e4m3(uint32_t x, uint32_t& hi, uint3
   lo = f16x2_to_e4m3x2(*reinterpret_cast<const uint32_t*>(&r));
 }
 
+// Value of a non-negative e4m3 byte (bits 0-6 of b; the sign bit must be clear) as fp32, with
+// integer and one multiply instead of a conversion: the 7 exponent+mantissa bits placed at
+// fp32 bits 20-26 read as 2^(e-127)(1 + m/8) (or m 2^-130 for e = 0), and 2^120 rebiases that
+// to e4m3's 2^(e-7)(1 + m/8) (m 2^-9): exact for normals and subnormals (mul.rn, no flush).
+__device__ __forceinline__ float e4m3_pos_to_f32(uint32_t b) {
+  float y;
+  asm("mul.rn.f32 %0, %1, 0f7B800000;" : "=f"(y) : "f"(__uint_as_float((b & 0x7Fu) << 20)));
+  return y;
+}
+
+// Two non-negative floats -> e4m3 hi and lo pairs (a -> low bytes) with a ~= hi + lo: hi =
+// e4m3(a), lo = e4m3(a - hi), about 8 significant bits; two conversions per pair.
+__device__ __forceinline__ void split_pos_f32x2_e4m3(float a, float b, uint32_t& hi, uint32_t& lo) {
+  hi = f32x2_to_e4m3x2(a, b);
+  lo = f32x2_to_e4m3x2(a - e4m3_pos_to_f32(hi), b - e4m3_pos_to_f32(hi >> 8));
+}
+
 // (lo, hi) floats -> f16x2 with lo in the low half; round to nearest even.
 __device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
   __half2 h = __floats2half2_rn(lo, hi);

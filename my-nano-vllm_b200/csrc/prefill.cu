@@ -8,18 +8,20 @@
 // block_tables (first max_num_blocks columns visited, :281) or from contiguous [Tk, KVH, 128]
 // rows starting at cu_k[s] (:254-263); rows with no visible key give 0 (:311).
 //
-// One CTA = one (q tile of 128 rows, q head, sequence).  Six warps:
-//   warps 0-3 softmax, thread = query row: converts its q row to e4m3 hi + lo (power-of-two row
-//             scale) at the start, then per key tile reads its row of S from tensor memory twice
-//             (max, then p), quantises P = 16 * 2^(s - m) as e4m3 hi + lo, and finally divides
-//             the tensor-memory O row by its sum.  O is rescaled only when a row maximum grows by
-//             more than 2^4 (P stays <= 256, inside e4m3's range);
-//   warp 4    TMA producer: 128-token K and V tiles (128-byte rows, 128B swizzle) into a 3-deep
+// One CTA = one (q tile of 128 rows, NG q heads of one kv head, sequence): NG = 2 when the GQA
+// group is even, so two softmax warpgroups share every K/V tile and take turns on the tensor
+// cores (while one quantises its P, the MMAs of the other run).  Warps:
+//   warps 4g..4g+3  softmax group g, thread = query row of head g: converts its q row to e4m3
+//             hi + lo (power-of-two row scale), then per key tile reads its row of S from tensor
+//             memory twice (max, then p), quantises P = 16 * 2^(s - m) as e4m3 hi + lo, and
+//             finally divides the tensor-memory O row by its sum.  O is rescaled only when a row
+//             maximum grows by more than 2^4 (P stays <= 256, inside e4m3's range);
+//   warp 4 NG       TMA producer: 128-token K and V tiles (128-byte rows, 128B swizzle) into the
 //             ring; key tiles past the causal limit of the q tile's last row are never loaded;
-//   warp 5    MMA issuer (one thread):
-//               S  = [Qhi; Qlo] . K^T   two accumulating kind::f8f6f4 chains, M = N = 128
-//               O += [Phi; Plo] . V     V is read MN-major straight from its TMA tile
-//             S double-buffered in tensor memory, P double-buffered in shared memory.
+//   warp 4 NG + 1   MMA issuer (one thread), per tile and group:
+//               S_g  = [Qhi_g; Qlo_g] . K^T   two accumulating kind::f8f6f4 chains, M = N = 128
+//               O_g += [Phi_g; Plo_g] . V     V is read MN-major straight from its TMA tile
+//             S_g and O_g in tensor memory, P_g in shared memory (one buffer per group).
 #include <climits>
 
 #include "common.cuh"
@@ -31,45 +33,51 @@ namespace {
 
 constexpr int kBM = 128;      // query rows per CTA
 constexpr int kBN = 128;      // key positions per tile
-constexpr int kStages = 3;
-constexpr int kThreads = 6 * 32;
-constexpr int kProducerWarp = 4;
-constexpr int kMmaWarp = 5;
 constexpr int kMaxBoxes = kBN / 16;
 constexpr float kRescaleLog2 = 4.f;  // lazy rescale threshold (log2 units)
-constexpr float kPScale = 16.f;      // P is quantised as 16 * 2^(s - m_ref) <= 16 * 2^4
+constexpr float kPScaleLog2 = 4.f;   // P is quantised as 16 * 2^(s - m_ref) <= 16 * 2^4
 
 struct PrefillTile {
   int j0;                     // first key position of the tile
   int blk[kMaxBoxes];         // paged: physical block of each box (-1: masked)
 };
 
-struct __align__(1024) PrefillSmem {
-  uint8_t qhi[kBM * 128];               // A operand of S: K-major SW128
-  uint8_t qlo[kBM * 128];
-  uint8_t k[kStages][kBN * 128];
-  uint8_t v[kStages][kBN * 128];
-  uint8_t phi[2][kBM * 128];            // A operand of PV, by tile parity
-  uint8_t plo[2][kBM * 128];
-  PrefillTile tile[kStages];
-  // general-path column table of the S buffer's tile (thread r fills column r): key and value
-  // scales, and a validity bit per column
-  float colk[2][kBN];
-  float colv[2][kBN];
-  uint32_t colok[2][kBN / 32];
-  uint64_t kv_full[kStages];
-  uint64_t kv_empty[kStages];
-  uint64_t q_full;
-  uint64_t s_full[2];
-  uint64_t s_empty[2];
-  uint64_t p_full[2];
-  uint64_t pv_done[2];
-  uint32_t tmem_base;
+template <int NG>
+struct PrefillCfg {
+  static constexpr int kStages = NG == 2 ? 2 : 3;
+  static constexpr int kThreads = (4 * NG + 2) * 32;
+  static constexpr int kProducerWarp = 4 * NG;
+  static constexpr int kMmaWarp = 4 * NG + 1;
+  // tensor memory: group g's S at 256 g, its O at 256 g + 128
+  static constexpr uint32_t kTmemCols = NG == 2 ? 512 : 256;
 };
 
-// Tensor-memory columns: S buffers at [0, 128) and [128, 256), O at [256, 384).
-constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColS0 = 0, kColO = 256;
+template <int NG>
+struct __align__(1024) PrefillSmem {
+  static constexpr int kStages = PrefillCfg<NG>::kStages;
+  uint8_t qhi[NG][kBM * 128];           // A operand of S: K-major SW128
+  uint8_t qlo[NG][kBM * 128];
+  uint8_t k[kStages][kBN * 128];
+  uint8_t v[kStages][kBN * 128];
+  uint8_t phi[NG][kBM * 128];           // A operand of PV
+  uint8_t plo[NG][kBM * 128];
+  PrefillTile tile[kStages];
+  // general-path column table of the group's current tile (thread r fills column r): key and
+  // value scales, and a validity bit per column
+  float colk[NG][kBN];
+  float colv[NG][kBN];
+  uint32_t colok[NG][kBN / 32];
+  uint64_t kv_full[kStages];
+  uint64_t kv_empty[kStages];
+  uint64_t q_full[NG];
+  uint64_t s_full[NG];
+  uint64_t s_empty[NG];
+  uint64_t p_full[NG];
+  uint64_t pv_done[NG];
+  uint32_t tmem_base;
+};
+static_assert(sizeof(PrefillSmem<2>) + 1024 <= 227 * 1024, "smem");
+static_assert(sizeof(PrefillSmem<1>) + 1024 <= 227 * 1024, "smem");
 
 struct SeqInfo {
   int q_begin, nq, k_begin, nk;
@@ -134,20 +142,27 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   }
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+__host__ __device__ constexpr int box_rows_of(bool paged, int bs) {
+  return paged ? (bs % 128 == 0 ? 128 : bs % 64 == 0 ? 64 : bs % 32 == 0 ? 32 : 16) : kBN;
+}
+
+template <int NG>
+__global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                    const PrefillParams p) {
+  using Cfg = PrefillCfg<NG>;
+  constexpr int kStages = Cfg::kStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  PrefillSmem& sm = *reinterpret_cast<PrefillSmem*>(
+  PrefillSmem<NG>& sm = *reinterpret_cast<PrefillSmem<NG>*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   // heavy tiles first: later q tiles see more keys
   const int qt = static_cast<int>(gridDim.x) - 1 - static_cast<int>(blockIdx.x);
-  const int h = blockIdx.y, s = blockIdx.z;
+  const int h0 = blockIdx.y * NG, s = blockIdx.z;  // q heads h0 .. h0 + NG - 1 share a kv head
   SeqInfo si;
   if (!seq_info(p, s, qt, si)) return;  // uniform across the CTA
   const int G = p.group;
-  const int kvh = h / G;
+  const int kvh = h0 / G;
   const int q0 = qt * kBM;
   const int rows = min(kBM, si.nq - q0);
 
@@ -156,21 +171,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&sm.kv_full[i], 1);
       mbar_init(&sm.kv_empty[i], 1);
     }
-    mbar_init(&sm.q_full, 128);
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&sm.s_full[i], 1);
-      mbar_init(&sm.s_empty[i], 128);
-      mbar_init(&sm.p_full[i], 128);
-      mbar_init(&sm.pv_done[i], 1);
+    for (int g = 0; g < NG; ++g) {
+      mbar_init(&sm.q_full[g], 128);
+      mbar_init(&sm.s_full[g], 1);
+      mbar_init(&sm.s_empty[g], 128);
+      mbar_init(&sm.p_full[g], 128);
+      mbar_init(&sm.pv_done[g], 1);
     }
     fence_mbar_init();
   }
-  if (warp == kProducerWarp && lane == 0) {
+  if (warp == Cfg::kProducerWarp && lane == 0) {
     prefetch_tensormap(&tmk);
     prefetch_tensormap(&tmv);
   }
-  if (warp == kMmaWarp) {
-    tc::tmem_alloc(&sm.tmem_base, kTmemCols);
+  if (warp == Cfg::kMmaWarp) {
+    tc::tmem_alloc(&sm.tmem_base, Cfg::kTmemCols);
     tc::tmem_relinquish();
   }
   tc::fence_before_sync();
@@ -179,12 +194,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = sm.tmem_base;
   const int ntiles = si.ntiles;
 
-  if (warp == kProducerWarp) {
+  if (warp == Cfg::kProducerWarp) {
     // ============================================================ TMA producer
     const bool paged = p.block_tables != nullptr;
     const int bs = p.block_size;
-    const int box_rows = paged ? (bs % 128 == 0 ? 128 : bs % 64 == 0 ? 64 : bs % 32 == 0 ? 32 : 16)
-                               : kBN;
+    const int box_rows = box_rows_of(paged, bs);
     const int nbox = kBN / box_rows;
     const int64_t bt_row = static_cast<int64_t>(s) * p.bt_stride;
     int ebase = INT_MIN / 2, myent = -1;
@@ -242,78 +256,87 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (++stage == kStages) { stage = 0; phase ^= 1; }
     }
-  } else if (warp == kMmaWarp) {
+  } else if (warp == Cfg::kMmaWarp) {
     // ============================================================ MMA issuer
+    // per tile j and group g in turn: S_g(j) once group g has read S_g(j-1), then PV_g(j-1)
+    // once P_g(j-1) is written; the stage of tile j-1 is released after every group's PV
     if (lane == 0 && ntiles > 0) {
       const uint32_t idesc_s = tc::idesc_e4m3(128, 128, false, false);
       const uint32_t idesc_pv = tc::idesc_e4m3(128, 128, false, true);
-      const uint32_t qh = smem_u32(sm.qhi), ql = smem_u32(sm.qlo);
-      bool ok = mbar_wait(&sm.q_full, 0, p.err);
+      bool ok = true;
+      for (int g = 0; g < NG && ok; ++g) ok = mbar_wait(&sm.q_full[g], 0, p.err);
       int stage = 0;
       uint32_t phase = 0;
       int prev_stage = 0;
-      auto issue_pv = [&](int jt, int st) -> bool {
-        const int b = jt & 1;
-        if (!mbar_wait(&sm.p_full[b], (jt >> 1) & 1, p.err)) return false;
+      auto issue_pv = [&](int g, int jt, int st) -> bool {
+        if (!mbar_wait(&sm.p_full[g], jt & 1, p.err)) return false;
         tc::fence_after_sync();
         const uint32_t va = smem_u32(&sm.v[st][0]);
-        const uint32_t pa[2] = {smem_u32(&sm.phi[b][0]), smem_u32(&sm.plo[b][0])};
+        const uint32_t pa[2] = {smem_u32(&sm.phi[g][0]), smem_u32(&sm.plo[g][0])};
 #pragma unroll
         for (int plane = 0; plane < 2; ++plane)
 #pragma unroll
           for (int ks = 0; ks < 4; ++ks) {
             const uint64_t ad = tc::smem_desc(pa[plane] + ks * 32, 16, 1024, tc::kSw128);
             const uint64_t bd = tc::smem_desc(va + ks * 32 * 128, 0, 1024, tc::kSw128);
-            tc::mma_f8(tmem + kColO, ad, bd, idesc_pv, (jt > 0 || plane > 0 || ks > 0) ? 1u : 0u);
+            tc::mma_f8(tmem + 256 * g + 128, ad, bd, idesc_pv, (jt > 0 || plane > 0 || ks > 0) ? 1u : 0u);
           }
-        tc::commit(&sm.kv_empty[st]);
-        tc::commit(&sm.pv_done[b]);
+        tc::commit(&sm.pv_done[g]);
         return true;
       };
       for (int j = 0; ok && j < ntiles; ++j) {
         if (!mbar_wait(&sm.kv_full[stage], phase, p.err)) break;
-        const int sb = j & 1;
-        if (!mbar_wait(&sm.s_empty[sb], ((j >> 1) & 1) ^ 1, p.err)) break;
-        tc::fence_after_sync();
         const uint32_t ka = smem_u32(&sm.k[stage][0]);
+        for (int g = 0; g < NG && ok; ++g) {
+          if (j > 0 && !mbar_wait(&sm.s_empty[g], (j - 1) & 1, p.err)) { ok = false; break; }
+          tc::fence_after_sync();
+          const uint32_t qh = smem_u32(&sm.qhi[g][0]), ql = smem_u32(&sm.qlo[g][0]);
 #pragma unroll
-        for (int plane = 0; plane < 2; ++plane)
+          for (int plane = 0; plane < 2; ++plane)
 #pragma unroll
-          for (int ks = 0; ks < 4; ++ks) {
-            const uint64_t ad = tc::smem_desc((plane ? ql : qh) + ks * 32, 16, 1024, tc::kSw128);
-            const uint64_t bd = tc::smem_desc(ka + ks * 32, 16, 1024, tc::kSw128);
-            tc::mma_f8(tmem + kColS0 + sb * 128, ad, bd, idesc_s, (plane > 0 || ks > 0) ? 1u : 0u);
-          }
-        tc::commit(&sm.s_full[sb]);
-        if (j > 0 && !issue_pv(j - 1, prev_stage)) { ok = false; break; }
+            for (int ks = 0; ks < 4; ++ks) {
+              const uint64_t ad = tc::smem_desc((plane ? ql : qh) + ks * 32, 16, 1024, tc::kSw128);
+              const uint64_t bd = tc::smem_desc(ka + ks * 32, 16, 1024, tc::kSw128);
+              tc::mma_f8(tmem + 256 * g, ad, bd, idesc_s, (plane > 0 || ks > 0) ? 1u : 0u);
+            }
+          tc::commit(&sm.s_full[g]);
+          if (j > 0 && !issue_pv(g, j - 1, prev_stage)) { ok = false; break; }
+        }
+        if (!ok) break;
+        if (j > 0) tc::commit(&sm.kv_empty[prev_stage]);
         prev_stage = stage;
         if (++stage == kStages) { stage = 0; phase ^= 1; }
       }
-      if (ok) issue_pv(ntiles - 1, prev_stage);
+      if (ok) {
+        for (int g = 0; g < NG && ok; ++g) ok = issue_pv(g, ntiles - 1, prev_stage);
+        if (ok) tc::commit(&sm.kv_empty[prev_stage]);
+      }
     }
     __syncwarp();
   } else {
-    // ============================================================ softmax warps 0-3
-    const int r = tid;               // query row within the tile
+    // ============================================================ softmax group g
+    const int g = warp >> 2;
+    const int h = h0 + g;
+    const int r = tid & 127;         // query row within the tile
     const bool row_ok = r < rows;
     const int qi = q0 + r;           // query index within the sequence
     const int lim = qi + (si.nk - si.nq);  // largest visible key position of this row
-    const uint32_t lane_base = static_cast<uint32_t>(32 * warp) << 16;
+    const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
+    const uint32_t s_tmem = tmem + lane_base + 256 * g;
+    const uint32_t o_tmem = s_tmem + 128;
+    uint8_t* const qhi = sm.qhi[g];
+    uint8_t* const qlo = sm.qlo[g];
+    uint8_t* const phi = sm.phi[g];
+    uint8_t* const plo = sm.plo[g];
     // ---- query row -> e4m3 hi / lo, 128B-swizzled K-major rows
     float cs;
     {
-      uint4 w[16];  // the row as packed bf16 pairs
-      if (row_ok) {
-        const uint4* src = reinterpret_cast<const uint4*>(
-            p.q + static_cast<int64_t>(si.q_begin + qi) * p.q_row_stride + static_cast<int64_t>(h) * 128);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) w[i] = __ldg(src + i);
-      } else {
-#pragma unroll
-        for (int i = 0; i < 16; ++i) w[i] = make_uint4(0, 0, 0, 0);
-      }
-      auto widen = [&](int i, float (&x)[8]) {
-        const uint32_t ww[4] = {w[i].x, w[i].y, w[i].z, w[i].w};
+      const uint4* src = reinterpret_cast<const uint4*>(
+          p.q + static_cast<int64_t>(si.q_begin + (row_ok ? qi : q0)) * p.q_row_stride +
+          static_cast<int64_t>(h) * 128);
+      auto load = [&](int i) -> uint4 { return row_ok ? __ldg(src + i) : make_uint4(0, 0, 0, 0); };
+      auto widen = [&](const uint4& w, float* x) {
+        const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           x[2 * k] = __uint_as_float(ww[k] << 16);
@@ -324,7 +347,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
         float x[8];
-        widen(i, x);
+        widen(load(i), x);
 #pragma unroll
         for (int k = 0; k < 8; ++k) amax = fmaxf(amax, fabsf(x[k]));
       }
@@ -332,29 +355,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float inv = pow2_inv_scale(amax, &srow);
       cs = srow * p.scale_log2;
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {  // 16 dims per 16-byte chunk
-        float x[16], a[8], b[8];
-        widen(2 * c, a);
-        widen(2 * c + 1, b);
+      for (int c = 0; c < 8; ++c) {  // 16 dims per 16-byte chunk (the row re-read from L1)
+        float x[16];
+        widen(load(2 * c), x);
+        widen(load(2 * c + 1), x + 8);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          x[k] = a[k] * inv;
-          x[8 + k] = b[k] * inv;
-        }
+        for (int k = 0; k < 16; ++k) x[k] *= inv;
         uint4 hv, lv;
         split16(x, hv, lv);
         const int off = r * 128 + ((c ^ (r & 7)) << 4);
-        *reinterpret_cast<uint4*>(&sm.qhi[off]) = hv;
-        *reinterpret_cast<uint4*>(&sm.qlo[off]) = lv;
+        *reinterpret_cast<uint4*>(&qhi[off]) = hv;
+        *reinterpret_cast<uint4*>(&qlo[off]) = lv;
       }
     }
     fence_proxy_async_smem();
-    mbar_arrive(&sm.q_full);
+    mbar_arrive(&sm.q_full[g]);
 
     const bool kscaled = p.k_scale != nullptr;
     const bool paged = p.block_tables != nullptr;
     const int bs = p.block_size;
-    const int box_rows = paged ? (bs % 128 == 0 ? 128 : bs % 64 == 0 ? 64 : bs % 32 == 0 ? 32 : 16) : kBN;
+    const int box_rows = box_rows_of(paged, bs);
+    const int box_shift = 31 - __clz(box_rows);
     float m_ref = -INFINITY;  // reference max of O and l (log2 units)
     float l = 0.f;
     int stage = 0;
@@ -372,17 +393,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int b = 0; b < kMaxBoxes; ++b)
           if (b * box_rows < kBN && sm.tile[stage].blk[b] >= 0) boxmask |= 1u << b;
       }
-      const int box_shift = 31 - __clz(box_rows);
       // columns [0, vlim) of this tile are visible to this row.  A tile with a masked block, or
       // any tile of a scaled cache, takes the general path through the column table (uniform
-      // across the four softmax warps)
+      // across the group's four warps)
       const int vlim = row_ok ? max(0, min(col_end, lim - j0 + 1)) : 0;
       const bool general = kscaled || !(p.scale_log2 > 0.f) || boxmask != (1u << (kBN / box_rows)) - 1u;
-      const int sb = j & 1;
-      if (!mbar_wait(&sm.s_full[sb], (j >> 1) & 1, p.err)) { ok = false; break; }
+      if (!mbar_wait(&sm.s_full[g], j & 1, p.err)) { ok = false; break; }
       tc::fence_after_sync();
       if (general) {
-        // S(j) complete => every softmax thread finished tile j-2, the last reader of table sb
+        // S_g(j) complete => the group finished tile j-1, the table's last reader
         const int c = r;
         const bool cok = c < col_end && ((boxmask >> (c >> box_shift)) & 1u);
         float ks = 1.f, vs = 1.f;
@@ -393,29 +412,38 @@ __global__ void __launch_bounds__(kThreads, 1)
           ks = __ldg(p.k_scale + slot * p.num_kv_heads + kvh);
           vs = __ldg(p.v_scale + slot * p.num_kv_heads + kvh);
         }
-        sm.colk[sb][c] = ks;
-        sm.colv[sb][c] = vs;
+        sm.colk[g][c] = ks;
+        sm.colv[g][c] = vs;
         const uint32_t bal = __ballot_sync(0xffffffffu, cok);
-        if (lane == 0) sm.colok[sb][warp] = bal;
-        named_barrier(1, 128);
+        if (lane == 0) sm.colok[g][warp & 3] = bal;
+        named_barrier(1 + g, 128);
       }
-      const uint32_t sc = tmem + lane_base + kColS0 + sb * 128;
       // ---- pass 1: row maximum (of the raw scores on the fast path: cs > 0 commutes with max)
       float tmax = -INFINITY;
 #pragma unroll 1
       for (int c0 = 0; c0 < kBN; c0 += 32) {
         float v[32];
-        tmem_ld32(sc + c0, v);
+        tmem_ld32(s_tmem + c0, v);
         tc::wait_ld();
-        if (!general) {
+        if (!general && c0 + 32 <= vlim) {  // every column visible: four independent chains
+          float a0 = v[0], a1 = v[1], a2 = v[2], a3 = v[3];
+#pragma unroll
+          for (int i = 4; i < 32; i += 4) {
+            a0 = fmaxf(a0, v[i]);
+            a1 = fmaxf(a1, v[i + 1]);
+            a2 = fmaxf(a2, v[i + 2]);
+            a3 = fmaxf(a3, v[i + 3]);
+          }
+          tmax = fmaxf(tmax, fmaxf(fmaxf(a0, a1), fmaxf(a2, a3)));
+        } else if (!general) {
 #pragma unroll
           for (int i = 0; i < 32; ++i) tmax = fmaxf(tmax, c0 + i < vlim ? v[i] : -INFINITY);
         } else {
-          const uint32_t okw = sm.colok[sb][c0 >> 5];
+          const uint32_t okw = sm.colok[g][c0 >> 5];
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             const bool cok = ((okw >> i) & 1u) && c0 + i < vlim;
-            tmax = fmaxf(tmax, cok ? v[i] * sm.colk[sb][c0 + i] * cs : -INFINITY);
+            tmax = fmaxf(tmax, cok ? v[i] * sm.colk[g][c0 + i] * cs : -INFINITY);
           }
         }
       }
@@ -428,65 +456,78 @@ __global__ void __launch_bounds__(kThreads, 1)
         m_ref = m_new;
         l *= alpha;
       }
-      const bool need_rescale = __any_sync(0xffffffffu, alpha != 1.f) && j > 0;
-      // O is quiescent once the previous tile's PV is done; P buffer sb was last read by PV(j-2)
-      // each warp rescales its own rows; a warp that waits here for PV(j-1) waits on the phase
-      // the other warps meet at tile j+1, and PV(j+1) cannot complete before this warp's P(j+1)
-      if (need_rescale) {
-        if (!mbar_wait(&sm.pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, p.err)) { ok = false; break; }
+      // O and the P buffer are free once PV_g(j-1) is done; each warp rescales its own rows
+      if (j >= 1) {
+        if (!mbar_wait(&sm.pv_done[g], (j - 1) & 1, p.err)) { ok = false; break; }
         tc::fence_after_sync();
-        const uint32_t oc = tmem + lane_base + kColO;
+      }
+      if (__any_sync(0xffffffffu, alpha != 1.f) && j > 0) {
 #pragma unroll
         for (int c0 = 0; c0 < 128; c0 += 16) {
           float o16[16];
-          tc::ld16(oc + c0, o16);
+          tc::ld16(o_tmem + c0, o16);
           tc::wait_ld();
 #pragma unroll
           for (int i = 0; i < 16; ++i) o16[i] *= alpha;
-          tc::st16(oc + c0, o16);
+          tc::st16(o_tmem + c0, o16);
         }
         tc::wait_st();
       }
-      if (j >= 2) {
-        if (!mbar_wait(&sm.pv_done[sb], ((j - 2) >> 1) & 1, p.err)) { ok = false; break; }
-      }
-      // ---- pass 2: P = 16 * 2^(s - m_ref) as e4m3 hi + lo, row sum
+      // ---- pass 2: P = 16 * 2^(s - m_ref) as e4m3 hi + lo; l sums the same 16 * 2^(s - m_ref)
       const float m_use = m_ref == -INFINITY ? 0.f : m_ref;
+      const float bias = kPScaleLog2 - m_use;  // the factor 16 folded into the exponent
 #pragma unroll 1
       for (int c0 = 0; c0 < kBN; c0 += 32) {
         float v[32];
-        tmem_ld32(sc + c0, v);
+        tmem_ld32(s_tmem + c0, v);
         tc::wait_ld();
-        if (!general) {
+        float la[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial sums
+        if (!general && c0 + 32 <= vlim) {
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
-            const float e = c0 + i < vlim ? ex2(fmaf(v[i], cs, -m_use)) : 0.f;
-            l += e;
-            v[i] = kPScale * e;
+            v[i] = ex2(fmaf(v[i], cs, bias));
+            la[i & 3] += v[i];
+          }
+        } else if (!general) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            v[i] = c0 + i < vlim ? ex2(fmaf(v[i], cs, bias)) : 0.f;
+            la[i & 3] += v[i];
           }
         } else {
-          const uint32_t okw = sm.colok[sb][c0 >> 5];
+          const uint32_t okw = sm.colok[g][c0 >> 5];
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             const bool cok = ((okw >> i) & 1u) && c0 + i < vlim;
-            const float e = cok ? ex2(v[i] * sm.colk[sb][c0 + i] * cs - m_use) : 0.f;
-            l += e;
-            v[i] = kPScale * e * sm.colv[sb][c0 + i];
+            const float e = cok ? ex2(v[i] * sm.colk[g][c0 + i] * cs + bias) : 0.f;
+            la[i & 3] += e;
+            v[i] = e * sm.colv[g][c0 + i];
           }
         }
+        l += (la[0] + la[1]) + (la[2] + la[3]);
+        // hi + lo split straight from fp32 (P >= 0)
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
-          uint4 hv, lv;
-          split16(&v[16 * half], hv, lv);
+          uint32_t hw[4], lw[4];
+#pragma unroll
+          for (int w = 0; w < 4; ++w) {
+            const float* x = &v[16 * half + 4 * w];
+            uint32_t ah, al, bh, bl;
+            split_pos_f32x2_e4m3(x[0], x[1], ah, al);
+            split_pos_f32x2_e4m3(x[2], x[3], bh, bl);
+            hw[w] = ah | (bh << 16);
+            lw[w] = al | (bl << 16);
+          }
           const int c = (c0 >> 4) + half;  // 16-byte chunk index within the 128-byte row
           const int off = r * 128 + ((c ^ (r & 7)) << 4);
-          *reinterpret_cast<uint4*>(&sm.phi[sb][off]) = hv;
-          *reinterpret_cast<uint4*>(&sm.plo[sb][off]) = lv;
+          *reinterpret_cast<uint4*>(&phi[off]) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+          *reinterpret_cast<uint4*>(&plo[off]) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
         }
       }
       tc::fence_before_sync();
-      mbar_arrive(&sm.s_empty[sb]);
+      mbar_arrive(&sm.s_empty[g]);
       // V rows of keys outside the sequence (or in masked blocks) may hold any bytes: zero them
+      // (every group does, before its own PV; the bytes written are the same zeros)
       {
         const int kr = r;  // this thread also owns key row kr of the tile
         const bool kv_ok = kr < col_end && ((boxmask >> (kr >> box_shift)) & 1u);
@@ -498,7 +539,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       fence_proxy_async_smem();
       tc::fence_before_sync();
-      mbar_arrive(&sm.p_full[sb]);
+      mbar_arrive(&sm.p_full[g]);
       if (++stage == kStages) { stage = 0; phase ^= 1; }
     }
     // ---- epilogue: O / l -> fp16 -> bf16 (the reference's output path)
@@ -509,15 +550,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     if (ntiles > 0 && ok) {
-      const int jl = ntiles - 1;
-      if (mbar_wait(&sm.pv_done[jl & 1], (jl >> 1) & 1, p.err)) {
+      if (mbar_wait(&sm.pv_done[g], (ntiles - 1) & 1, p.err)) {
         tc::fence_after_sync();
-        const uint32_t oc = tmem + lane_base + kColO;
-        const float inv = l > 0.f ? 1.f / (kPScale * l) : 0.f;
+        const float inv = l > 0.f ? 1.f / l : 0.f;  // O and l carry the same factor 16
 #pragma unroll
         for (int c0 = 0; c0 < 128; c0 += 16) {
           float o16[16];
-          tc::ld16(oc + c0, o16);
+          tc::ld16(o_tmem + c0, o16);
           tc::wait_ld();
           if (row_ok) {
             uint32_t pk[8];
@@ -540,7 +579,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
-  if (warp == kMmaWarp) tc::tmem_dealloc(tmem, kTmemCols);
+  if (warp == Cfg::kMmaWarp) tc::tmem_dealloc(tmem, Cfg::kTmemCols);
 }
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
@@ -574,30 +613,36 @@ bool make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t row_byte
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+template <int NG>
+cudaError_t launch_groups(const PrefillParams& p, const CUtensorMap& tmk, const CUtensorMap& tmv,
+                          cudaStream_t stream) {
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const size_t smem = sizeof(PrefillSmem<NG>) + 1024;
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    cudaFuncSetAttribute(prefill_kernel<NG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(smem));
+    configured[dev] = true;
+  }
+  const dim3 grid((p.max_seqlen_q + kBM - 1) / kBM, p.num_heads / NG, p.num_seqs);
+  prefill_kernel<NG><<<grid, PrefillCfg<NG>::kThreads, smem, stream>>>(tmk, tmv, p);
+  return cudaGetLastError();
+}
+
 }  // namespace
 
 cudaError_t launch_prefill(const PrefillParams& p, cudaStream_t stream) {
   const bool paged = p.block_tables != nullptr;
-  const int box_rows = paged ? (p.block_size % 128 == 0 ? 128 : p.block_size % 64 == 0 ? 64
-                                : p.block_size % 32 == 0 ? 32 : 16)
-                             : kBN;
+  const int box_rows = box_rows_of(paged, p.block_size);
   const int64_t rows = paged ? p.num_blocks * p.block_size : p.num_blocks;
   CUtensorMap tmk, tmv;
   if (!make_map(&tmk, p.k, rows, p.kv_row_stride, p.num_kv_heads, box_rows) ||
       !make_map(&tmv, p.v, rows, p.kv_row_stride, p.num_kv_heads, box_rows))
     return cudaErrorInvalidValue;
-  static bool configured[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  const size_t smem = sizeof(PrefillSmem) + 1024;
-  if (dev >= 0 && dev < 64 && !configured[dev]) {
-    cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         static_cast<int>(smem));
-    configured[dev] = true;
-  }
-  const dim3 grid((p.max_seqlen_q + kBM - 1) / kBM, p.num_heads, p.num_seqs);
-  prefill_kernel<<<grid, kThreads, smem, stream>>>(tmk, tmv, p);
-  return cudaGetLastError();
+  // two q heads of one kv head per CTA when the GQA group is even
+  return p.group % 2 == 0 ? launch_groups<2>(p, tmk, tmv, stream)
+                          : launch_groups<1>(p, tmk, tmv, stream);
 }
 
 }  // namespace fp8attn
