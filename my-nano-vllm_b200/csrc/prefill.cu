@@ -331,12 +331,18 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
     // ---- query row -> e4m3 hi / lo, 128B-swizzled K-major rows
     float cs;
     {
-      const uint4* src = reinterpret_cast<const uint4*>(
-          p.q + static_cast<int64_t>(si.q_begin + (row_ok ? qi : q0)) * p.q_row_stride +
-          static_cast<int64_t>(h) * 128);
-      auto load = [&](int i) -> uint4 { return row_ok ? __ldg(src + i) : make_uint4(0, 0, 0, 0); };
-      auto widen = [&](const uint4& w, float* x) {
-        const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+      uint4 w[16];  // the row as packed bf16 pairs, all 16 loads in flight at once
+      if (row_ok) {
+        const uint4* src = reinterpret_cast<const uint4*>(
+            p.q + static_cast<int64_t>(si.q_begin + qi) * p.q_row_stride + static_cast<int64_t>(h) * 128);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) w[i] = ldg_keep_v4(src + i);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) w[i] = make_uint4(0, 0, 0, 0);
+      }
+      auto widen = [&](const uint4& v, float* x) {
+        const uint32_t ww[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           x[2 * k] = __uint_as_float(ww[k] << 16);
@@ -347,7 +353,7 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
         float x[8];
-        widen(load(i), x);
+        widen(w[i], x);
 #pragma unroll
         for (int k = 0; k < 8; ++k) amax = fmaxf(amax, fabsf(x[k]));
       }
@@ -355,10 +361,10 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
       const float inv = pow2_inv_scale(amax, &srow);
       cs = srow * p.scale_log2;
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {  // 16 dims per 16-byte chunk (the row re-read from L1)
+      for (int c = 0; c < 8; ++c) {  // 16 dims per 16-byte chunk
         float x[16];
-        widen(load(2 * c), x);
-        widen(load(2 * c + 1), x + 8);
+        widen(w[2 * c], x);
+        widen(w[2 * c + 1], x + 8);
 #pragma unroll
         for (int k = 0; k < 16; ++k) x[k] *= inv;
         uint4 hv, lv;
