@@ -230,6 +230,13 @@ __device__ __forceinline__ float lg2(float x) {
   return y;
 }
 
+// 2^x on both halves of an f16x2 (one MUFU operation for two elements).
+__device__ __forceinline__ uint32_t ex2_f16x2(uint32_t x) {
+  uint32_t y;
+  asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));

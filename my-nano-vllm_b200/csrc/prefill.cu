@@ -487,21 +487,38 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
         float v[32];
         tmem_ld32(s_tmem + c0, v);
         tc::wait_ld();
-        float la[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial sums
-        if (!general && c0 + 32 <= vlim) {
+        uint32_t hw[8], lw[8];  // this chunk's P row: hi and lo e4m3 bytes, 4 per word
+        if (!general) {
+          // packed f16 pipeline: exponent argument (<= 8) to f16x2, one ex2 for two elements,
+          // split in f16x2, row sum in four f16x2 partials (values <= 256, four per partial)
+          __half2 lacc[4];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            v[i] = ex2(fmaf(v[i], cs, bias));
-            la[i & 3] += v[i];
-          }
-        } else if (!general) {
+          for (int k = 0; k < 4; ++k) lacc[k] = __float2half2_rn(0.f);
+          const bool full = c0 + 32 <= vlim;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            v[i] = c0 + i < vlim ? ex2(fmaf(v[i], cs, bias)) : 0.f;
-            la[i & 3] += v[i];
+          for (int k = 0; k < 16; ++k) {
+            float a0 = fmaf(v[2 * k], cs, bias), a1 = fmaf(v[2 * k + 1], cs, bias);
+            if (!full) {
+              a0 = c0 + 2 * k < vlim ? a0 : -INFINITY;
+              a1 = c0 + 2 * k + 1 < vlim ? a1 : -INFINITY;
+            }
+            const uint32_t pe = ex2_f16x2(pack_f16x2(a0, a1));
+            lacc[k & 3] = __hadd2(lacc[k & 3], *reinterpret_cast<const __half2*>(&pe));
+            uint32_t h2, l2;
+            split_f16x2_e4m3(pe, h2, l2);
+            if (k & 1) {
+              hw[k >> 1] |= h2 << 16;
+              lw[k >> 1] |= l2 << 16;
+            } else {
+              hw[k >> 1] = h2;
+              lw[k >> 1] = l2;
+            }
           }
+          const __half2 ls = __hadd2(__hadd2(lacc[0], lacc[1]), __hadd2(lacc[2], lacc[3]));
+          l += __low2float(ls) + __high2float(ls);
         } else {
           const uint32_t okw = sm.colok[g][c0 >> 5];
+          float la[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial sums
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             const bool cok = ((okw >> i) & 1u) && c0 + i < vlim;
@@ -509,25 +526,24 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
             la[i & 3] += e;
             v[i] = e * sm.colv[g][c0 + i];
           }
+          l += (la[0] + la[1]) + (la[2] + la[3]);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            uint32_t ah, al, bh, bl;
+            split_pos_f32x2_e4m3(v[4 * k], v[4 * k + 1], ah, al);
+            split_pos_f32x2_e4m3(v[4 * k + 2], v[4 * k + 3], bh, bl);
+            hw[k] = ah | (bh << 16);
+            lw[k] = al | (bl << 16);
+          }
         }
-        l += (la[0] + la[1]) + (la[2] + la[3]);
-        // hi + lo split straight from fp32 (P >= 0)
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
-          uint32_t hw[4], lw[4];
-#pragma unroll
-          for (int w = 0; w < 4; ++w) {
-            const float* x = &v[16 * half + 4 * w];
-            uint32_t ah, al, bh, bl;
-            split_pos_f32x2_e4m3(x[0], x[1], ah, al);
-            split_pos_f32x2_e4m3(x[2], x[3], bh, bl);
-            hw[w] = ah | (bh << 16);
-            lw[w] = al | (bl << 16);
-          }
           const int c = (c0 >> 4) + half;  // 16-byte chunk index within the 128-byte row
           const int off = r * 128 + ((c ^ (r & 7)) << 4);
-          *reinterpret_cast<uint4*>(&phi[off]) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-          *reinterpret_cast<uint4*>(&plo[off]) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+          *reinterpret_cast<uint4*>(&phi[off]) =
+              make_uint4(hw[4 * half], hw[4 * half + 1], hw[4 * half + 2], hw[4 * half + 3]);
+          *reinterpret_cast<uint4*>(&plo[off]) =
+              make_uint4(lw[4 * half], lw[4 * half + 1], lw[4 * half + 2], lw[4 * half + 3]);
         }
       }
       tc::fence_before_sync();
