@@ -39,6 +39,7 @@ constexpr float kPScaleLog2 = 4.f;   // P is quantised as 16 * 2^(s - m_ref) <= 
 
 struct PrefillTile {
   int j0;                     // first key position of the tile
+  uint32_t boxmask;           // boxes whose block is valid (contiguous layout: all)
   int blk[kMaxBoxes];         // paged: physical block of each box (-1: masked)
 };
 
@@ -229,12 +230,16 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
       if (lane == 0) {
         PrefillTile& t = sm.tile[stage];
         t.j0 = j0;
-        uint32_t bytes = 0;
+        uint32_t bytes = 0, mask = 0;
 #pragma unroll
         for (int b = 0; b < kMaxBoxes; ++b) {
           t.blk[b] = paged ? blks[b] : 0;
-          if (b < nbox && (!paged || blks[b] >= 0)) bytes += 2u * box_rows * 128;
+          if (b < nbox && (!paged || blks[b] >= 0)) {
+            bytes += 2u * box_rows * 128;
+            mask |= 1u << b;
+          }
         }
+        t.boxmask = mask;
         mbar_arrive_expect_tx(&sm.kv_full[stage], bytes);
       }
       __syncwarp();
@@ -390,15 +395,9 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
     for (int j = 0; j < ntiles; ++j) {
       if (!mbar_wait(&sm.kv_full[stage], phase, p.err)) { ok = false; break; }
       const int j0 = sm.tile[stage].j0;
+      const uint32_t boxmask = sm.tile[stage].boxmask;  // boxes whose block is valid
       // key columns of this tile that can be valid at all (visible, inside this sequence)
       const int col_end = min(kBN, si.vis - j0);
-      uint32_t boxmask = 0xFFu;  // paged: boxes whose block is valid
-      if (paged) {
-        boxmask = 0;
-#pragma unroll
-        for (int b = 0; b < kMaxBoxes; ++b)
-          if (b * box_rows < kBN && sm.tile[stage].blk[b] >= 0) boxmask |= 1u << b;
-      }
       // columns [0, vlim) of this tile are visible to this row.  A tile with a masked block, or
       // any tile of a scaled cache, takes the general path through the column table (uniform
       // across the group's four warps)
