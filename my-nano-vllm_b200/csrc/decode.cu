@@ -62,6 +62,7 @@ static_assert(kHdrSlot0 + kMaxBoxes <= kHdrWords, "header");
 // Per-item facts the softmax epilogue needs, by q slot (written with the item's Q operand).
 struct ItemInfo {
   int kvh, rg, nchunks, qrow0, rows;
+  int mbase;  // spec mode: nk - nq (row q sees key positions <= mbase + its token index)
 };
 
 template <int NT>
@@ -74,7 +75,6 @@ struct __align__(1024) DecodeSmem {
   uint8_t q2[2][N * kHeadDim];            // K-major SW128 query operand, by item parity
   uint8_t p2[2][NT][kTile * 16];          // P^T planes of 16 columns, MN-major, by tile parity
   float qscale[2][R];                     // per-row score multiplier (scale * log2 e * 2^k)
-  int qlim[2][R];                         // per-row largest visible key position (-1: no row)
   uint8_t qstage[R * 256];                // raw bf16 query rows of the next item (cp.async)
   float alpha[4][R];                      // per-warp copy of a tile's rescale factors (rare)
   float red[2][4][R];                     // cross-warp row maxima, double-buffered by tile
@@ -292,12 +292,7 @@ __device__ __forceinline__ void prepare_q(const Cursor<NT>& P, int slot, const D
       *reinterpret_cast<uint4*>(&sm.q2[slot][rl * 128 + ((chunk ^ (rl & 7)) << 4)]) =
           make_uint4(lo[4 * half], lo[4 * half + 1], lo[4 * half + 2], lo[4 * half + 3]);
     }
-    if (quarter == 0) {
-      sm.qscale[slot][r] = s_row * p.scale_log2;
-      sm.qlim[slot][r] = r < P.rows ? (p.spec_mode ? P.lim_base + (r + P.row0 % p.group) / p.group
-                                                   : INT_MAX)
-                                    : -1;
-    }
+    if (quarter == 0) sm.qscale[slot][r] = s_row * p.scale_log2;
   }
 }
 
@@ -474,9 +469,9 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
       if (P.t == P.t0) {
         if (!mbar_wait(&sm.q_empty[slot], ((P.nth >> 1) & 1) ^ 1, p.ctrl)) break;
         prepare_q<NT>(P, slot, p, sm, lane);
-        if (lane < 5) {
+        if (lane < 6) {
           const int v = lane == 0 ? P.kvh : lane == 1 ? P.rg : lane == 2 ? P.nchunks
-                                    : lane == 3 ? P.qrow0 : P.rows;
+                        : lane == 3 ? P.qrow0 : lane == 4 ? P.rows : P.lim_base - P.row0 / p.group;
           reinterpret_cast<int*>(&sm.iinfo[slot])[lane] = v;
         }
         fence_proxy_async_smem();
@@ -610,7 +605,7 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
     // up to 8 live rows keep their score multiplier and causal limit in registers
     constexpr bool kRowRegs = RV <= 8;
     float cs_r[kRowRegs ? RV : 1];
-    int lim_r[kRowRegs ? RV : 1];
+    int rows_i = 0, qrow_lo = 0;  // the item's live rows; spec mode: (nk - nq) G + rg R
     int kvh = 0;
     int stage = 0, j = 0, sync_uses = 0, item_first_tile = 0;
     uint32_t phase = 0;
@@ -641,14 +636,15 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
         qcount[slot]++;
         item_first_tile = j;
         kvh = sm.iinfo[slot].kvh;
+        rows_i = sm.iinfo[slot].rows;
+        // spec mode: row q = rg R + q of the sequence (token (rg R + q) / G) sees key positions
+        // <= mbase + token, i.e. position pos is visible to rows q >= (pos - mbase) G - rg R
+        qrow_lo = p.spec_mode ? sm.iinfo[slot].mbase * G + sm.iinfo[slot].rg * R : 0;
 #pragma unroll
         for (int q = 0; q < RV; ++q) {
           m_ref[q] = -INFINITY;
           l_part[q] = 0.f;
-          if constexpr (kRowRegs) {
-            cs_r[q] = sm.qscale[slot][q];
-            lim_r[q] = sm.qlim[slot][q];
-          }
+          if constexpr (kRowRegs) cs_r[q] = sm.qscale[slot][q];
         }
       }
       float ks = 1.f, lv = 0.f;
@@ -673,14 +669,21 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
       tc::fence_before_sync();
       mbar_arrive(&sm.s_empty[sb]);
       const int pos = tok0 + r;
+      // rows [qmin, rows_i) see this thread's key position (all live rows outside spec mode)
+      const int qmin = !valid ? INT_MAX : (p.spec_mode ? pos * G - qrow_lo : INT_MIN);
       float xs[RV];  // score (log2 units) + log2 of the value scale: P's exponent
       bool over = false;  // a score the current reference cannot take (P would pass 256)
 #pragma unroll
       for (int q = 0; q < RV; ++q) {
-        const float csq = kRowRegs ? cs_r[kRowRegs ? q : 0] : sm.qscale[slot][q];
-        const int limq = kRowRegs ? lim_r[kRowRegs ? q : 0] : sm.qlim[slot][q];
+        float csq;
+        if constexpr (kRowRegs) {
+          csq = cs_r[kRowRegs ? q : 0];
+        } else {
+          const float4 c4 = *reinterpret_cast<const float4*>(&sm.qscale[slot][q & ~3]);
+          csq = (q & 3) == 0 ? c4.x : (q & 3) == 1 ? c4.y : (q & 3) == 2 ? c4.z : c4.w;
+        }
         float sc = (x[q] + x[R + q]) * csq * ks;
-        if (!(valid && pos <= limq)) sc = -INFINITY;
+        if (!(q >= qmin && q < rows_i)) sc = -INFINITY;
         xs[q] = sc + lv;
         over |= xs[q] > m_ref[q] + kRescaleLog2;
       }
