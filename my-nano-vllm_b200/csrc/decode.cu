@@ -48,7 +48,11 @@ constexpr int kMmaWarp = 5;
 constexpr int kThreads = 8 * 32;  // warps 6-7 idle (no role): 2 warps per scheduler, 2 CTAs per SM
 constexpr int kSoftmaxThreads = 128;
 constexpr int kMaxBoxes = kTile / 16;
-constexpr int kItemsPerCta = 16;  // plan target: work items per CTA
+// Plan target: work items per CTA (an upper bound for the workspace).  Wide row groups have
+// costly item epilogues (24 rows of sums and partials), so they split less.
+constexpr int kItemsPerCta = 16;
+template <int NT>
+__host__ __device__ constexpr int items_per_cta() { return NT == 1 ? kItemsPerCta : 2; }
 
 enum : int { kFirst = 1, kLast = 2 };
 
@@ -364,7 +368,7 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
   const uint32_t tmem = sm.tmem_base;
   const unsigned long long total_work =
       sm.total_work * static_cast<unsigned long long>(p.num_kv_heads);
-  const unsigned long long target = static_cast<unsigned long long>(kItemsPerCta) * gridDim.x;
+  const unsigned long long target = static_cast<unsigned long long>(items_per_cta<NT>()) * gridDim.x;
   long long ct = static_cast<long long>((total_work + target - 1) / target);
   if (ct < p.min_chunk) ct = p.min_chunk;
   ct = (ct + kTile - 1) / kTile * kTile;
