@@ -218,7 +218,15 @@ def secondary(dev, hbm_peak, bf16_peak):
             ts.append(a.elapsed_time(b))
         return statistics.median(ts)
 
-    st_ms = timed(lambda: store_kvcache(c.new_k, c.new_v, c.k, c.v, c.slot_mapping))
+    # the store is ~10 us of device work: time a CUDA graph of the call so that the host-side
+    # launch (the Python wrapper) is not measured
+    store_kvcache(c.new_k, c.new_v, c.k, c.v, c.slot_mapping)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        store_kvcache(c.new_k, c.new_v, c.k, c.v, c.slot_mapping)
+    st_ms = timed(graph.replay)
+    del graph
     pf_ms = timed(lambda: fp8_prefill_attention(
         c.q, c.k, c.v, block_tables=c.block_tables, cu_seqlens_q=c.cu_seqlens_q,
         cu_seqlens_k=c.cu_seqlens_k, max_seqlen_q=c.max_seqlen_q, max_seqlen_k=c.max_seqlen_k,
@@ -234,6 +242,7 @@ def secondary(dev, hbm_peak, bf16_peak):
                                  "peak_note": "e4m3 dense = 2 x measured bf16 GEMM"},
                     "l2": "flushed before each call"},
         "store": {"ms": st_ms, "gbs": store_bytes / (st_ms * 1e-3) / 1e9, "rows": n,
+                  "timing": "CUDA-graph replay, L2 flushed before each call",
                   "bytes": store_bytes, "frac": store_bytes / (st_ms * 1e-3) / 1e9 / hbm_peak},
     }
 
