@@ -846,12 +846,20 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
 
 // Combines the split-KV partials of every (sequence, kv head, row group) with more than one
 // chunk, using the plan the decode kernel published.  One CTA per pair (grid-strided); thread =
-// output dim.  Partial rows hold O (unnormalised, 128 floats), then the running max (log2 units)
-// and the row sum.
+// output dim.  Partial rows hold O (unnormalised, 128 floats), then the reference max (log2
+// units) and the row sum.  Per pair: the (max, sum) of every (row, chunk) are gathered in parallel
+// (per-row maxima by shared-memory atomics on order-preserving ints), their weights computed once,
+// then each thread's partial-O loads are all independent.  Launched as a programmatic dependent
+// of the decode kernel: it waits for the decode grid before touching the partials.
+constexpr int kCombineSlots = 1024;  // (row, chunk) weights staged per round
 template <int NT>
 __global__ void __launch_bounds__(kHeadDim)
     combine_kernel(const DecodeParams p) {
   constexpr int R = 8 * NT;
+  __shared__ int smax[R];
+  __shared__ float ssum[R];
+  __shared__ float swt[kCombineSlots];
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // the decode grid has finished
   const int G = p.group;
   const int CT = p.plan[0];
   const int64_t npairs = static_cast<int64_t>(p.num_seqs) * p.num_kv_heads * p.max_rowgroups;
@@ -870,25 +878,50 @@ __global__ void __launch_bounds__(kHeadDim)
     const int rows = min(R, nq * G - rg * R);
     const int64_t first = p.plan[2 + b] + kvh * nrg + rg;
     const int64_t stride = static_cast<int64_t>(p.num_kv_heads) * nrg;
-    for (int q = 0; q < rows; ++q) {
-      float M = -INFINITY;
-      for (int c = 0; c < nchunks; ++c)
-        M = fmaxf(M, p.partials[((first + c * stride) * R + q) * (kHeadDim + 4) + kHeadDim]);
-      const float Mu = M == -INFINITY ? 0.f : M;
-      float L2 = 0.f, O = 0.f;
-#pragma unroll 4
-      for (int c = 0; c < nchunks; ++c) {
-        const float* part = p.partials + ((first + c * stride) * R + q) * (kHeadDim + 4);
-        const float wt = ex2(part[kHeadDim] - Mu);
-        L2 += wt * part[kHeadDim + 1];
-        O += wt * part[d];
+    auto part = [&](int q, int c) -> const float* {
+      return p.partials + ((first + c * stride) * R + q) * (kHeadDim + 4);
+    };
+    if (d < R) { smax[d] = f2ord(-INFINITY); ssum[d] = 0.f; }
+    __syncthreads();
+    const int n = rows * nchunks;
+    for (int i = d; i < n; i += kHeadDim) {
+      const int q = i / nchunks, c = i - q * nchunks;
+      atomicMax(&smax[q], f2ord(__ldcg(part(q, c) + kHeadDim)));
+    }
+    __syncthreads();
+    float o[R];
+#pragma unroll
+    for (int q = 0; q < R; ++q) o[q] = 0.f;
+    for (int base = 0; base < n; base += kCombineSlots) {
+      const int m = min(kCombineSlots, n - base);
+      for (int i = d; i < m; i += kHeadDim) {
+        const int q = (base + i) / nchunks, c = (base + i) - q * nchunks;
+        const float M = ord2f(smax[q]);
+        const float* pr = part(q, c);
+        const float w = ex2(__ldcg(pr + kHeadDim) - (M == -INFINITY ? 0.f : M));
+        swt[i] = w;
+        atomicAdd(&ssum[q], w * __ldcg(pr + kHeadDim + 1));
       }
+      __syncthreads();
+#pragma unroll
+      for (int q = 0; q < R; ++q) {
+        if (q >= rows) break;
+        const int c0 = max(0, base - q * nchunks), c1 = min(nchunks, base + m - q * nchunks);
+#pragma unroll 4
+        for (int c = c0; c < c1; ++c) o[q] += swt[q * nchunks + c - base] * __ldcg(part(q, c) + d);
+      }
+      __syncthreads();
+    }
+#pragma unroll
+    for (int q = 0; q < R; ++q) {
+      if (q >= rows) break;
       const int rr = rg * R + q;
       const int jj = rr / G, hh = kvh * G + (rr - jj * G);
-      __nv_bfloat16 v = out_round(O / fmaxf(L2, 1e-10f));
+      __nv_bfloat16 v = out_round(o[q] / fmaxf(ssum[q], 1e-10f));
       p.out[static_cast<int64_t>(qrow0 + jj) * p.out_row_stride + hh * kHeadDim + d] =
           *reinterpret_cast<uint16_t*>(&v);
     }
+    __syncthreads();
   }
 }
 
@@ -974,14 +1007,28 @@ void launch_variant(const DecodeParams& p, const CUtensorMap& tmk, const CUtenso
                     int cgrid, cudaStream_t stream) {
   const int grid = decode_grid_for<NT, RV>(p.num_seqs);
   decode_kernel<NT, RV><<<grid, kThreads, decode_smem_bytes<NT>(p.num_seqs), stream>>>(tmk, tmv, p);
-  if (cgrid > 0) combine_kernel<NT><<<cgrid, kHeadDim, 0, stream>>>(p);
+  if (cgrid > 0) {
+    // programmatic dependent launch: the combine CTAs may be scheduled as decode CTAs retire;
+    // each waits (griddepcontrol.wait) for the whole decode grid before reading the partials
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(cgrid);
+    cfg.blockDim = dim3(kHeadDim);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, combine_kernel<NT>, p);
+  }
 }
 }  // namespace
 
 cudaError_t launch_decode(const DecodeParams& p, int nt, int rv, const CUtensorMap& tmk,
                           const CUtensorMap& tmv, cudaStream_t stream) {
   const int64_t pairs = static_cast<int64_t>(p.num_seqs) * p.num_kv_heads * p.max_rowgroups;
-  const int cgrid = static_cast<int>(pairs < 8LL * sm_count() ? pairs : 8LL * sm_count());
+  const int cgrid = static_cast<int>(pairs < 16LL * sm_count() ? pairs : 16LL * sm_count());
   switch (nt) {
     case 1:
       if (rv <= 4) launch_variant<1, 4>(p, tmk, tmv, cgrid, stream);
