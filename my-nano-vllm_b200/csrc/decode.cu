@@ -83,7 +83,8 @@ struct __align__(1024) DecodeSmem {
   float alpha[4][R];                      // per-warp copy of a tile's rescale factors (rare)
   float red[2][4][R];                     // cross-warp row maxima, double-buffered by tile
   alignas(16) int vote[2][4];             // per warp: a score above its row's reference + 2^4
-  float redl[4][R];                       // cross-warp row sums (epilogue)
+  float redl[2][4][R];                    // an item's per-warp row sums, by item parity
+  float mfin[2][R];                       // an item's final reference maxima, by item parity
   alignas(16) int hdr[STAGES][kHdrWords];
   ItemInfo iinfo[2];
   uint64_t kv_full[STAGES];
@@ -309,7 +310,7 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
   constexpr int N = Smem::N;
   constexpr int kStages = Smem::STAGES;
   static_assert(RV >= 1 && RV <= R && RV % 4 == 0, "live rows");
-  constexpr uint32_t kTmemCols = 3 * N <= 64 ? 64 : (3 * N <= 128 ? 128 : 256);  // S x2, O
+  constexpr uint32_t kTmemCols = 4 * N <= 64 ? 64 : (4 * N <= 128 ? 128 : 256);  // S x2, O x2
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -536,8 +537,9 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
       uint32_t phase = 0;
       int qcount[2] = {0, 0};
       bool pend = false;  // a tile whose PV is still to be issued
-      int pend_stage = 0, pend_first = 0;
-      auto issue_pv = [&](int st, int tile, int fresh) -> bool {
+      int pend_stage = 0, pend_first = 0, pend_ob = 0;
+      int items = 0;  // items started: O buffer of an item = its parity
+      auto issue_pv = [&](int st, int tile, int fresh, int ob) -> bool {
         const int b = tile & 1;
         if (!mbar_wait(&sm.p_full[b], (tile >> 1) & 1, p.ctrl)) return false;
         tc::fence_after_sync();
@@ -549,7 +551,7 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
           for (int ks = 0; ks < 4; ++ks) {
             const uint64_t ad = tc::smem_desc(va + ks * 32 * 128, 0, 1024, tc::kSw128);
             const uint64_t bd = tc::smem_desc(pa + ks * 32 * 16, 128, 2048, tc::kSwNone);
-            tc::mma_f8(tmem + 2 * N + 16 * plane, ad, bd, idesc_pv, (ks > 0 || !fresh) ? 1u : 0u);
+            tc::mma_f8(tmem + (2 + ob) * N + 16 * plane, ad, bd, idesc_pv, (ks > 0 || !fresh) ? 1u : 0u);
           }
         }
         tc::commit(&sm.kv_empty[st]);
@@ -566,7 +568,9 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
         if (first) {
           if (!mbar_wait(&sm.q_full[slot], qcount[slot] & 1, p.ctrl)) break;
           qcount[slot]++;
+          ++items;
         }
+        const int ob = (items - 1) & 1;
         const int sb = j & 1;
         if (!mbar_wait(&sm.s_empty[sb], ((j >> 1) & 1) ^ 1, p.ctrl)) break;
         tc::fence_after_sync();
@@ -579,18 +583,19 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
           tc::mma_f8(tmem + sb * N, ad, bd, idesc_s, ks > 0 ? 1u : 0u);
         }
         tc::commit(&sm.s_full[sb]);
-        if (pend && !issue_pv(pend_stage, j - 1, pend_first)) break;
+        if (pend && !issue_pv(pend_stage, j - 1, pend_first, pend_ob)) break;
         pend = true;
         pend_stage = stage;
         pend_first = first;
+        pend_ob = ob;
         if (last) {  // the item's epilogue waits on this PV: issue it now, not after the next S
-          if (!issue_pv(stage, j, first)) break;
+          if (!issue_pv(stage, j, first, ob)) break;
           pend = false;
         }
         ++j;
         if (++stage == kStages) { stage = 0; phase ^= 1; }
       }
-      if (pend) issue_pv(pend_stage, j - 1, pend_first);
+      if (pend) issue_pv(pend_stage, j - 1, pend_first, pend_ob);
     }
     __syncwarp();
   } else if (fits && warp < 4) {
@@ -624,7 +629,57 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
       tc::fence_after_sync();
       return true;
     };
-    const uint32_t o_tmem = tmem + lane_base + 2 * N;
+    const uint32_t o_base = tmem + lane_base + 2 * N;  // O of an item: o_base + (item parity) N
+    int nitem = 0;  // items started
+    // the item whose read-out is deferred to the next tile (its last PV is then normally done,
+    // and its row-sum exchange rides on that tile's barrier)
+    bool pend_ep = false;
+    int pend_j = 0, pend_ob = 0, pend_slot = 0, pend_item = 0;
+    auto finish = [&]() -> bool {
+      if (!wait_pv(pend_j)) return false;
+      float o[RV];
+#pragma unroll
+      for (int q = 0; q < RV; ++q) o[q] = 0.f;
+#pragma unroll
+      for (int c = 0; c < N; c += 16) {
+        float o16[16];
+        tc::ld16(o_base + pend_ob * N + c, o16);
+        tc::wait_ld();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int q = (c + i) % R;
+          if (q < RV) o[q] += o16[i];
+        }
+      }
+      tc::fence_before_sync();
+      const ItemInfo ii = sm.iinfo[pend_slot];
+      const int rows = ii.rows, nchunks = ii.nchunks, rg = ii.rg, qrow0 = ii.qrow0;
+      const int d = r;  // output dim
+#pragma unroll
+      for (int q = 0; q < RV; ++q) {
+        if (q >= rows) break;
+        const float lsum = sm.redl[pend_ob][0][q] + sm.redl[pend_ob][1][q] +
+                           sm.redl[pend_ob][2][q] + sm.redl[pend_ob][3][q];
+        if (nchunks == 1) {
+          const int rr = rg * R + q;
+          const int jj = rr / G, hh = ii.kvh * G + (rr - jj * G);
+          __nv_bfloat16 v = out_round(o[q] / fmaxf(lsum, 1e-10f));
+          p.out[static_cast<int64_t>(qrow0 + jj) * p.out_row_stride + hh * kHeadDim + d] =
+              *reinterpret_cast<uint16_t*>(&v);
+        } else {
+          float* part = p.partials + (static_cast<int64_t>(pend_item) * R + q) * (kHeadDim + 4);
+          part[d] = o[q];
+          if (d == 0) {
+            // a chunk whose rows saw no key position carries no weight in the combine
+            part[kHeadDim] = lsum > 0.f ? sm.mfin[pend_ob][q] : -INFINITY;
+            part[kHeadDim + 1] = lsum;
+          }
+        }
+      }
+      mbar_arrive(&sm.q_empty[pend_slot]);
+      pend_ep = false;
+      return true;
+    };
     while (true) {
       if (!mbar_wait(&sm.kv_full[stage], phase, p.ctrl)) break;
       // everything this tile needs from its header, read now: once P is handed over, the PV
@@ -638,6 +693,7 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
       if (flags & kFirst) {
         if (!mbar_wait(&sm.q_full[slot], qcount[slot] & 1, p.ctrl)) break;
         qcount[slot]++;
+        ++nitem;
         item_first_tile = j;
         kvh = sm.iinfo[slot].kvh;
         rows_i = sm.iinfo[slot].rows;
@@ -747,14 +803,15 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
 #pragma unroll
         for (int c = 0; c < N; c += 16) {
           float o16[16];
-          tc::ld16(o_tmem + c, o16);
+          const uint32_t o_cur = o_base + ((nitem - 1) & 1) * N;
+          tc::ld16(o_cur + c, o16);
           tc::wait_ld();
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             const int q = (c + i) % R;
             if (q < RV && ((resc >> q) & 1u)) o16[i] *= sm.alpha[warp][q];
           }
-          tc::st16(o_tmem + c, o16);
+          tc::st16(o_cur + c, o16);
         }
         tc::wait_st();
       }
@@ -773,60 +830,33 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
       tc::fence_before_sync();
       mbar_arrive(&sm.p_full[sb]);
 
+      // the previous item's read-out (its sums were exchanged at this tile's barrier)
+      if (pend_ep && !finish()) break;
       if (flags & kLast) {
-        // ------------------------------------------------ epilogue of the item
-        if (!wait_pv(j)) break;
-        float o[RV];
-#pragma unroll
-        for (int q = 0; q < RV; ++q) o[q] = 0.f;
-#pragma unroll
-        for (int c = 0; c < N; c += 16) {
-          float o16[16];
-          tc::ld16(o_tmem + c, o16);
-          tc::wait_ld();
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int q = (c + i) % R;
-            if (q < RV) o[q] += o16[i];
-          }
-        }
-        tc::fence_before_sync();
+        // park the item: per-warp row sums and the final maxima, read out one tile later
+        const int ob = (nitem - 1) & 1;
 #pragma unroll
         for (int q = 0; q < RV; ++q) {
           float l = l_part[q];
 #pragma unroll
           for (int off = 16; off > 0; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
-          if (lane == 0) sm.redl[warp][q] = l;
+          if (lane == 0) sm.redl[ob][warp][q] = l;
+          if (tid == 0) sm.mfin[ob][q] = m_ref[q];
         }
-        if (!sync()) break;
-        const ItemInfo ii = sm.iinfo[slot];
-        const int rows = ii.rows, nchunks = ii.nchunks, rg = ii.rg, qrow0 = ii.qrow0;
-        const int d = r;  // output dim
-#pragma unroll
-        for (int q = 0; q < RV; ++q) {
-          if (q >= rows) break;
-          const float lsum = sm.redl[0][q] + sm.redl[1][q] + sm.redl[2][q] + sm.redl[3][q];
-          if (nchunks == 1) {
-            const int rr = rg * R + q;
-            const int jj = rr / G, hh = kvh * G + (rr - jj * G);
-            __nv_bfloat16 v = out_round(o[q] / fmaxf(lsum, 1e-10f));
-            p.out[static_cast<int64_t>(qrow0 + jj) * p.out_row_stride + hh * kHeadDim + d] =
-                *reinterpret_cast<uint16_t*>(&v);
-          } else {
-            float* part = p.partials + (static_cast<int64_t>(item) * R + q) * (kHeadDim + 4);
-            part[d] = o[q];
-            if (d == 0) {
-              // a chunk whose rows saw no key position carries no weight in the combine
-              part[kHeadDim] = lsum > 0.f ? m_ref[q] : -INFINITY;
-              part[kHeadDim + 1] = lsum;
-            }
-          }
+        pend_ep = true;
+        pend_j = j;
+        pend_ob = ob;
+        pend_slot = slot;
+        pend_item = item;
+        if constexpr (NT > 1) {  // wide row groups: read out at once (registers are scarce)
+          if (!sync() || !finish()) break;
         }
-        mbar_arrive(&sm.q_empty[slot]);
       }
       ++j;
       if (++stage == kStages) { stage = 0; phase ^= 1; }
     }
+    // the last item's read-out (a barrier first: every warp has parked its sums)
+    if (pend_ep && sync()) finish();
   }
 
   // ---------------------------------------------------------------- teardown
