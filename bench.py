@@ -54,31 +54,68 @@ def _traffic(kernel: str):
 
 
 class ClockSampler:
-    """Samples nvidia-smi SM clocks and throttle reasons while the timed region runs."""
+    """Samples SM clocks and clock-event (throttle) reasons while the timed region runs: NVML
+    polled every 0.5 ms (the timed region is a few ms), or nvidia-smi every 200 ms without NVML."""
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASON_BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+                   "hw_thermal_slowdown": 0x40}
 
     def __init__(self, index: int):
         self.index = index
-        self.samples = []
+        self.samples = []  # (sm_mhz, max_mhz, set of reasons)
         self._stop = threading.Event()
         self._t = None
+        self._nvml = None
+        try:
+            import pynvml
+            import torch
+            pynvml.nvmlInit()
+            h = None
+            try:  # the CUDA device (CUDA_VISIBLE_DEVICES may renumber) by its PCI address
+                pr = torch.cuda.get_device_properties(index)
+                bus = f"{pr.pci_domain_id:08X}:{pr.pci_bus_id:02X}:{pr.pci_device_id:02X}.0"
+                h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            except Exception:
+                h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self._nvml = (pynvml, h)
+        except Exception:
+            self._nvml = None
 
-    def _run(self):
+    def _run_nvml(self):
+        nv, h = self._nvml
+        get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons",
+                              getattr(nv, "nvmlDeviceGetCurrentClocksThrottleReasons", None))
+        mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        while not self._stop.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                bits = get_reasons(h) if get_reasons else 0
+                self.samples.append((float(sm), float(mx),
+                                     {n for n, b in self.REASON_BITS.items() if bits & b}))
+            except Exception:
+                pass
+            self._stop.wait(0.0005)
+
+    def _run_smi(self):
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         while not self._stop.is_set():
             try:
                 out = subprocess.run(["nvidia-smi", f"--id={self.index}",
                                       f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits"],
                                      capture_output=True, text=True, timeout=5).stdout.strip()
                 if out:
-                    self.samples.append([x.strip() for x in out.split(",")])
+                    f = [x.strip() for x in out.split(",")]
+                    self.samples.append((float(f[1]), float(f[2]),
+                                         {n for n, v in zip(names, f[5:9]) if v.lower() == "active"}))
             except Exception:
                 pass
             self._stop.wait(0.2)
 
     def __enter__(self):
-        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t = threading.Thread(target=self._run_nvml if self._nvml else self._run_smi,
+                                   daemon=True)
         self._t.start()
         return self
 
@@ -89,17 +126,12 @@ class ClockSampler:
     def summary(self):
         if not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
-        mx = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = set()
-        for s in self.samples:
-            for n, v in zip(names, s[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
-                "samples": len(self.samples)}
+        for _, _, r in self.samples:
+            reasons |= r
+        return {"sm_mhz": statistics.median(x[0] for x in self.samples),
+                "sm_max_mhz": max(x[1] for x in self.samples), "reasons": sorted(reasons),
+                "samples": len(self.samples), "source": "nvml" if self._nvml else "nvidia-smi"}
 
 
 def _dist_init():
@@ -282,7 +314,8 @@ def run_ours(args, world, rank, local):
             e.record(stream)
         t_end.record(stream)
         torch.cuda.synchronize()
-        time.sleep(0.3)
+        if not clk.samples:  # nvidia-smi fallback: make sure at least one sample is taken
+            time.sleep(0.25)
     total_ms = t_start.elapsed_time(t_end)
     per_launch_ms = statistics.mean(s.elapsed_time(e) for s, e in ev)
     total_ms = _max_over_ranks(total_ms, world)
