@@ -423,49 +423,138 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
         if (lane == 0) sm.colok[g][warp & 3] = bal;
         named_barrier(1 + g, 128);
       }
-      // ---- pass 1: row maximum (of the raw scores on the fast path: cs > 0 commutes with max)
-      float tmax = -INFINITY;
-#pragma unroll 1
-      for (int c0 = 0; c0 < kBN; c0 += 32) {
-        float v[32];
-        tmem_ld32(s_tmem + c0, v);
-        tc::wait_ld();
-        if (!general && c0 + 32 <= vlim) {  // every column visible: four independent chains
-          float a0 = v[0], a1 = v[1], a2 = v[2], a3 = v[3];
-#pragma unroll
-          for (int i = 4; i < 32; i += 4) {
-            a0 = fmaxf(a0, v[i]);
-            a1 = fmaxf(a1, v[i + 1]);
-            a2 = fmaxf(a2, v[i + 2]);
-            a3 = fmaxf(a3, v[i + 3]);
-          }
-          tmax = fmaxf(tmax, fmaxf(fmaxf(a0, a1), fmaxf(a2, a3)));
-        } else if (!general) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) tmax = fmaxf(tmax, c0 + i < vlim ? v[i] : -INFINITY);
-        } else {
-          const uint32_t okw = sm.colok[g][c0 >> 5];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const bool cok = ((okw >> i) & 1u) && c0 + i < vlim;
-            tmax = fmaxf(tmax, cok ? v[i] * sm.colk[g][c0 + i] * cs : -INFINITY);
-          }
-        }
-      }
-      if (!general && tmax != -INFINITY) tmax *= cs;
-      // ---- lazy rescale: move the reference max only when it grows by more than 2^4
-      float alpha = 1.f;
-      if (tmax > m_ref + kRescaleLog2) {
-        const float m_new = tmax;
-        alpha = m_ref == -INFINITY ? 0.f : ex2(m_ref - m_new);
-        m_ref = m_new;
-        l *= alpha;
-      }
-      // O and the P buffer are free once PV_g(j-1) is done; each warp rescales its own rows
+      // O and the P buffer are free once PV_g(j-1) is done
       if (j >= 1) {
         if (!mbar_wait(&sm.pv_done[g], (j - 1) & 1, p.err)) { ok = false; break; }
         tc::fence_after_sync();
       }
+      // ---- P = 16 * 2^(s - m_ref) as e4m3 hi + lo into the P buffer; returns the row sum of the
+      // same values.  On the fast path the largest P is tracked (packed f16) in *pmax.
+      auto write_p = [&](float bias, float* pmax) -> float {
+        float lt = 0.f;
+        __half2 mx = __float2half2_rn(0.f);
+#pragma unroll 1
+        for (int c0 = 0; c0 < kBN; c0 += 32) {
+          float v[32];
+          tmem_ld32(s_tmem + c0, v);
+          tc::wait_ld();
+          uint32_t hw[8], lw[8];  // this chunk's P row: hi and lo e4m3 bytes, 4 per word
+          if (!general) {
+            // packed f16 pipeline: exponent argument to f16x2, one ex2 for two elements, split
+            // in f16x2, row sum in four f16x2 partials (values <= 256, four per partial)
+            __half2 lacc[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) lacc[k] = __float2half2_rn(0.f);
+            const bool full = c0 + 32 <= vlim;
+#pragma unroll
+            for (int k = 0; k < 16; ++k) {
+              float a0 = fmaf(v[2 * k], cs, bias), a1 = fmaf(v[2 * k + 1], cs, bias);
+              if (!full) {
+                a0 = c0 + 2 * k < vlim ? a0 : -INFINITY;
+                a1 = c0 + 2 * k + 1 < vlim ? a1 : -INFINITY;
+              }
+              const uint32_t pe = ex2_f16x2(pack_f16x2(a0, a1));
+              const __half2 ph = *reinterpret_cast<const __half2*>(&pe);
+              lacc[k & 3] = __hadd2(lacc[k & 3], ph);
+              mx = __hmax2(mx, ph);
+              uint32_t h2, l2;
+              split_f16x2_e4m3(pe, h2, l2);
+              if (k & 1) {
+                hw[k >> 1] |= h2 << 16;
+                lw[k >> 1] |= l2 << 16;
+              } else {
+                hw[k >> 1] = h2;
+                lw[k >> 1] = l2;
+              }
+            }
+            const __half2 ls = __hadd2(__hadd2(lacc[0], lacc[1]), __hadd2(lacc[2], lacc[3]));
+            lt += __low2float(ls) + __high2float(ls);
+          } else {
+            const uint32_t okw = sm.colok[g][c0 >> 5];
+            float la[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial sums
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const bool cok = ((okw >> i) & 1u) && c0 + i < vlim;
+              const float e = cok ? ex2(v[i] * sm.colk[g][c0 + i] * cs + bias) : 0.f;
+              la[i & 3] += e;
+              v[i] = e * sm.colv[g][c0 + i];
+            }
+            lt += (la[0] + la[1]) + (la[2] + la[3]);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              uint32_t ah, al, bh, bl;
+              split_pos_f32x2_e4m3(v[4 * k], v[4 * k + 1], ah, al);
+              split_pos_f32x2_e4m3(v[4 * k + 2], v[4 * k + 3], bh, bl);
+              hw[k] = ah | (bh << 16);
+              lw[k] = al | (bl << 16);
+            }
+          }
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            const int c = (c0 >> 4) + half;  // 16-byte chunk index within the 128-byte row
+            const int off = r * 128 + ((c ^ (r & 7)) << 4);
+            *reinterpret_cast<uint4*>(&phi[off]) =
+                make_uint4(hw[4 * half], hw[4 * half + 1], hw[4 * half + 2], hw[4 * half + 3]);
+            *reinterpret_cast<uint4*>(&plo[off]) =
+                make_uint4(lw[4 * half], lw[4 * half + 1], lw[4 * half + 2], lw[4 * half + 3]);
+          }
+        }
+        *pmax = fmaxf(__low2float(mx), __high2float(mx));
+        return lt;
+      };
+      // ---- fast path: one pass against the current reference; a score more than 2^4 above it
+      // (P > 256) sends the warp through the exact two passes below (the same rescale rule)
+      float l_tile = 0.f;
+      bool exact = general || (vlim > 0 && m_ref == -INFINITY);  // a row's first visible keys
+      if (!__any_sync(0xffffffffu, exact)) {
+        float pmax;
+        l_tile = write_p(kPScaleLog2 - m_ref, &pmax);
+        exact = pmax > 256.f;
+      }
+      float alpha = 1.f;
+      if (__any_sync(0xffffffffu, exact)) {
+        // ---- pass 1: row maximum (of the raw scores on the fast path: cs > 0 commutes with max)
+        float tmax = -INFINITY;
+#pragma unroll 1
+        for (int c0 = 0; c0 < kBN; c0 += 32) {
+          float v[32];
+          tmem_ld32(s_tmem + c0, v);
+          tc::wait_ld();
+          if (!general && c0 + 32 <= vlim) {  // every column visible: four independent chains
+            float a0 = v[0], a1 = v[1], a2 = v[2], a3 = v[3];
+#pragma unroll
+            for (int i = 4; i < 32; i += 4) {
+              a0 = fmaxf(a0, v[i]);
+              a1 = fmaxf(a1, v[i + 1]);
+              a2 = fmaxf(a2, v[i + 2]);
+              a3 = fmaxf(a3, v[i + 3]);
+            }
+            tmax = fmaxf(tmax, fmaxf(fmaxf(a0, a1), fmaxf(a2, a3)));
+          } else if (!general) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) tmax = fmaxf(tmax, c0 + i < vlim ? v[i] : -INFINITY);
+          } else {
+            const uint32_t okw = sm.colok[g][c0 >> 5];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const bool cok = ((okw >> i) & 1u) && c0 + i < vlim;
+              tmax = fmaxf(tmax, cok ? v[i] * sm.colk[g][c0 + i] * cs : -INFINITY);
+            }
+          }
+        }
+        if (!general && tmax != -INFINITY) tmax *= cs;
+        // lazy rescale: move the reference max only when it grows by more than 2^4
+        if (tmax > m_ref + kRescaleLog2) {
+          alpha = m_ref == -INFINITY ? 0.f : ex2(m_ref - tmax);
+          m_ref = tmax;
+          l *= alpha;
+        }
+        // ---- pass 2 (overwrites the fast pass's P)
+        float unused;
+        l_tile = write_p(kPScaleLog2 - (m_ref == -INFINITY ? 0.f : m_ref), &unused);
+      }
+      l += l_tile;
+      // O (quiescent: PV_g(j-1) done) follows a moved reference; each warp rescales its own rows
       if (__any_sync(0xffffffffu, alpha != 1.f) && j > 0) {
 #pragma unroll
         for (int c0 = 0; c0 < 128; c0 += 16) {
@@ -477,73 +566,6 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
           tc::st16(o_tmem + c0, o16);
         }
         tc::wait_st();
-      }
-      // ---- pass 2: P = 16 * 2^(s - m_ref) as e4m3 hi + lo; l sums the same 16 * 2^(s - m_ref)
-      const float m_use = m_ref == -INFINITY ? 0.f : m_ref;
-      const float bias = kPScaleLog2 - m_use;  // the factor 16 folded into the exponent
-#pragma unroll 1
-      for (int c0 = 0; c0 < kBN; c0 += 32) {
-        float v[32];
-        tmem_ld32(s_tmem + c0, v);
-        tc::wait_ld();
-        uint32_t hw[8], lw[8];  // this chunk's P row: hi and lo e4m3 bytes, 4 per word
-        if (!general) {
-          // packed f16 pipeline: exponent argument (<= 8) to f16x2, one ex2 for two elements,
-          // split in f16x2, row sum in four f16x2 partials (values <= 256, four per partial)
-          __half2 lacc[4];
-#pragma unroll
-          for (int k = 0; k < 4; ++k) lacc[k] = __float2half2_rn(0.f);
-          const bool full = c0 + 32 <= vlim;
-#pragma unroll
-          for (int k = 0; k < 16; ++k) {
-            float a0 = fmaf(v[2 * k], cs, bias), a1 = fmaf(v[2 * k + 1], cs, bias);
-            if (!full) {
-              a0 = c0 + 2 * k < vlim ? a0 : -INFINITY;
-              a1 = c0 + 2 * k + 1 < vlim ? a1 : -INFINITY;
-            }
-            const uint32_t pe = ex2_f16x2(pack_f16x2(a0, a1));
-            lacc[k & 3] = __hadd2(lacc[k & 3], *reinterpret_cast<const __half2*>(&pe));
-            uint32_t h2, l2;
-            split_f16x2_e4m3(pe, h2, l2);
-            if (k & 1) {
-              hw[k >> 1] |= h2 << 16;
-              lw[k >> 1] |= l2 << 16;
-            } else {
-              hw[k >> 1] = h2;
-              lw[k >> 1] = l2;
-            }
-          }
-          const __half2 ls = __hadd2(__hadd2(lacc[0], lacc[1]), __hadd2(lacc[2], lacc[3]));
-          l += __low2float(ls) + __high2float(ls);
-        } else {
-          const uint32_t okw = sm.colok[g][c0 >> 5];
-          float la[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial sums
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const bool cok = ((okw >> i) & 1u) && c0 + i < vlim;
-            const float e = cok ? ex2(v[i] * sm.colk[g][c0 + i] * cs + bias) : 0.f;
-            la[i & 3] += e;
-            v[i] = e * sm.colv[g][c0 + i];
-          }
-          l += (la[0] + la[1]) + (la[2] + la[3]);
-#pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            uint32_t ah, al, bh, bl;
-            split_pos_f32x2_e4m3(v[4 * k], v[4 * k + 1], ah, al);
-            split_pos_f32x2_e4m3(v[4 * k + 2], v[4 * k + 3], bh, bl);
-            hw[k] = ah | (bh << 16);
-            lw[k] = al | (bl << 16);
-          }
-        }
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          const int c = (c0 >> 4) + half;  // 16-byte chunk index within the 128-byte row
-          const int off = r * 128 + ((c ^ (r & 7)) << 4);
-          *reinterpret_cast<uint4*>(&phi[off]) =
-              make_uint4(hw[4 * half], hw[4 * half + 1], hw[4 * half + 2], hw[4 * half + 3]);
-          *reinterpret_cast<uint4*>(&plo[off]) =
-              make_uint4(lw[4 * half], lw[4 * half + 1], lw[4 * half + 2], lw[4 * half + 3]);
-        }
       }
       tc::fence_before_sync();
       mbar_arrive(&sm.s_empty[g]);
