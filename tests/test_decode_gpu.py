@@ -53,7 +53,8 @@ def test_decode_config1():
 
 @pytest.mark.parametrize("min_chunk", [128, 512])
 @pytest.mark.parametrize("bs,hq,kvh", [(16, 4, 4), (32, 8, 2), (64, 16, 1), (256, 32, 8),
-                                       (48, 8, 8), (80, 32, 2), (256, 64, 8)])
+                                       (48, 8, 8), (80, 32, 2), (256, 64, 8),
+                                       (64, 12, 4), (128, 48, 8)])  # GQA 3 and 6
 def test_decode_edge_cases(bs, hq, kvh, min_chunk):
     from nanovllm_b200 import workloads
     lens = [0, 1, bs - 1, bs, bs + 1, 63, 64, 65, 3 * bs + 17, 700, -5, 1000]

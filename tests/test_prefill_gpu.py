@@ -83,7 +83,7 @@ def test_prefill_config4_mixed_spec_and_fresh():
 
 
 @pytest.mark.parametrize("bs", [16, 32, 64, 256])
-@pytest.mark.parametrize("hq,kvh", [(4, 4), (8, 2), (16, 2)])
+@pytest.mark.parametrize("hq,kvh", [(4, 4), (8, 2), (16, 2), (12, 4), (24, 4)])  # + GQA 3, 6
 def test_prefill_paged_edge_cases(bs, hq, kvh):
     from nanovllm_b200 import workloads
     nqs = [127, 128, 129, 1, 300, 0, 40, 9]
