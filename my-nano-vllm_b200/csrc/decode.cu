@@ -350,6 +350,10 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
     tc::tmem_relinquish();
   }
 
+  // launched as a programmatic dependent of the previous kernel on the stream: everything above
+  // overlaps its tail; no input is read before it has finished
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+
   // ---------------------------------------------------------------- plan (every CTA, same result)
   const int per = (B + kThreads - 1) / kThreads;
   const int s0 = min(B, tid * per), s1 = min(B, s0 + per);
@@ -889,6 +893,8 @@ __global__ void __launch_bounds__(kHeadDim)
   __shared__ int smax[R];
   __shared__ float ssum[R];
   __shared__ float swt[kCombineSlots];
+  // a following decode launch may start its setup now; it waits for this grid before any read
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");  // the decode grid has finished
   const int G = p.group;
   const int CT = p.plan[0];
@@ -1036,7 +1042,19 @@ template <int NT, int RV>
 void launch_variant(const DecodeParams& p, const CUtensorMap& tmk, const CUtensorMap& tmv,
                     int cgrid, cudaStream_t stream) {
   const int grid = decode_grid_for<NT, RV>(p.num_seqs);
-  decode_kernel<NT, RV><<<grid, kThreads, decode_smem_bytes<NT>(p.num_seqs), stream>>>(tmk, tmv, p);
+  // programmatic dependent launch: the CTAs' setup (barriers, tensor memory) overlaps the tail of
+  // the previous kernel; the kernel waits for it (griddepcontrol.wait) before reading any input
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t dcfg = {};
+  dcfg.gridDim = dim3(grid);
+  dcfg.blockDim = dim3(kThreads);
+  dcfg.dynamicSmemBytes = decode_smem_bytes<NT>(p.num_seqs);
+  dcfg.stream = stream;
+  dcfg.attrs = attr;
+  dcfg.numAttrs = 1;
+  cudaLaunchKernelEx(&dcfg, decode_kernel<NT, RV>, tmk, tmv, p);
   if (cgrid > 0) {
     // programmatic dependent launch: the combine CTAs may be scheduled as decode CTAs retire;
     // each waits (griddepcontrol.wait) for the whole decode grid before reading the partials
