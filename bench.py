@@ -322,31 +322,59 @@ def run_ours(args, world, rank, local):
     per_launch_ms = _max_over_ranks(per_launch_ms, world)
     err = device_error(dev)
 
-    # ---- end to end through the public API with host buffers
+    # ---- end to end through the public API with host buffers: every step copies its inputs
+    # (q, block tables, lengths) from pinned host memory and its output back.  The copies run on a
+    # second stream with double-buffered device inputs (events order them), so step i+1's
+    # upload and step i's download overlap a kernel; all of them are inside the timed region.
     q_h = case.q.cpu().pin_memory()
     bt_h = case.block_tables.cpu().pin_memory()
     ctx_h = case.context_lens.cpu().pin_memory()
-    out_h = torch.empty(case.q.shape, dtype=torch.bfloat16).pin_memory()
-    q_d, bt_d, ctx_d = torch.empty_like(case.q), torch.empty_like(case.block_tables), \
-        torch.empty_like(case.context_lens)
+    out_h = [torch.empty(case.q.shape, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    q_d = [torch.empty_like(case.q) for _ in range(2)]
+    bt_d = [torch.empty_like(case.block_tables) for _ in range(2)]
+    ctx_d = [torch.empty_like(case.context_lens) for _ in range(2)]
     h2d = q_h.numel() * 2 + bt_h.numel() * 4 + ctx_h.numel() * 4
-    d2h = out_h.numel() * 2
+    d2h = out_h[0].numel() * 2
+    copy_stream = torch.cuda.Stream(dev)
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_out = [torch.cuda.Event() for _ in range(2)]
+    ev_free = [torch.cuda.Event() for _ in range(2)]  # buffer b's output copied: reusable
+    for e in ev_free:
+        e.record(copy_stream)
 
-    def e2e_step():
-        q_d.copy_(q_h, non_blocking=True)
-        bt_d.copy_(bt_h, non_blocking=True)
-        ctx_d.copy_(ctx_h, non_blocking=True)
-        o = fp8_decode_attention(q_d, case.k_cache, case.v_cache, bt_d, ctx_d, case.scale)
-        out_h.copy_(o, non_blocking=True)
+    def upload(b):
+        with torch.cuda.stream(copy_stream):
+            copy_stream.wait_event(ev_free[b])
+            q_d[b].copy_(q_h, non_blocking=True)
+            bt_d[b].copy_(bt_h, non_blocking=True)
+            ctx_d[b].copy_(ctx_h, non_blocking=True)
+            ev_in[b].record(copy_stream)
 
-    for _ in range(args.warmup):
-        e2e_step()
+    def run(b):
+        stream.wait_event(ev_in[b])
+        o = fp8_decode_attention(q_d[b], case.k_cache, case.v_cache, bt_d[b], ctx_d[b], case.scale)
+        ev_out[b].record(stream)
+        with torch.cuda.stream(copy_stream):
+            copy_stream.wait_event(ev_out[b])
+            o.record_stream(copy_stream)
+            out_h[b].copy_(o, non_blocking=True)
+            ev_free[b].record(copy_stream)
+
+    def e2e_loop(n):
+        upload(0)
+        for i in range(n):
+            if i + 1 < n:
+                upload((i + 1) % 2)
+            run(i % 2)
+        stream.wait_stream(copy_stream)
+
+    e2e_loop(args.warmup)
     torch.cuda.synchronize()
     _barrier(world)
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record(stream)
-    for _ in range(args.steps):
-        e2e_step()
+    copy_stream.wait_event(a)  # the first upload starts inside the timed region
+    e2e_loop(args.steps)
     b.record(stream)
     torch.cuda.synchronize()
     e2e_ms = _max_over_ranks(a.elapsed_time(b), world)
