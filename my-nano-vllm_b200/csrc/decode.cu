@@ -195,8 +195,11 @@ __device__ __forceinline__ void cursor_set(Cursor<NT>& P, int item, const Decode
   P.rg = pair_local - P.kvh * nrg;
   P.c = c;
   P.nchunks = nchunks;
-  P.t0 = c * CT;
-  P.t1 = min(L, P.t0 + CT);
+  // the sequence's chunks are balanced (equal up to one tile) instead of CT, CT, ..., remainder,
+  // so no item is a short tail; the chunk count, which the combine uses, stays ceil(L / CT)
+  const int cts = ((L + nchunks - 1) / nchunks + kTile - 1) / kTile * kTile;
+  P.t0 = c * cts;
+  P.t1 = min(L, P.t0 + cts);
   P.t = P.t0;
   int nq = 1;
   P.qrow0 = b;
