@@ -10,18 +10,19 @@
 //
 // One CTA = one (q tile of 128 rows, NG q heads of one kv head, sequence): NG = 2 when the GQA
 // group is even, so two softmax warpgroups share every K/V tile and take turns on the tensor
-// cores (while one quantises its P, the MMAs of the other run).  Warps:
+// cores (while one computes its P, the MMAs of the other run).  Warps:
 //   warps 4g..4g+3  softmax group g, thread = query row of head g: converts its q row to e4m3
 //             hi + lo (power-of-two row scale), then per key tile reads its row of S from tensor
-//             memory twice (max, then p), quantises P = 16 * 2^(s - m) as e4m3 hi + lo, and
-//             finally divides the tensor-memory O row by its sum.  O is rescaled only when a row
-//             maximum grows by more than 2^4 (P stays <= 256, inside e4m3's range);
+//             memory twice (max, then P), writes P = 16 * 2^(s - m) as e4m3 hi + lo back into
+//             the S columns already read, and finally divides the tensor-memory O row by its
+//             sum.  O is rescaled only when a row maximum grows by more than 2^4 (P <= 256);
 //   warp 4 NG       TMA producer: 128-token K and V tiles (128-byte rows, 128B swizzle) into the
 //             ring; key tiles past the causal limit of the q tile's last row are never loaded;
 //   warp 4 NG + 1   MMA issuer (one thread), per tile and group:
-//               S_g  = [Qhi_g; Qlo_g] . K^T   two accumulating kind::f8f6f4 chains, M = N = 128
-//               O_g += [Phi_g; Plo_g] . V     V is read MN-major straight from its TMA tile
-//             S_g and O_g in tensor memory, P_g in shared memory (one buffer per group).
+//               O_g += [Phi_g; Plo_g] . V   two accumulating kind::f8f6f4 chains, P_g read from
+//                                           tensor memory, V MN-major straight from its TMA tile
+//               S_g  = [Qhi_g; Qlo_g] . K^T  two accumulating kind::f8f6f4 chains, M = N = 128
+//             in that order: P_g occupies S_g's columns until its PV has read it.
 #include <climits>
 
 #include "common.cuh"
@@ -45,11 +46,12 @@ struct PrefillTile {
 
 template <int NG>
 struct PrefillCfg {
-  static constexpr int kStages = NG == 2 ? 2 : 3;
-  static constexpr int kThreads = (4 * NG + 2) * 32;
+  static constexpr int kStages = 3;
   static constexpr int kProducerWarp = 4 * NG;
   static constexpr int kMmaWarp = 4 * NG + 1;
-  // tensor memory: group g's S at 256 g, its O at 256 g + 128
+  static constexpr int kThreads = (4 * NG + 2) * 32;
+  // tensor memory: group g's S (and its P, written over the columns already read) at 256 g,
+  // its O at 256 g + 128
   static constexpr uint32_t kTmemCols = NG == 2 ? 512 : 256;
 };
 
@@ -58,10 +60,8 @@ struct __align__(1024) PrefillSmem {
   static constexpr int kStages = PrefillCfg<NG>::kStages;
   uint8_t qhi[NG][kBM * 128];           // A operand of S: K-major SW128
   uint8_t qlo[NG][kBM * 128];
-  uint8_t k[kStages][kBN * 128];
+  uint8_t k[kStages][kBN * 128];        // TMA tiles, 128-byte rows, 128B swizzle
   uint8_t v[kStages][kBN * 128];
-  uint8_t phi[NG][kBM * 128];           // A operand of PV
-  uint8_t plo[NG][kBM * 128];
   PrefillTile tile[kStages];
   // general-path column table of the group's current tile (thread r fills column r): key and
   // value scales, and a validity bit per column
@@ -69,12 +69,11 @@ struct __align__(1024) PrefillSmem {
   float colv[NG][kBN];
   uint32_t colok[NG][kBN / 32];
   uint64_t kv_full[kStages];
-  uint64_t kv_empty[kStages];
+  uint64_t kv_empty[kStages];  // K and V read by every group's MMAs (one commit), header by the
+                               // softmax threads
   uint64_t q_full[NG];
-  uint64_t s_full[NG];
-  uint64_t s_empty[NG];
-  uint64_t p_full[NG];
-  uint64_t pv_done[NG];
+  uint64_t s_full[NG];         // S_g(j) ready (and, after the last tile, O_g final)
+  uint64_t p_full[NG];         // P_g(j) in tensor memory, O_g rescaled, invalid V rows zeroed
   uint32_t tmem_base;
 };
 static_assert(sizeof(PrefillSmem<2>) + 1024 <= 227 * 1024, "smem");
@@ -170,14 +169,12 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
   if (tid == 0) {
     for (int i = 0; i < kStages; ++i) {
       mbar_init(&sm.kv_full[i], 1);
-      mbar_init(&sm.kv_empty[i], 1);
+      mbar_init(&sm.kv_empty[i], 1 + 128 * NG);  // MMA commit, softmax threads
     }
     for (int g = 0; g < NG; ++g) {
       mbar_init(&sm.q_full[g], 128);
       mbar_init(&sm.s_full[g], 1);
-      mbar_init(&sm.s_empty[g], 128);
       mbar_init(&sm.p_full[g], 128);
-      mbar_init(&sm.pv_done[g], 1);
     }
     fence_mbar_init();
   }
@@ -194,12 +191,14 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
   tc::fence_after_sync();
   const uint32_t tmem = sm.tmem_base;
   const int ntiles = si.ntiles;
+  const bool kscaled = p.k_scale != nullptr;
+  const bool paged = p.block_tables != nullptr;
+  const int bs = p.block_size;
+  const int box_rows = box_rows_of(paged, bs);
+  const int box_shift = 31 - __clz(box_rows);
 
   if (warp == Cfg::kProducerWarp) {
     // ============================================================ TMA producer
-    const bool paged = p.block_tables != nullptr;
-    const int bs = p.block_size;
-    const int box_rows = box_rows_of(paged, bs);
     const int nbox = kBN / box_rows;
     const int64_t bt_row = static_cast<int64_t>(s) * p.bt_stride;
     int ebase = INT_MIN / 2, myent = -1;
@@ -263,38 +262,36 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
     }
   } else if (warp == Cfg::kMmaWarp) {
     // ============================================================ MMA issuer
-    // per tile j and group g in turn: S_g(j) once group g has read S_g(j-1), then PV_g(j-1)
-    // once P_g(j-1) is written; the stage of tile j-1 is released after every group's PV
+    // per tile j and group g in turn: PV_g(j-1) once P_g(j-1) is written (P lives in S_g's
+    // columns, so it must be read before the next S), then S_g(j); the tensor pipe runs one
+    // thread's MMAs in order.  The stage of tile j-1 is released after every group's PV.
     if (lane == 0 && ntiles > 0) {
       const uint32_t idesc_s = tc::idesc_e4m3(128, 128, false, false);
       const uint32_t idesc_pv = tc::idesc_e4m3(128, 128, false, true);
       bool ok = true;
       for (int g = 0; g < NG && ok; ++g) ok = mbar_wait(&sm.q_full[g], 0, p.err);
-      int stage = 0;
+      int stage = 0, prev_stage = 0;
       uint32_t phase = 0;
-      int prev_stage = 0;
       auto issue_pv = [&](int g, int jt, int st) -> bool {
         if (!mbar_wait(&sm.p_full[g], jt & 1, p.err)) return false;
         tc::fence_after_sync();
         const uint32_t va = smem_u32(&sm.v[st][0]);
-        const uint32_t pa[2] = {smem_u32(&sm.phi[g][0]), smem_u32(&sm.plo[g][0])};
+        const uint32_t pt = tmem + 256 * g;  // P_g: 32-key step ks has hi at 16 ks, lo at 16 ks + 8
 #pragma unroll
-        for (int plane = 0; plane < 2; ++plane)
+        for (int ks = 0; ks < 4; ++ks) {
+          const uint64_t bd = tc::smem_desc(va + ks * 32 * 128, 0, 1024, tc::kSw128);
 #pragma unroll
-          for (int ks = 0; ks < 4; ++ks) {
-            const uint64_t ad = tc::smem_desc(pa[plane] + ks * 32, 16, 1024, tc::kSw128);
-            const uint64_t bd = tc::smem_desc(va + ks * 32 * 128, 0, 1024, tc::kSw128);
-            tc::mma_f8(tmem + 256 * g + 128, ad, bd, idesc_pv, (jt > 0 || plane > 0 || ks > 0) ? 1u : 0u);
-          }
-        tc::commit(&sm.pv_done[g]);
+          for (int plane = 0; plane < 2; ++plane)
+            tc::mma_f8_ts(tmem + 256 * g + 128, pt + 16 * ks + 8 * plane, bd, idesc_pv,
+                          (jt > 0 || ks > 0 || plane > 0) ? 1u : 0u);
+        }
         return true;
       };
       for (int j = 0; ok && j < ntiles; ++j) {
-        if (!mbar_wait(&sm.kv_full[stage], phase, p.err)) break;
         const uint32_t ka = smem_u32(&sm.k[stage][0]);
         for (int g = 0; g < NG && ok; ++g) {
-          if (j > 0 && !mbar_wait(&sm.s_empty[g], (j - 1) & 1, p.err)) { ok = false; break; }
-          tc::fence_after_sync();
+          if (j > 0 && !issue_pv(g, j - 1, prev_stage)) { ok = false; break; }
+          if (g == 0 && !mbar_wait(&sm.kv_full[stage], phase, p.err)) { ok = false; break; }
           const uint32_t qh = smem_u32(&sm.qhi[g][0]), ql = smem_u32(&sm.qlo[g][0]);
 #pragma unroll
           for (int plane = 0; plane < 2; ++plane)
@@ -305,7 +302,6 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
               tc::mma_f8(tmem + 256 * g, ad, bd, idesc_s, (plane > 0 || ks > 0) ? 1u : 0u);
             }
           tc::commit(&sm.s_full[g]);
-          if (j > 0 && !issue_pv(g, j - 1, prev_stage)) { ok = false; break; }
         }
         if (!ok) break;
         if (j > 0) tc::commit(&sm.kv_empty[prev_stage]);
@@ -313,7 +309,10 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
         if (++stage == kStages) { stage = 0; phase ^= 1; }
       }
       if (ok) {
-        for (int g = 0; g < NG && ok; ++g) ok = issue_pv(g, ntiles - 1, prev_stage);
+        for (int g = 0; g < NG && ok; ++g) {
+          ok = issue_pv(g, ntiles - 1, prev_stage);
+          if (ok) tc::commit(&sm.s_full[g]);  // O_g final
+        }
         if (ok) tc::commit(&sm.kv_empty[prev_stage]);
       }
     }
@@ -331,8 +330,6 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
     const uint32_t o_tmem = s_tmem + 128;
     uint8_t* const qhi = sm.qhi[g];
     uint8_t* const qlo = sm.qlo[g];
-    uint8_t* const phi = sm.phi[g];
-    uint8_t* const plo = sm.plo[g];
     // ---- query row -> e4m3 hi / lo, 128B-swizzled K-major rows
     float cs;
     {
@@ -382,11 +379,6 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
     fence_proxy_async_smem();
     mbar_arrive(&sm.q_full[g]);
 
-    const bool kscaled = p.k_scale != nullptr;
-    const bool paged = p.block_tables != nullptr;
-    const int bs = p.block_size;
-    const int box_rows = box_rows_of(paged, bs);
-    const int box_shift = 31 - __clz(box_rows);
     float m_ref = -INFINITY;  // reference max of O and l (log2 units)
     float l = 0.f;
     int stage = 0;
@@ -403,6 +395,7 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
       // across the group's four warps)
       const int vlim = row_ok ? max(0, min(col_end, lim - j0 + 1)) : 0;
       const bool general = kscaled || !(p.scale_log2 > 0.f) || boxmask != (1u << (kBN / box_rows)) - 1u;
+      // S_g(j) complete => PV_g(j-1) complete (issued before it): O is quiescent
       if (!mbar_wait(&sm.s_full[g], j & 1, p.err)) { ok = false; break; }
       tc::fence_after_sync();
       if (general) {
@@ -423,138 +416,117 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
         if (lane == 0) sm.colok[g][warp & 3] = bal;
         named_barrier(1 + g, 128);
       }
-      // O and the P buffer are free once PV_g(j-1) is done
-      if (j >= 1) {
-        if (!mbar_wait(&sm.pv_done[g], (j - 1) & 1, p.err)) { ok = false; break; }
-        tc::fence_after_sync();
-      }
-      // ---- P = 16 * 2^(s - m_ref) as e4m3 hi + lo into the P buffer; returns the row sum of the
-      // same values.  On the fast path the largest P is tracked (packed f16) in *pmax.
-      auto write_p = [&](float bias, float* pmax) -> float {
-        float lt = 0.f;
-        __half2 mx = __float2half2_rn(0.f);
+      mbar_arrive(&sm.kv_empty[stage]);  // done with the tile's header and block list
+      // ---- pass 1: row maximum (of the raw scores on the fast path: cs > 0 commutes with max)
+      float tmax = -INFINITY;
 #pragma unroll 1
-        for (int c0 = 0; c0 < kBN; c0 += 32) {
-          float v[32];
-          tmem_ld32(s_tmem + c0, v);
-          tc::wait_ld();
-          uint32_t hw[8], lw[8];  // this chunk's P row: hi and lo e4m3 bytes, 4 per word
-          if (!general) {
-            // packed f16 pipeline: exponent argument to f16x2, one ex2 for two elements, split
-            // in f16x2, row sum in four f16x2 partials (values <= 256, four per partial)
-            __half2 lacc[4];
+      for (int c0 = 0; c0 < kBN; c0 += 32) {
+        float v[32];
+        tmem_ld32(s_tmem + c0, v);
+        tc::wait_ld();
+        if (!general && c0 + 32 <= vlim) {  // every column visible: four independent chains
+          float a0 = v[0], a1 = v[1], a2 = v[2], a3 = v[3];
 #pragma unroll
-            for (int k = 0; k < 4; ++k) lacc[k] = __float2half2_rn(0.f);
-            const bool full = c0 + 32 <= vlim;
-#pragma unroll
-            for (int k = 0; k < 16; ++k) {
-              float a0 = fmaf(v[2 * k], cs, bias), a1 = fmaf(v[2 * k + 1], cs, bias);
-              if (!full) {
-                a0 = c0 + 2 * k < vlim ? a0 : -INFINITY;
-                a1 = c0 + 2 * k + 1 < vlim ? a1 : -INFINITY;
-              }
-              const uint32_t pe = ex2_f16x2(pack_f16x2(a0, a1));
-              const __half2 ph = *reinterpret_cast<const __half2*>(&pe);
-              lacc[k & 3] = __hadd2(lacc[k & 3], ph);
-              mx = __hmax2(mx, ph);
-              uint32_t h2, l2;
-              split_f16x2_e4m3(pe, h2, l2);
-              if (k & 1) {
-                hw[k >> 1] |= h2 << 16;
-                lw[k >> 1] |= l2 << 16;
-              } else {
-                hw[k >> 1] = h2;
-                lw[k >> 1] = l2;
-              }
-            }
-            const __half2 ls = __hadd2(__hadd2(lacc[0], lacc[1]), __hadd2(lacc[2], lacc[3]));
-            lt += __low2float(ls) + __high2float(ls);
-          } else {
-            const uint32_t okw = sm.colok[g][c0 >> 5];
-            float la[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial sums
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const bool cok = ((okw >> i) & 1u) && c0 + i < vlim;
-              const float e = cok ? ex2(v[i] * sm.colk[g][c0 + i] * cs + bias) : 0.f;
-              la[i & 3] += e;
-              v[i] = e * sm.colv[g][c0 + i];
-            }
-            lt += (la[0] + la[1]) + (la[2] + la[3]);
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-              uint32_t ah, al, bh, bl;
-              split_pos_f32x2_e4m3(v[4 * k], v[4 * k + 1], ah, al);
-              split_pos_f32x2_e4m3(v[4 * k + 2], v[4 * k + 3], bh, bl);
-              hw[k] = ah | (bh << 16);
-              lw[k] = al | (bl << 16);
-            }
+          for (int i = 4; i < 32; i += 4) {
+            a0 = fmaxf(a0, v[i]);
+            a1 = fmaxf(a1, v[i + 1]);
+            a2 = fmaxf(a2, v[i + 2]);
+            a3 = fmaxf(a3, v[i + 3]);
           }
+          tmax = fmaxf(tmax, fmaxf(fmaxf(a0, a1), fmaxf(a2, a3)));
+        } else if (!general) {
 #pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            const int c = (c0 >> 4) + half;  // 16-byte chunk index within the 128-byte row
-            const int off = r * 128 + ((c ^ (r & 7)) << 4);
-            *reinterpret_cast<uint4*>(&phi[off]) =
-                make_uint4(hw[4 * half], hw[4 * half + 1], hw[4 * half + 2], hw[4 * half + 3]);
-            *reinterpret_cast<uint4*>(&plo[off]) =
-                make_uint4(lw[4 * half], lw[4 * half + 1], lw[4 * half + 2], lw[4 * half + 3]);
+          for (int i = 0; i < 32; ++i) tmax = fmaxf(tmax, c0 + i < vlim ? v[i] : -INFINITY);
+        } else {
+          const uint32_t okw = sm.colok[g][c0 >> 5];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const bool cok = ((okw >> i) & 1u) && c0 + i < vlim;
+            tmax = fmaxf(tmax, cok ? v[i] * sm.colk[g][c0 + i] * cs : -INFINITY);
           }
         }
-        *pmax = fmaxf(__low2float(mx), __high2float(mx));
-        return lt;
-      };
-      // ---- fast path: one pass against the current reference; a score more than 2^4 above it
-      // (P > 256) sends the warp through the exact two passes below (the same rescale rule)
-      float l_tile = 0.f;
-      bool exact = general || (vlim > 0 && m_ref == -INFINITY);  // a row's first visible keys
-      if (!__any_sync(0xffffffffu, exact)) {
-        float pmax;
-        l_tile = write_p(kPScaleLog2 - m_ref, &pmax);
-        exact = pmax > 256.f;
       }
+      if (!general && tmax != -INFINITY) tmax *= cs;
+      // lazy rescale: move the reference max only when it grows by more than 2^4, so that
+      // P = 16 * 2^(s - m_ref) <= 256
       float alpha = 1.f;
-      if (__any_sync(0xffffffffu, exact)) {
-        // ---- pass 1: row maximum (of the raw scores on the fast path: cs > 0 commutes with max)
-        float tmax = -INFINITY;
+      if (tmax > m_ref + kRescaleLog2) {
+        alpha = m_ref == -INFINITY ? 0.f : ex2(m_ref - tmax);
+        m_ref = tmax;
+        l *= alpha;
+      }
+      // ---- pass 2: P as e4m3 hi + lo into the S columns already read (chunk c0 of 32 keys ->
+      // hi in columns c0 / 2 .. + 8, lo in the next 8)
+      const float bias = kPScaleLog2 - (m_ref == -INFINITY ? 0.f : m_ref);
+      float l_tile = 0.f;
 #pragma unroll 1
-        for (int c0 = 0; c0 < kBN; c0 += 32) {
-          float v[32];
-          tmem_ld32(s_tmem + c0, v);
-          tc::wait_ld();
-          if (!general && c0 + 32 <= vlim) {  // every column visible: four independent chains
-            float a0 = v[0], a1 = v[1], a2 = v[2], a3 = v[3];
+      for (int c0 = 0; c0 < kBN; c0 += 32) {
+        float v[32];
+        tmem_ld32(s_tmem + c0, v);
+        tc::wait_ld();
+        uint32_t pw[16];  // hi words 0..7, lo words 8..15 (four e4m3 each)
+        if (!general) {
+          // exponent arguments as packed pairs; three pairs in four take the MUFU ex2, the
+          // fourth a polynomial on the FMA pipe (the MUFU rate bounds this loop); the row sum
+          // adds the fp32 values in four packed partials
+          const uint64_t cs2 = f2_pack(cs, cs), bias2 = f2_pack(bias, bias);
+          uint64_t la[4];
 #pragma unroll
-            for (int i = 4; i < 32; i += 4) {
-              a0 = fmaxf(a0, v[i]);
-              a1 = fmaxf(a1, v[i + 1]);
-              a2 = fmaxf(a2, v[i + 2]);
-              a3 = fmaxf(a3, v[i + 3]);
+          for (int k = 0; k < 4; ++k) la[k] = f2_pack(0.f, 0.f);
+          const bool full = c0 + 32 <= vlim;
+#pragma unroll
+          for (int k = 0; k < 16; ++k) {
+            float a0, a1;
+            f2_unpack(f2_fma(f2_pack(v[2 * k], v[2 * k + 1]), cs2, bias2), a0, a1);
+            if (!full) {
+              a0 = c0 + 2 * k < vlim ? a0 : -INFINITY;
+              a1 = c0 + 2 * k + 1 < vlim ? a1 : -INFINITY;
             }
-            tmax = fmaxf(tmax, fmaxf(fmaxf(a0, a1), fmaxf(a2, a3)));
-          } else if (!general) {
-#pragma unroll
-            for (int i = 0; i < 32; ++i) tmax = fmaxf(tmax, c0 + i < vlim ? v[i] : -INFINITY);
-          } else {
-            const uint32_t okw = sm.colok[g][c0 >> 5];
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const bool cok = ((okw >> i) & 1u) && c0 + i < vlim;
-              tmax = fmaxf(tmax, cok ? v[i] * sm.colk[g][c0 + i] * cs : -INFINITY);
+            float e0, e1;
+            if ((k & 3) == 3) {
+              exp2_poly_x2(a0, a1, e0, e1);
+            } else {
+              e0 = ex2(a0);
+              e1 = ex2(a1);
+            }
+            la[k & 3] = f2_add(la[k & 3], f2_pack(e0, e1));
+            uint32_t h2, l2;
+            split_f16x2_e4m3(pack_f16x2(e0, e1), h2, l2);
+            if (k & 1) {
+              pw[k >> 1] |= h2 << 16;
+              pw[8 + (k >> 1)] |= l2 << 16;
+            } else {
+              pw[k >> 1] = h2;
+              pw[8 + (k >> 1)] = l2;
             }
           }
+          float s0, s1;
+          f2_unpack(f2_add(f2_add(la[0], la[1]), f2_add(la[2], la[3])), s0, s1);
+          l_tile += s0 + s1;
+        } else {
+          const uint32_t okw = sm.colok[g][c0 >> 5];
+          float la[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial sums
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const bool cok = ((okw >> i) & 1u) && c0 + i < vlim;
+            const float e = cok ? ex2(v[i] * sm.colk[g][c0 + i] * cs + bias) : 0.f;
+            la[i & 3] += e;
+            v[i] = e * sm.colv[g][c0 + i];
+          }
+          l_tile += (la[0] + la[1]) + (la[2] + la[3]);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            uint32_t ah, al, bh, bl;
+            split_pos_f32x2_e4m3(v[4 * k], v[4 * k + 1], ah, al);
+            split_pos_f32x2_e4m3(v[4 * k + 2], v[4 * k + 3], bh, bl);
+            pw[k] = ah | (bh << 16);
+            pw[8 + k] = al | (bl << 16);
+          }
         }
-        if (!general && tmax != -INFINITY) tmax *= cs;
-        // lazy rescale: move the reference max only when it grows by more than 2^4
-        if (tmax > m_ref + kRescaleLog2) {
-          alpha = m_ref == -INFINITY ? 0.f : ex2(m_ref - tmax);
-          m_ref = tmax;
-          l *= alpha;
-        }
-        // ---- pass 2 (overwrites the fast pass's P)
-        float unused;
-        l_tile = write_p(kPScaleLog2 - (m_ref == -INFINITY ? 0.f : m_ref), &unused);
+        tc::st16u(s_tmem + (c0 >> 1), pw);
       }
       l += l_tile;
-      // O (quiescent: PV_g(j-1) done) follows a moved reference; each warp rescales its own rows
+      // O (quiescent) follows a moved reference; each warp rescales its own rows
       if (__any_sync(0xffffffffu, alpha != 1.f) && j > 0) {
 #pragma unroll
         for (int c0 = 0; c0 < 128; c0 += 16) {
@@ -565,10 +537,7 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
           for (int i = 0; i < 16; ++i) o16[i] *= alpha;
           tc::st16(o_tmem + c0, o16);
         }
-        tc::wait_st();
       }
-      tc::fence_before_sync();
-      mbar_arrive(&sm.s_empty[g]);
       // V rows of keys outside the sequence (or in masked blocks) may hold any bytes: zero them
       // (every group does, before its own PV; the bytes written are the same zeros)
       {
@@ -581,6 +550,7 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
         }
       }
       fence_proxy_async_smem();
+      tc::wait_st();
       tc::fence_before_sync();
       mbar_arrive(&sm.p_full[g]);
       if (++stage == kStages) { stage = 0; phase ^= 1; }
@@ -593,7 +563,7 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
       }
     }
     if (ntiles > 0 && ok) {
-      if (mbar_wait(&sm.pv_done[g], (ntiles - 1) & 1, p.err)) {
+      if (mbar_wait(&sm.s_full[g], ntiles & 1, p.err)) {
         tc::fence_after_sync();
         const float inv = l > 0.f ? 1.f / l : 0.f;  // O and l carry the same factor 16
 #pragma unroll
