@@ -47,9 +47,11 @@ struct PrefillTile {
 template <int NG>
 struct PrefillCfg {
   static constexpr int kStages = 3;
-  static constexpr int kProducerWarp = 4 * NG;
-  static constexpr int kMmaWarp = 4 * NG + 1;
-  static constexpr int kThreads = (4 * NG + 2) * 32;
+  static constexpr int kNH = 2;                      // warps per row quadrant (column halves)
+  static constexpr int kGroupThreads = 128 * kNH;    // softmax threads of one group
+  static constexpr int kProducerWarp = 4 * kNH * NG;
+  static constexpr int kMmaWarp = kProducerWarp + 1;
+  static constexpr int kThreads = (kProducerWarp + 2) * 32;
   // tensor memory: group g's S (and its P, written over the columns already read) at 256 g,
   // its O at 256 g + 128
   static constexpr uint32_t kTmemCols = NG == 2 ? 512 : 256;
@@ -71,9 +73,14 @@ struct __align__(1024) PrefillSmem {
   uint64_t kv_full[kStages];
   uint64_t kv_empty[kStages];  // K and V read by every group's MMAs (one commit), header by the
                                // softmax threads
+  // per-row values the two column halves of a group exchange (q amax, tile max, row sum)
+  float xq[NG][2][kBM];
+  float xmax[NG][2][kBM];
+  float xl[NG][2][kBM];
   uint64_t q_full[NG];
   uint64_t s_full[NG];         // S_g(j) ready (and, after the last tile, O_g final)
   uint64_t p_full[NG];         // P_g(j) in tensor memory, O_g rescaled, invalid V rows zeroed
+  uint64_t xch[NG];            // the group's exchanges (all its softmax threads)
   uint32_t tmem_base;
 };
 static_assert(sizeof(PrefillSmem<2>) + 1024 <= 227 * 1024, "smem");
@@ -146,6 +153,13 @@ __host__ __device__ constexpr int box_rows_of(bool paged, int bs) {
   return paged ? (bs % 128 == 0 ? 128 : bs % 64 == 0 ? 64 : bs % 32 == 0 ? 32 : 16) : kBN;
 }
 
+// Tensor-memory column of the P words of the 32-key chunk at key column c0 (hi: 8 columns, then
+// lo: 8): inside the 64 S columns of the chunk's half, over the first 32, which that half has
+// already read when it writes P.
+__device__ __forceinline__ constexpr uint32_t p_col(int c0) {
+  return static_cast<uint32_t>((c0 & ~63) + ((c0 & 63) >> 1));
+}
+
 template <int NG>
 __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
@@ -169,12 +183,13 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
   if (tid == 0) {
     for (int i = 0; i < kStages; ++i) {
       mbar_init(&sm.kv_full[i], 1);
-      mbar_init(&sm.kv_empty[i], 1 + 128 * NG);  // MMA commit, softmax threads
+      mbar_init(&sm.kv_empty[i], 1 + Cfg::kGroupThreads * NG);  // MMA commit, softmax threads
     }
     for (int g = 0; g < NG; ++g) {
-      mbar_init(&sm.q_full[g], 128);
+      mbar_init(&sm.q_full[g], Cfg::kGroupThreads);
       mbar_init(&sm.s_full[g], 1);
-      mbar_init(&sm.p_full[g], 128);
+      mbar_init(&sm.p_full[g], Cfg::kGroupThreads);
+      mbar_init(&sm.xch[g], Cfg::kGroupThreads);
     }
     fence_mbar_init();
   }
@@ -276,13 +291,13 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
         if (!mbar_wait(&sm.p_full[g], jt & 1, p.err)) return false;
         tc::fence_after_sync();
         const uint32_t va = smem_u32(&sm.v[st][0]);
-        const uint32_t pt = tmem + 256 * g;  // P_g: 32-key step ks has hi at 16 ks, lo at 16 ks + 8
+        const uint32_t pt = tmem + 256 * g;  // P_g: 32-key step ks at p_col(32 ks), hi then lo
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks) {
           const uint64_t bd = tc::smem_desc(va + ks * 32 * 128, 0, 1024, tc::kSw128);
 #pragma unroll
           for (int plane = 0; plane < 2; ++plane)
-            tc::mma_f8_ts(tmem + 256 * g + 128, pt + 16 * ks + 8 * plane, bd, idesc_pv,
+            tc::mma_f8_ts(tmem + 256 * g + 128, pt + p_col(32 * ks) + 8 * plane, bd, idesc_pv,
                           (jt > 0 || ks > 0 || plane > 0) ? 1u : 0u);
         }
         return true;
@@ -319,9 +334,15 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
     __syncwarp();
   } else {
     // ============================================================ softmax group g
-    const int g = warp >> 2;
+    // warp (g, half, quadrant): query rows 32 quadrant .. + 31 of head g, key columns
+    // 64 half .. + 63 of every tile (and the same half of each q and O row)
+    constexpr int kNH = Cfg::kNH;
+    constexpr int kCols = kBN / kNH;
+    const int g = warp / (4 * kNH);
+    const int half = (warp >> 2) & (kNH - 1);
+    const int cb = half * kCols;
     const int h = h0 + g;
-    const int r = tid & 127;         // query row within the tile
+    const int r = 32 * (warp & 3) + lane;  // query row within the tile
     const bool row_ok = r < rows;
     const int qi = q0 + r;           // query index within the sequence
     const int lim = qi + (si.nk - si.nq);  // largest visible key position of this row
@@ -330,18 +351,28 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
     const uint32_t o_tmem = s_tmem + 128;
     uint8_t* const qhi = sm.qhi[g];
     uint8_t* const qlo = sm.qlo[g];
-    // ---- query row -> e4m3 hi / lo, 128B-swizzled K-major rows
+    uint32_t xphase = 0;
+    // the group's exchange: every softmax thread arrives, then waits (bounded) for all
+    auto exchange = [&]() -> bool {
+      mbar_arrive(&sm.xch[g]);
+      const bool done = mbar_wait(&sm.xch[g], xphase, p.err);
+      xphase ^= 1;
+      return done;
+    };
+    // ---- query row -> e4m3 hi / lo, 128B-swizzled K-major rows (this half's dims)
     float cs;
+    bool ok = true;
     {
-      uint4 w[16];  // the row as packed bf16 pairs, all 16 loads in flight at once
+      constexpr int kW = 16 / kNH;  // 16-byte loads of this half (8 bf16 each)
+      uint4 w[kW];  // all loads in flight at once
       if (row_ok) {
         const uint4* src = reinterpret_cast<const uint4*>(
-            p.q + static_cast<int64_t>(si.q_begin + qi) * p.q_row_stride + static_cast<int64_t>(h) * 128);
+            p.q + static_cast<int64_t>(si.q_begin + qi) * p.q_row_stride + static_cast<int64_t>(h) * 128 + cb);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) w[i] = ldg_keep_v4(src + i);
+        for (int i = 0; i < kW; ++i) w[i] = ldg_keep_v4(src + i);
       } else {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) w[i] = make_uint4(0, 0, 0, 0);
+        for (int i = 0; i < kW; ++i) w[i] = make_uint4(0, 0, 0, 0);
       }
       auto widen = [&](const uint4& v, float* x) {
         const uint32_t ww[4] = {v.x, v.y, v.z, v.w};
@@ -353,20 +384,26 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
       };
       float amax = 0.f;
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
+      for (int i = 0; i < kW; ++i) {
         float x[8];
         widen(w[i], x);
 #pragma unroll
         for (int k = 0; k < 8; ++k) amax = fmaxf(amax, fabsf(x[k]));
       }
+      if (kNH > 1) {
+        sm.xq[g][half][r] = amax;
+        ok = exchange();
+        amax = fmaxf(sm.xq[g][0][r], sm.xq[g][1][r]);
+      }
       float srow;
       const float inv = pow2_inv_scale(amax, &srow);
       cs = srow * p.scale_log2;
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {  // 16 dims per 16-byte chunk
+      for (int cc = 0; cc < kW / 2; ++cc) {  // 16 dims per 16-byte chunk
+        const int c = cb / 16 + cc;
         float x[16];
-        widen(w[2 * c], x);
-        widen(w[2 * c + 1], x + 8);
+        widen(w[2 * cc], x);
+        widen(w[2 * cc + 1], x + 8);
 #pragma unroll
         for (int k = 0; k < 16; ++k) x[k] *= inv;
         uint4 hv, lv;
@@ -383,8 +420,7 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
     float l = 0.f;
     int stage = 0;
     uint32_t phase = 0;
-    bool ok = true;
-    for (int j = 0; j < ntiles; ++j) {
+    for (int j = 0; ok && j < ntiles; ++j) {
       if (!mbar_wait(&sm.kv_full[stage], phase, p.err)) { ok = false; break; }
       const int j0 = sm.tile[stage].j0;
       const uint32_t boxmask = sm.tile[stage].boxmask;  // boxes whose block is valid
@@ -399,28 +435,31 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
       if (!mbar_wait(&sm.s_full[g], j & 1, p.err)) { ok = false; break; }
       tc::fence_after_sync();
       if (general) {
-        // S_g(j) complete => the group finished tile j-1, the table's last reader
+        // S_g(j) complete => the group finished tile j-1, the table's last reader; the first
+        // column half fills it (thread r: column r)
         const int c = r;
-        const bool cok = c < col_end && ((boxmask >> (c >> box_shift)) & 1u);
-        float ks = 1.f, vs = 1.f;
-        if (kscaled && cok) {
-          const int kv = j0 + c;
-          const int64_t slot = paged ? static_cast<int64_t>(sm.tile[stage].blk[c >> box_shift]) * bs + (kv % bs)
-                                     : static_cast<int64_t>(si.k_begin) + kv;
-          ks = __ldg(p.k_scale + slot * p.num_kv_heads + kvh);
-          vs = __ldg(p.v_scale + slot * p.num_kv_heads + kvh);
+        if (half == 0) {
+          const bool cok = c < col_end && ((boxmask >> (c >> box_shift)) & 1u);
+          float ks = 1.f, vs = 1.f;
+          if (kscaled && cok) {
+            const int kv = j0 + c;
+            const int64_t slot = paged ? static_cast<int64_t>(sm.tile[stage].blk[c >> box_shift]) * bs + (kv % bs)
+                                       : static_cast<int64_t>(si.k_begin) + kv;
+            ks = __ldg(p.k_scale + slot * p.num_kv_heads + kvh);
+            vs = __ldg(p.v_scale + slot * p.num_kv_heads + kvh);
+          }
+          sm.colk[g][c] = ks;
+          sm.colv[g][c] = vs;
+          const uint32_t bal = __ballot_sync(0xffffffffu, cok);
+          if (lane == 0) sm.colok[g][warp & 3] = bal;
         }
-        sm.colk[g][c] = ks;
-        sm.colv[g][c] = vs;
-        const uint32_t bal = __ballot_sync(0xffffffffu, cok);
-        if (lane == 0) sm.colok[g][warp & 3] = bal;
-        named_barrier(1 + g, 128);
+        if (!exchange()) { ok = false; break; }
       }
       mbar_arrive(&sm.kv_empty[stage]);  // done with the tile's header and block list
       // ---- pass 1: row maximum (of the raw scores on the fast path: cs > 0 commutes with max)
       float tmax = -INFINITY;
 #pragma unroll 1
-      for (int c0 = 0; c0 < kBN; c0 += 32) {
+      for (int c0 = cb; c0 < cb + kCols; c0 += 32) {
         float v[32];
         tmem_ld32(s_tmem + c0, v);
         tc::wait_ld();
@@ -447,6 +486,11 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
         }
       }
       if (!general && tmax != -INFINITY) tmax *= cs;
+      if (kNH > 1) {  // the row's other half (its S reads are done once it arrives)
+        sm.xmax[g][half][r] = tmax;
+        if (!exchange()) { ok = false; break; }
+        tmax = fmaxf(sm.xmax[g][0][r], sm.xmax[g][1][r]);
+      }
       // lazy rescale: move the reference max only when it grows by more than 2^4, so that
       // P = 16 * 2^(s - m_ref) <= 256
       float alpha = 1.f;
@@ -455,12 +499,12 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
         m_ref = tmax;
         l *= alpha;
       }
-      // ---- pass 2: P as e4m3 hi + lo into the S columns already read (chunk c0 of 32 keys ->
-      // hi in columns c0 / 2 .. + 8, lo in the next 8)
+      // ---- pass 2: P as e4m3 hi + lo into this half's S columns already read (chunk c0 of 32
+      // keys -> hi in columns p_col(c0) .. + 8, lo in the next 8)
       const float bias = kPScaleLog2 - (m_ref == -INFINITY ? 0.f : m_ref);
       float l_tile = 0.f;
 #pragma unroll 1
-      for (int c0 = 0; c0 < kBN; c0 += 32) {
+      for (int c0 = cb; c0 < cb + kCols; c0 += 32) {
         float v[32];
         tmem_ld32(s_tmem + c0, v);
         tc::wait_ld();
@@ -523,13 +567,13 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
             pw[8 + k] = al | (bl << 16);
           }
         }
-        tc::st16u(s_tmem + (c0 >> 1), pw);
+        tc::st16u(s_tmem + p_col(c0), pw);
       }
       l += l_tile;
       // O (quiescent) follows a moved reference; each warp rescales its own rows
       if (__any_sync(0xffffffffu, alpha != 1.f) && j > 0) {
 #pragma unroll
-        for (int c0 = 0; c0 < 128; c0 += 16) {
+        for (int c0 = cb; c0 < cb + kCols; c0 += 16) {
           float o16[16];
           tc::ld16(o_tmem + c0, o16);
           tc::wait_ld();
@@ -544,9 +588,9 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
         const int kr = r;  // this thread also owns key row kr of the tile
         const bool kv_ok = kr < col_end && ((boxmask >> (kr >> box_shift)) & 1u);
         if (!kv_ok) {
-          uint4* vrow = reinterpret_cast<uint4*>(&sm.v[stage][kr * 128]);
+          uint4* vrow = reinterpret_cast<uint4*>(&sm.v[stage][kr * 128 + cb]);
 #pragma unroll
-          for (int i = 0; i < 8; ++i) vrow[i] = make_uint4(0, 0, 0, 0);
+          for (int i = 0; i < kCols / 16; ++i) vrow[i] = make_uint4(0, 0, 0, 0);
         }
       }
       fence_proxy_async_smem();
@@ -556,10 +600,15 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
       if (++stage == kStages) { stage = 0; phase ^= 1; }
     }
     // ---- epilogue: O / l -> fp16 -> bf16 (the reference's output path)
+    if (ntiles > 0 && ok && kNH > 1) {  // the row sum over both halves
+      sm.xl[g][half][r] = l;
+      ok = exchange();
+      l = sm.xl[g][0][r] + sm.xl[g][1][r];
+    }
     if (row_ok) {
-      uint16_t* dst = p.out + static_cast<int64_t>(si.q_begin + qi) * p.out_row_stride + h * 128;
+      uint16_t* dst = p.out + static_cast<int64_t>(si.q_begin + qi) * p.out_row_stride + h * 128 + cb;
       if (ntiles == 0 || !ok) {
-        for (int i = 0; i < 16; ++i) reinterpret_cast<uint4*>(dst)[i] = make_uint4(0, 0, 0, 0);
+        for (int i = 0; i < kCols / 8; ++i) reinterpret_cast<uint4*>(dst)[i] = make_uint4(0, 0, 0, 0);
       }
     }
     if (ntiles > 0 && ok) {
@@ -567,7 +616,7 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
         tc::fence_after_sync();
         const float inv = l > 0.f ? 1.f / l : 0.f;  // O and l carry the same factor 16
 #pragma unroll
-        for (int c0 = 0; c0 < 128; c0 += 16) {
+        for (int c0 = cb; c0 < cb + kCols; c0 += 16) {
           float o16[16];
           tc::ld16(o_tmem + c0, o16);
           tc::wait_ld();
