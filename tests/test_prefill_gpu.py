@@ -82,6 +82,32 @@ def test_prefill_config4_mixed_spec_and_fresh():
     _no_device_error()
 
 
+def test_prefill_long_context_with_score_spikes():
+    """Long cached contexts where chosen query rows meet a matching key late in the context: their
+    scores jump far above everything before (a reference move well after the first tiles, several
+    times per row, in both column halves of a row), against the fp32 oracle."""
+    from nanovllm_b200 import workloads
+    nqs, pre, bs = [300, 700, 129], [12000, 5000, 0], 256
+    c = workloads.prefill_case(nqs, pre, 8, 2, seed=11, device="cuda", block_size=bs,
+                               pool_factor=1.1)
+    _store_new_rows(c)
+    bt = c.block_tables.cpu()
+    cq = c.cu_seqlens_q.cpu()
+    g = 8 // 2
+    plants = [(0, 299, 1, [700, 6000, 9000, 11500], [0.5, 1.0, 1.5, 2.0]),   # last row, head 1
+              (0, 150, 4, [3000, 11999], [1.0, 3.0]),                         # mid row, head 4
+              (1, 699, 6, [100, 2500, 4999], [0.7, 1.4, 2.5])]                # seq 1, head 6
+    for s, row, h, positions, gains in plants:
+        qrow = c.q[int(cq[s]) + row, h].float()
+        for pos, gain in zip(positions, gains):
+            blk, off = int(bt[s, pos // bs]), pos % bs
+            c.k[blk, off, h // g] = (gain * qrow).to(torch.float8_e4m3fn)
+    out = _prefill(c.q, c.k, c.v, c.block_tables, c.cu_seqlens_q, c.cu_seqlens_k, c.max_seqlen_q,
+                   c.max_seqlen_k, c.scale)
+    assert_close(out, _oracle(c), what="long context with score spikes")
+    _no_device_error()
+
+
 @pytest.mark.parametrize("bs", [16, 32, 64, 256])
 @pytest.mark.parametrize("hq,kvh", [(4, 4), (8, 2), (16, 2), (12, 4), (24, 4)])  # + GQA 3, 6
 def test_prefill_paged_edge_cases(bs, hq, kvh):
