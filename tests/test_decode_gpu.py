@@ -71,6 +71,32 @@ def test_decode_edge_cases(bs, hq, kvh, min_chunk):
     _no_device_error()
 
 
+@pytest.mark.parametrize("min_chunk", [128, 32768])
+def test_decode_score_spikes(min_chunk):
+    """Keys planted to match chosen query heads late in long contexts: their scores jump far
+    above everything before (the reference moves inside an item, or between the chunks the
+    combine merges), against the fp32 oracle."""
+    from nanovllm_b200 import workloads
+    lens = [20000, 9000, 4000, 300, 16000, 2500]
+    c = workloads.decode_case(len(lens), 32, 8, 0, 0, seed=21, device="cuda", block_size=256,
+                              pool_factor=1.1, lens=lens)
+    bt = c.block_tables.cpu()
+    g = 32 // 8
+    plants = [(0, 5, [100, 9000, 19999], [0.6, 1.2, 2.5]), (1, 31, [8999], [3.0]),
+              (2, 0, [10, 3000], [1.0, 2.0]), (4, 17, [2000, 8000, 15000], [0.8, 1.6, 2.4])]
+    for b, h, positions, gains in plants:
+        qrow = c.q[b, h].float()
+        for pos, gain in zip(positions, gains):
+            c.k_cache[int(bt[b, pos // 256]), pos % 256, h // g] = (gain * qrow).to(torch.float8_e4m3fn)
+    prev = _lib().fp8attn_set_decode_min_chunk(min_chunk)
+    try:
+        out = _decode((c.q, c.k_cache, c.v_cache, c.block_tables, c.context_lens, c.scale))
+    finally:
+        _lib().fp8attn_set_decode_min_chunk(prev)
+    assert_close(out, _oracle_case(c), what=f"score spikes, min chunk {min_chunk}")
+    _no_device_error()
+
+
 def test_decode_nan_bytes_beyond_context_are_ignored():
     # slots past each context hold NaN codes (0x7F): they must not leak into the output
     from nanovllm_b200 import workloads
