@@ -1,7 +1,7 @@
 // Shared device helpers for the FP8 PagedAttention kernels (sm_100a).
 //
-// Everything here is a thin wrapper over one PTX instruction (mbarrier, TMA, bulk copy,
-// mma.sync, movmatrix, tcgen05) or a small integer helper.  Every wait on an mbarrier is
+// Everything here is a thin wrapper over one PTX instruction (mbarrier, TMA, cp.async,
+// conversions, packed f32x2 arithmetic) or a small numeric helper.  Every wait on an mbarrier is
 // bounded by wall-clock time (%globaltimer): when the bound is hit the waiter records an error
 // code in a global flag and gives up, so a logic error cannot hang the GPU.
 #pragma once
@@ -96,7 +96,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
 }
 
 // ---------------------------------------------------------------------------------------------
-// TMA (no multicast anywhere in this library) and bulk copies
+// TMA (no multicast anywhere in this library)
 // ---------------------------------------------------------------------------------------------
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar,
                                             int x, int y) {
@@ -111,56 +111,10 @@ __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
-// 1-D bulk copy global -> shared; both addresses 16-byte aligned, bytes a multiple of 16.
-__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
-                                          uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
-          "r"(smem_u32(dst)),
-      "l"(src), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
-}
-
 // Order this thread's generic-proxy shared-memory writes before later async-proxy reads
 // (tensor-core operand fetches).
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-
-// ---------------------------------------------------------------------------------------------
-// Warp-level tensor-core MMA (used by the HBM-bound decode engine)
-// ---------------------------------------------------------------------------------------------
-__device__ __forceinline__ void mma_f16_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0,
-                                              uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-// D += A.B with e4m3 operands (m16n8k32, fp32 accumulate).  Fragment layout (g = lane / 4,
-// t = lane % 4): a0 = A[g][4t..4t+3], a1 = A[g+8][4t..4t+3], a2 = A[g][4t+16..], a3 = A[g+8][4t+16..]
-// (byte i = column +i); b0 = B[4t..4t+3][g], b1 = B[4t+16..4t+19][g]; c as for m16n8k16.
-__device__ __forceinline__ void mma_e4m3_16832(float (&c)[4], const uint32_t (&a)[4], uint32_t b0,
-                                               uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k32.row.col.f32.e4m3.e4m3.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
-  uint32_t y;
-  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
-  return y;
-}
-
-__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
-  uint32_t d;
-  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
-  return d;
 }
 
 // Two e4m3 bytes (low byte -> low half) to f16x2; exact.
@@ -217,23 +171,9 @@ __device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// bf16x2 (as raw 32 bits) -> f16x2, through fp32 (exact widening, one RNE narrowing).
-__device__ __forceinline__ uint32_t bf16x2_to_f16x2(uint32_t v) {
-  float lo = __uint_as_float(v << 16);
-  float hi = __uint_as_float(v & 0xFFFF0000u);
-  return pack_f16x2(lo, hi);
-}
-
 __device__ __forceinline__ float lg2(float x) {
   float y;
   asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
-// 2^x on both halves of an f16x2 (one MUFU operation for two elements).
-__device__ __forceinline__ uint32_t ex2_f16x2(uint32_t x) {
-  uint32_t y;
-  asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(x));
   return y;
 }
 
@@ -323,11 +263,6 @@ __device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
                : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
                : "r"(addr));
   return v;
-}
-
-// Named barrier over a subset of warps (id 1..15; id 0 is __syncthreads).
-__device__ __forceinline__ void named_barrier(int id, int nthreads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
 }  // namespace fp8attn
