@@ -46,7 +46,7 @@ struct PrefillTile {
 
 template <int NG>
 struct PrefillCfg {
-  static constexpr int kStages = 3;
+  static constexpr int kStages = 2;
   static constexpr int kNH = 2;                      // warps per row quadrant (column halves)
   static constexpr int kGroupThreads = 128 * kNH;    // softmax threads of one group
   static constexpr int kProducerWarp = 4 * kNH * NG;
@@ -510,9 +510,9 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
         tc::wait_ld();
         uint32_t pw[16];  // hi words 0..7, lo words 8..15 (four e4m3 each)
         if (!general) {
-          // exponent arguments as packed pairs; three pairs in four take the MUFU ex2, the
-          // fourth a polynomial on the FMA pipe (the MUFU rate bounds this loop); the row sum
-          // adds the fp32 values in four packed partials
+          // exponent arguments as packed pairs; every third pair (5 of the 16) takes a
+          // polynomial on the FMA pipe, the others the MUFU ex2 (whose rate bounds this loop);
+          // the row sum adds the fp32 values in four packed partials
           const uint64_t cs2 = f2_pack(cs, cs), bias2 = f2_pack(bias, bias);
           uint64_t la[4];
 #pragma unroll
@@ -527,7 +527,7 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
               a1 = c0 + 2 * k + 1 < vlim ? a1 : -INFINITY;
             }
             float e0, e1;
-            if ((k & 3) == 3) {
+            if (k % 3 == 2) {
               exp2_poly_x2(a0, a1, e0, e1);
             } else {
               e0 = ex2(a0);
