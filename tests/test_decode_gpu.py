@@ -1,6 +1,6 @@
 """Decode engine parity: reference golden outputs, the fp32 oracle on the benchmark configs and on
-edge cases (ragged lengths, zero lengths, -1 padding, block sizes 16..256, GQA 1..16, split-KV
-chunking), scaled caches, and CUDA-graph capture."""
+edge cases (ragged lengths, zero lengths, -1 padding, block sizes 16..512, GQA 1..16, split-KV
+chunking, a 128k-token sequence), scaled caches, and CUDA-graph capture."""
 import pytest
 import torch
 
@@ -54,7 +54,8 @@ def test_decode_config1():
 @pytest.mark.parametrize("min_chunk", [128, 512])
 @pytest.mark.parametrize("bs,hq,kvh", [(16, 4, 4), (32, 8, 2), (64, 16, 1), (256, 32, 8),
                                        (48, 8, 8), (80, 32, 2), (256, 64, 8),
-                                       (64, 12, 4), (128, 48, 8)])  # GQA 3 and 6
+                                       (64, 12, 4), (128, 48, 8),  # GQA 3 and 6
+                                       (512, 32, 8)])
 def test_decode_edge_cases(bs, hq, kvh, min_chunk):
     from nanovllm_b200 import workloads
     lens = [0, 1, bs - 1, bs, bs + 1, 63, 64, 65, 3 * bs + 17, 700, -5, 1000]
@@ -94,6 +95,18 @@ def test_decode_score_spikes(min_chunk):
     finally:
         _lib().fp8attn_set_decode_min_chunk(prev)
     assert_close(out, _oracle_case(c), what=f"score spikes, min chunk {min_chunk}")
+    _no_device_error()
+
+
+def test_decode_single_long_sequence_many_chunks():
+    """A 128k-token sequence next to a short one: each of its (sequence, kv head) pairs splits
+    into hundreds of chunks, the producer refreshes its block-table window many times, and the
+    combine merges the chunks over more than one round of its staged weights."""
+    from nanovllm_b200 import workloads
+    c = workloads.decode_case(2, 32, 8, 0, 0, seed=33, device="cuda", block_size=256,
+                              lens=[131072, 37])
+    out = _decode((c.q, c.k_cache, c.v_cache, c.block_tables, c.context_lens, c.scale))
+    assert_close(out, _oracle_case(c), what="128k-token sequence")
     _no_device_error()
 
 

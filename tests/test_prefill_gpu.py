@@ -1,7 +1,7 @@
 """Prefill entry point parity: reference golden outputs (paged and contiguous layouts, long and
 speculative-verify sized query sequences), the fp32 oracle on benchmark configs 3 and 4 at full
 size, and edge cases (query tiles straddling 128 rows, nk < nq, empty sequences, block sizes
-16..256, GQA 1..8, NaN bytes outside the context, scaled caches)."""
+16..512, GQA 1..8, NaN bytes outside the context, scaled caches)."""
 import pytest
 import torch
 
@@ -108,7 +108,7 @@ def test_prefill_long_context_with_score_spikes():
     _no_device_error()
 
 
-@pytest.mark.parametrize("bs", [16, 32, 64, 256])
+@pytest.mark.parametrize("bs", [16, 32, 64, 256, 512])
 @pytest.mark.parametrize("hq,kvh", [(4, 4), (8, 2), (16, 2), (12, 4), (24, 4)])  # + GQA 3, 6
 def test_prefill_paged_edge_cases(bs, hq, kvh):
     from nanovllm_b200 import workloads
