@@ -8,10 +8,11 @@
 // A row group is up to R = 8*NT query rows that share one kv head (GQA: the group's q heads,
 // times the sequence's query tokens in spec mode), so each K/V byte is read from HBM once per
 // row group -- once in total for decode.  Every CTA first computes the same plan from the
-// sequence lengths (chunk size, item prefix sums in shared memory), then a persistent grid pulls
-// items from an atomic counter.  An item whose (sequence, kv head, row group) has more than one
-// chunk writes an unnormalised partial (O, reference max, row sum); combine_kernel, launched
-// after, merges them using the plan CTA 0 publishes.
+// sequence lengths (chunk size, item prefix sums in shared memory: per sequence, or for large
+// batches per range of sequences), then a persistent grid pulls items from an atomic counter.
+// An item whose (sequence, kv head, row group) has more than one chunk writes an unnormalised
+// partial (O, reference max, row sum); combine_kernel, launched after, merges them using the
+// plan CTA 0 publishes.
 //
 // Two CTAs per SM, eight warps each (warps 6-7 have no role; they balance the register file
 // across the four schedulers):
@@ -99,15 +100,23 @@ struct __align__(1024) DecodeSmem {
   uint32_t tmem_base;
   int scratch[16];
   unsigned long long total_work;
-  // followed in shared memory by int prefix[num_seqs + 1] (item prefix sums over sequences)
-  // and int info[num_seqs] ((L << 7) | rowgroups per sequence), sized per launch
+  // followed in shared memory by the plan, sized per launch:
+  //   per sequence: int prefix[num_seqs + 1] (item prefix sums) and int info[num_seqs]
+  //                 ((L << 7) | row groups);
+  //   sampled (batches whose per-sequence arrays would leave room for one CTA per SM only):
+  //                 the same two arrays over the kThreads ranges of `per` sequences that the plan
+  //                 threads own -- prefix[kThreads + 1] at each range's first sequence, and info
+  //                 of that sequence -- so the size no longer grows with the batch
 };
 
 // Two CTAs share an SM (228 KB of shared memory, 1 KB reserved per CTA) with the plan arrays of
-// up to 256 sequences (larger batches run one CTA per SM).
+// up to 256 sequences, and at any batch size with the sampled plan.
 static_assert(sizeof(DecodeSmem<1>) + 2 * 1024 + (2 * 256 + 1) * 4 <= 228 * 1024 / 2, "smem");
 static_assert(sizeof(DecodeSmem<2>) + 2 * 1024 + (2 * 256 + 1) * 4 <= 228 * 1024 / 2, "smem");
 static_assert(sizeof(DecodeSmem<3>) + 2 * 1024 + (2 * 256 + 1) * 4 <= 228 * 1024 / 2, "smem");
+// sequences per range of the sampled plan, at most: they fit the lanes of the producer warp
+constexpr int kMaxPlanPer = (kMaxSeqs + kThreads - 1) / kThreads;
+static_assert(kMaxPlanPer <= 32 && 2 * kThreads + 1 <= 2 * 256 + 1, "sampled plan");
 
 __device__ __forceinline__ int seq_len_clamped(const DecodeParams& p, int b, int* nq_out) {
   int L, nq;
@@ -123,6 +132,11 @@ __device__ __forceinline__ int seq_len_clamped(const DecodeParams& p, int b, int
   L = L < 0 ? 0 : (L > cap ? cap : L);
   *nq_out = nq;
   return L;
+}
+
+// Row groups of R query rows of a sequence with nq query tokens and L key positions.
+__device__ __forceinline__ int seq_rowgroups(int L, int nq, int group, int R) {
+  return L > 0 ? (nq * group + R - 1) / R : 0;
 }
 
 // Block-wide exclusive scan of one int per thread.
@@ -167,26 +181,58 @@ struct Cursor {
 };
 
 // Claims `item` for the cursor and starts the load of its first 32 block-table entries (one
-// per lane).
-template <int NT>
+// per lane).  Called by the whole producer warp.  With the sampled plan, a search finds the
+// item's range of `per` sequences and the lanes read that range's lengths (one sequence each)
+// to find its sequence.
+template <int NT, bool kSampled>
 __device__ __forceinline__ void cursor_set(Cursor<NT>& P, int item, const DecodeParams& p,
-                                           const int* prefix, const int* info, int total_items,
-                                           int CT, int B) {
+                                           const int* prefix, const int* info, int per,
+                                           int total_items, int CT, int B) {
   constexpr int R = DecodeSmem<NT>::R;
   P.item = item;
   if (item >= total_items) return;
-  int lo = 0, hi = B - 1;  // largest b with prefix[b] <= item
+  const int nranges = kSampled ? (B + per - 1) / per : B;
+  int lo = 0, hi = nranges - 1;  // largest range (or sequence) with prefix <= item
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
     if (prefix[mid] <= item) lo = mid; else hi = mid - 1;
   }
-  const int b = lo;
-  const int inf = info[b];
-  const int L = inf >> 7, nrg = inf & 127;
+  int b, L, nrg, r;
+  if (!kSampled || per == 1) {  // the range is one sequence
+    b = lo;
+    const int inf = info[b];
+    L = inf >> 7;
+    nrg = inf & 127;
+    r = item - prefix[b];
+  } else {
+    const int lane = threadIdx.x & 31;
+    const int bl = lo * per + lane;
+    int Ll = 0, nql = 0;
+    if (lane < per && bl < B) Ll = seq_len_clamped(p, bl, &nql);
+    const int rgl = seq_rowgroups(Ll, nql, p.group, R);
+    const int cnt = (Ll + CT - 1) / CT * p.num_kv_heads * rgl;
+    int incl = cnt;
+#pragma unroll
+    for (int o = 1; o < kMaxPlanPer; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    const int first = prefix[lo] + incl - cnt;
+    const unsigned hit = __ballot_sync(0xffffffffu, cnt > 0 && item >= first && item < first + cnt);
+    if (hit == 0) {  // cannot happen with a consistent plan: report it, take no work
+      if (lane == 0) atomicExch(p.ctrl, kDevErrWorkspace);
+      P.item = total_items;
+      return;
+    }
+    const int src = __ffs(hit) - 1;
+    b = lo * per + src;
+    L = __shfl_sync(0xffffffffu, Ll, src);
+    nrg = __shfl_sync(0xffffffffu, rgl, src);
+    r = item - __shfl_sync(0xffffffffu, first, src);
+  }
   const int nchunks = (L + CT - 1) / CT;
   // items of sequence b: chunk-major, then kv head, then row group, so the CTAs that start
   // at about the same time read the same token rows (neighbouring heads share DRAM pages)
-  const int r = item - prefix[b];
   const int npairs = p.num_kv_heads * nrg;
   const int c = r / npairs;
   const int pair_local = r - c * npairs;
@@ -304,7 +350,7 @@ __device__ __forceinline__ void prepare_q(const Cursor<NT>& P, int slot, const D
   }
 }
 
-template <int NT, int RV>
+template <int NT, int RV, bool kSampled>
 __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
     decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                   const DecodeParams p) {
@@ -323,7 +369,7 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
   const int G = p.group;
   const int B = p.num_seqs;
   int* prefix = reinterpret_cast<int*>(&sm + 1);
-  int* info = prefix + (B + 1);
+  int* info = prefix + (kSampled ? kThreads : B) + 1;
 
   if (tid == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -361,12 +407,24 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
   const int per = (B + kThreads - 1) / kThreads;
   const int s0 = min(B, tid * per), s1 = min(B, s0 + per);
   long long my_work = 0;
-  for (int b = s0; b < s1; ++b) {
-    int nq;
-    const int L = seq_len_clamped(p, b, &nq);
-    const int rg = L > 0 ? (nq * G + R - 1) / R : 0;
-    info[b] = (L << 7) | rg;
-    my_work += static_cast<long long>(L) * rg;
+  // sampled plan: the thread's lengths and row groups, read once and kept in registers
+  int len_r[kSampled ? kMaxPlanPer : 1], rg_r[kSampled ? kMaxPlanPer : 1];
+  if constexpr (kSampled) {
+#pragma unroll
+    for (int i = 0; i < kMaxPlanPer; ++i) {
+      int nq = 0;
+      len_r[i] = s0 + i < s1 ? seq_len_clamped(p, s0 + i, &nq) : 0;
+      rg_r[i] = seq_rowgroups(len_r[i], nq, G, R);
+      my_work += static_cast<long long>(len_r[i]) * rg_r[i];
+    }
+  } else {
+    for (int b = s0; b < s1; ++b) {
+      int nq;
+      const int L = seq_len_clamped(p, b, &nq);
+      const int rg = seq_rowgroups(L, nq, G, R);
+      info[b] = (L << 7) | rg;
+      my_work += static_cast<long long>(L) * rg;
+    }
   }
   tc::fence_before_sync();
   __syncthreads();
@@ -383,27 +441,53 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
   const int CT = static_cast<int>(ct > (1 << 24) ? (1 << 24) : ct);
 
   int my_items = 0;
-  for (int b = s0; b < s1; ++b) {
-    const int inf = info[b];
-    my_items += (((inf >> 7) + CT - 1) / CT) * p.num_kv_heads * (inf & 127);
+  if constexpr (kSampled) {
+#pragma unroll
+    for (int i = 0; i < kMaxPlanPer; ++i)
+      my_items += (len_r[i] + CT - 1) / CT * p.num_kv_heads * rg_r[i];
+  } else {
+    for (int b = s0; b < s1; ++b) {
+      const int inf = info[b];
+      my_items += (((inf >> 7) + CT - 1) / CT) * p.num_kv_heads * (inf & 127);
+    }
   }
   int total_items;
   const int base = block_exclusive_scan(my_items, sm.scratch, &total_items);
-  {
-    int acc = base;
-    for (int b = s0; b < s1; ++b) {
-      prefix[b] = acc;
-      const int inf = info[b];
-      acc += (((inf >> 7) + CT - 1) / CT) * p.num_kv_heads * (inf & 127);
+  if constexpr (kSampled) {
+    prefix[tid] = base;
+    if (tid == kThreads - 1) prefix[kThreads] = total_items;
+    info[tid] = (len_r[0] << 7) | rg_r[0];
+    if (blockIdx.x == 0) {  // the combine kernel reads each sequence's item prefix after this launch
+      int acc = base;
+#pragma unroll
+      for (int i = 0; i < kMaxPlanPer; ++i) {
+        if (s0 + i < s1) p.plan[2 + s0 + i] = acc;
+        acc += (len_r[i] + CT - 1) / CT * p.num_kv_heads * rg_r[i];
+      }
+      if (tid == 0) {
+        p.plan[0] = CT;
+        p.plan[1] = total_items;
+        p.plan[2 + B] = total_items;
+      }
     }
-    if (tid == kThreads - 1) prefix[B] = total_items;
-  }
-  __syncthreads();
-  if (blockIdx.x == 0) {  // the combine kernel reads the same plan after this launch
-    for (int b = tid; b <= B; b += kThreads) p.plan[2 + b] = prefix[b];
-    if (tid == 0) {
-      p.plan[0] = CT;
-      p.plan[1] = total_items;
+    __syncthreads();
+  } else {
+    {
+      int acc = base;
+      for (int b = s0; b < s1; ++b) {
+        prefix[b] = acc;
+        const int inf = info[b];
+        acc += (((inf >> 7) + CT - 1) / CT) * p.num_kv_heads * (inf & 127);
+      }
+      if (tid == kThreads - 1) prefix[B] = total_items;
+    }
+    __syncthreads();
+    if (blockIdx.x == 0) {  // the combine kernel reads the same plan after this launch
+      for (int b = tid; b <= B; b += kThreads) p.plan[2 + b] = prefix[b];
+      if (tid == 0) {
+        p.plan[0] = CT;
+        p.plan[1] = total_items;
+      }
     }
   }
   // partial results are indexed by item id; a workspace sized by decode_workspace_bytes always
@@ -414,8 +498,13 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
 
   // zero the outputs of routed sequences without key positions (reference: acc / max(s, 1e-10))
   for (int b = blockIdx.x; b < B; b += gridDim.x) {
-    if ((info[b] >> 7) != 0) continue;
     int nq = 1, qrow0 = b;
+    if constexpr (kSampled) {
+      if (per == 1 ? (info[b] >> 7) != 0 : seq_len_clamped(p, b, &nq) != 0) continue;
+      nq = 1;
+    } else {
+      if ((info[b] >> 7) != 0) continue;
+    }
     if (p.spec_mode) {
       qrow0 = __ldg(p.cu_q + b);
       nq = __ldg(p.cu_q + b + 1) - qrow0;
@@ -443,8 +532,8 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
       }
       ids[0] = __shfl_sync(0xffffffffu, ids[0], 0);
       ids[1] = __shfl_sync(0xffffffffu, ids[1], 0);
-      cursor_set<NT>(P, ids[0], p, prefix, info, total_items, CT, B);
-      cursor_set<NT>(Pn, ids[1], p, prefix, info, total_items, CT, B);
+      cursor_set<NT, kSampled>(P, ids[0], p, prefix, info, per, total_items, CT, B);
+      cursor_set<NT, kSampled>(Pn, ids[1], p, prefix, info, per, total_items, CT, B);
       if (P.item < total_items) stage_q<NT>(P, p, sm.qstage);
     }
     int stage = 0;
@@ -529,7 +618,7 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
         P = Pn;
         P.nth = nth;
         if (lane == 0) Pn.next = atomicAdd(p.ctrl + 1, 1);
-        if (P.item < total_items) cursor_set<NT>(Pn, nxt, p, prefix, info, total_items, CT, B);
+        if (P.item < total_items) cursor_set<NT, kSampled>(Pn, nxt, p, prefix, info, per, total_items, CT, B);
         else Pn.item = total_items;
       }
     }
@@ -977,23 +1066,36 @@ int sm_count() {
 }
 
 template <int NT>
-size_t decode_smem_bytes(int num_seqs) {
-  // + alignment slack, + the per-launch plan arrays (prefix[B + 1], info[B])
-  return sizeof(DecodeSmem<NT>) + 1024 + static_cast<size_t>(2 * num_seqs + 1) * sizeof(int);
+size_t decode_smem_bytes(int num_seqs, bool sampled) {
+  // + alignment slack, + the per-launch plan arrays (prefix, info)
+  const int plan_ints = sampled ? 2 * kThreads + 1 : 2 * num_seqs + 1;
+  return sizeof(DecodeSmem<NT>) + 1024 + static_cast<size_t>(plan_ints) * sizeof(int);
 }
 
-// Persistent grid for this launch: as many CTAs as fit on every SM (at most kMaxCtasPerSm; tensor
-// memory per CTA is at most 256 columns, so it never limits).
+using DecodeKernelFn = void (*)(CUtensorMap, CUtensorMap, DecodeParams);
+
+struct DecodeShape {
+  DecodeKernelFn fn;
+  int grid;
+  size_t smem;
+};
+
+// The launch of this batch: the per-sequence plan while two CTAs still fit on an SM with it,
+// else the sampled one; a persistent grid of as many CTAs as fit on every SM (at most
+// kMaxCtasPerSm; tensor memory per CTA is at most 256 columns, so it never limits).
 template <int NT, int RV>
-int decode_grid_for(int num_seqs) {
+DecodeShape decode_shape(int num_seqs) {
   static bool configured[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !configured[dev]) {
-    cudaFuncSetAttribute(decode_kernel<NT, RV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         static_cast<int>(decode_smem_bytes<NT>(kMaxSeqs)));
+    cudaFuncSetAttribute(decode_kernel<NT, RV, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(decode_smem_bytes<NT>(kMaxSeqs, false)));
+    cudaFuncSetAttribute(decode_kernel<NT, RV, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(decode_smem_bytes<NT>(0, true)));
     // all of the unified L1/shared storage as shared memory: two CTAs' rings must fit
-    cudaFuncSetAttribute(decode_kernel<NT, RV>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    cudaFuncSetAttribute(decode_kernel<NT, RV, false>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    cudaFuncSetAttribute(decode_kernel<NT, RV, true>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     configured[dev] = true;
   }
   // The occupancy calculator reports 1 for every kernel that allocates tensor memory, so the
@@ -1003,14 +1105,20 @@ int decode_grid_for(int num_seqs) {
   int smem_sm = 0, resv = 0;
   cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
   cudaDeviceGetAttribute(&resv, cudaDevAttrReservedSharedMemoryPerBlock, dev);
+  const bool sampled = static_cast<int>(decode_smem_bytes<NT>(num_seqs, false)) + resv >
+                       smem_sm / kMaxCtasPerSm;
+  DecodeShape sh;
+  sh.fn = sampled ? decode_kernel<NT, RV, true> : decode_kernel<NT, RV, false>;
+  sh.smem = decode_smem_bytes<NT>(num_seqs, sampled);
   cudaFuncAttributes fa;
-  cudaFuncGetAttributes(&fa, decode_kernel<NT, RV>);
-  const int per_cta_smem = static_cast<int>(decode_smem_bytes<NT>(num_seqs)) + resv;
+  cudaFuncGetAttributes(&fa, sh.fn);
+  const int per_cta_smem = static_cast<int>(sh.smem) + resv;
   int occ = per_cta_smem > 0 ? smem_sm / per_cta_smem : 1;
   const int by_regs = fa.numRegs > 0 ? 65536 / (fa.numRegs * kThreads) : 1;
   occ = occ < by_regs ? occ : by_regs;
   occ = occ < 1 ? 1 : (occ > kMaxCtasPerSm ? kMaxCtasPerSm : occ);
-  return sm_count() * occ;
+  sh.grid = sm_count() * occ;
+  return sh;
 }
 
 }  // namespace
@@ -1022,9 +1130,9 @@ int decode_grid(int nt) {
 
 int decode_launch_grid(int nt, int rv, int num_seqs) {
   switch (nt) {
-    case 1: return rv <= 4 ? decode_grid_for<1, 4>(num_seqs) : decode_grid_for<1, 8>(num_seqs);
-    case 2: return decode_grid_for<2, 16>(num_seqs);
-    default: return decode_grid_for<3, 24>(num_seqs);
+    case 1: return (rv <= 4 ? decode_shape<1, 4>(num_seqs) : decode_shape<1, 8>(num_seqs)).grid;
+    case 2: return decode_shape<2, 16>(num_seqs).grid;
+    default: return decode_shape<3, 24>(num_seqs).grid;
   }
 }
 
@@ -1044,20 +1152,20 @@ namespace {
 template <int NT, int RV>
 void launch_variant(const DecodeParams& p, const CUtensorMap& tmk, const CUtensorMap& tmv,
                     int cgrid, cudaStream_t stream) {
-  const int grid = decode_grid_for<NT, RV>(p.num_seqs);
+  const DecodeShape sh = decode_shape<NT, RV>(p.num_seqs);
   // programmatic dependent launch: the CTAs' setup (barriers, tensor memory) overlaps the tail of
   // the previous kernel; the kernel waits for it (griddepcontrol.wait) before reading any input
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cudaLaunchConfig_t dcfg = {};
-  dcfg.gridDim = dim3(grid);
+  dcfg.gridDim = dim3(sh.grid);
   dcfg.blockDim = dim3(kThreads);
-  dcfg.dynamicSmemBytes = decode_smem_bytes<NT>(p.num_seqs);
+  dcfg.dynamicSmemBytes = sh.smem;
   dcfg.stream = stream;
   dcfg.attrs = attr;
   dcfg.numAttrs = 1;
-  cudaLaunchKernelEx(&dcfg, decode_kernel<NT, RV>, tmk, tmv, p);
+  cudaLaunchKernelEx(&dcfg, sh.fn, tmk, tmv, p);
   if (cgrid > 0) {
     // programmatic dependent launch: the combine CTAs may be scheduled as decode CTAs retire;
     // each waits (griddepcontrol.wait) for the whole decode grid before reading the partials

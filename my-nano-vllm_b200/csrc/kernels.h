@@ -29,7 +29,7 @@ cudaError_t launch_store(const StoreParams& p, cudaStream_t stream);
 // Control block at the head of the decode workspace (ints):
 //   [0] sticky device error code, [1] next work item, [2] CTAs finished.
 constexpr int kCtrlInts = 64;  // 256 bytes
-constexpr int kMaxSeqs = 2048;  // per launch (plan lives in shared memory)
+constexpr int kMaxSeqs = 2048;  // per launch (the published plan below has room for this many)
 // Plan published by the decode kernel for its combine kernel, right after the control block:
 // [0] chunk size, [1] item count, [2 + b] item prefix of sequence b (b = 0 .. num_seqs).
 constexpr int kPlanInts = kMaxSeqs + 8;

@@ -110,6 +110,35 @@ def test_decode_single_long_sequence_many_chunks():
     _no_device_error()
 
 
+@pytest.mark.parametrize("bs,hq,kvh", [(2048, 32, 8), (601, 64, 8)])
+def test_decode_large_batches(bs, hq, kvh):
+    """Batches past 511 sequences run the sampled plan (ranges of ceil(B / 256) sequences):
+    2048 sequences (the most one call takes; ranges of 8, the last one without any work) and 601
+    (ranges of 3, the last one partial); lengths 0..300 with zeros and negatives among them."""
+    from nanovllm_b200 import workloads
+    gen = torch.Generator().manual_seed(44 + bs)
+    lens = torch.randint(0, 301, (bs,), generator=gen)
+    lens[torch.randint(0, bs, (bs // 7,), generator=gen)] = 0
+    lens[torch.randint(0, bs, (20,), generator=gen)] = -3
+    lens[-8:] = 0
+    c = workloads.decode_case(bs, hq, kvh, 0, 0, seed=44, device="cuda", block_size=64,
+                              lens=lens.tolist(), extra_cols=1)
+    out = _decode((c.q, c.k_cache, c.v_cache, c.block_tables, c.context_lens, c.scale))
+    assert_close(out, _oracle_case(c), what=f"{bs} sequences")
+    assert torch.all(out[lens.cuda() <= 0] == 0)
+    _no_device_error()
+
+
+def test_decode_two_ctas_per_sm_at_every_batch_size():
+    """The persistent grid keeps two CTAs on every SM from 1 to 2048 sequences, for each engine
+    variant (decode GQA 4 and 8; spec verify of 4 and 5 query rows): the in-kernel plan switches
+    to per-range arrays before its shared memory would push the second CTA off."""
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    for bs in [1, 256, 511, 512, 1000, 1919, 1920, 2048]:
+        for hq, kvh, mq in [(32, 8, 1), (64, 8, 1), (32, 8, 4), (32, 8, 5)]:
+            assert _lib().fp8attn_decode_ctas(bs, hq, kvh, mq) == 2 * sms, (bs, hq, kvh, mq)
+
+
 def test_decode_nan_bytes_beyond_context_are_ignored():
     # slots past each context hold NaN codes (0x7F): they must not leak into the output
     from nanovllm_b200 import workloads

@@ -108,6 +108,46 @@ def test_prefill_long_context_with_score_spikes():
     _no_device_error()
 
 
+def test_prefill_many_spec_verify_sequences():
+    """700 sequences, mostly speculative-verify sized (1..5 query rows, served by the decode
+    engine in spec mode) with some longer chunks among them (served by the prefill kernel): the
+    spec-mode plan then spans several sequences per range, some of them not routed to it."""
+    from nanovllm_b200 import workloads
+    gen = torch.Generator().manual_seed(45)
+    nqs = torch.randint(1, 6, (700,), generator=gen)
+    nqs[torch.randint(0, 700, (12,), generator=gen)] = 40
+    nqs[[3, 350, 699]] = 200
+    pre = torch.randint(0, 401, (700,), generator=gen)
+    pre[torch.randint(0, 700, (60,), generator=gen)] = 0
+    c = workloads.prefill_case(nqs.tolist(), pre.tolist(), 32, 8, seed=45, device="cuda",
+                               block_size=128)
+    _store_new_rows(c)
+    out = _prefill(c.q, c.k, c.v, c.block_tables, c.cu_seqlens_q, c.cu_seqlens_k, c.max_seqlen_q,
+                   c.max_seqlen_k, c.scale)
+    assert_close(out, _oracle(c), what="700 spec-verify sequences")
+    _no_device_error()
+
+
+@pytest.mark.parametrize("nseq,max_nq", [(700, 2), (2048, 5)])
+def test_prefill_spec_verify_large_batches(nseq, max_nq):
+    """Spec-verify batches whose decode-engine plan is sampled: 700 sequences of up to 2 query
+    rows (GQA 4: the 8-row engine, ranges of 3 sequences) and 2048 of up to 5 (the 24-row
+    engine, ranges of 8), with empty query sequences and empty prefixes among them."""
+    from nanovllm_b200 import workloads
+    gen = torch.Generator().manual_seed(46 + nseq)
+    nqs = torch.randint(1, max_nq + 1, (nseq,), generator=gen)
+    nqs[torch.randint(0, nseq, (nseq // 10,), generator=gen)] = 0
+    pre = torch.randint(0, 201, (nseq,), generator=gen)
+    pre[torch.randint(0, nseq, (nseq // 10,), generator=gen)] = 0
+    c = workloads.prefill_case(nqs.tolist(), pre.tolist(), 32, 8, seed=46, device="cuda",
+                               block_size=64)
+    _store_new_rows(c)
+    out = _prefill(c.q, c.k, c.v, c.block_tables, c.cu_seqlens_q, c.cu_seqlens_k, c.max_seqlen_q,
+                   c.max_seqlen_k, c.scale)
+    assert_close(out, _oracle(c), what=f"{nseq} spec-verify sequences")
+    _no_device_error()
+
+
 @pytest.mark.parametrize("bs", [16, 32, 64, 256, 512])
 @pytest.mark.parametrize("hq,kvh", [(4, 4), (8, 2), (16, 2), (12, 4), (24, 4)])  # + GQA 3, 6
 def test_prefill_paged_edge_cases(bs, hq, kvh):
