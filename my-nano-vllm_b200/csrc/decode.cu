@@ -49,9 +49,16 @@ constexpr int kMmaWarp = 5;
 constexpr int kThreads = 8 * 32;  // warps 6-7 idle (no role): 2 warps per scheduler, 2 CTAs per SM
 constexpr int kSoftmaxThreads = 128;
 constexpr int kMaxBoxes = kTile / 16;
-// Plan target: work items per CTA (an upper bound for the workspace).  Wide row groups have
-// costly item epilogues (24 rows of sums and partials), so they split less.
+// Plan target: work items per CTA, at most kItemsPerCta (the bound the workspace is sized for).
+// An item costs about kItemCostTokens key positions of fixed work (claim, query operand, first
+// tile's exact max, read-out, a partial to combine), so with W key positions per CTA the
+// finishing time ~ W + items * kItemCostTokens + one item's length is least near
+// sqrt(W / kItemCostTokens) items: 16 on 32k-token contexts, 10 on config-2-sized batches, and
+// at least 6.  Wide row groups have costly item epilogues (24 rows of sums and partials), so
+// they split less.
 constexpr int kItemsPerCta = 16;
+constexpr float kMinItemsPerCta = 6.f;
+constexpr float kItemCostTokens = 160.f;
 template <int NT>
 __host__ __device__ constexpr int items_per_cta() { return NT == 1 ? kItemsPerCta : 2; }
 
@@ -434,8 +441,17 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
   const uint32_t tmem = sm.tmem_base;
   const unsigned long long total_work =
       sm.total_work * static_cast<unsigned long long>(p.num_kv_heads);
-  const unsigned long long target = static_cast<unsigned long long>(items_per_cta<NT>()) * gridDim.x;
-  long long ct = static_cast<long long>((total_work + target - 1) / target);
+  long long ct;
+  if constexpr (NT == 1) {
+    const float per_cta = static_cast<float>(total_work) / static_cast<float>(gridDim.x);
+    const float items = fminf(fmaxf(sqrtf(per_cta / kItemCostTokens), kMinItemsPerCta),
+                              static_cast<float>(kItemsPerCta));
+    ct = static_cast<long long>(ceilf(per_cta / items));
+  } else {
+    const unsigned long long target =
+        static_cast<unsigned long long>(items_per_cta<NT>()) * gridDim.x;
+    ct = static_cast<long long>((total_work + target - 1) / target);
+  }
   if (ct < p.min_chunk) ct = p.min_chunk;
   ct = (ct + kTile - 1) / kTile * kTile;
   const int CT = static_cast<int>(ct > (1 << 24) ? (1 << 24) : ct);
