@@ -109,18 +109,29 @@ struct __align__(1024) DecodeSmem {
   unsigned long long total_work;
   // followed in shared memory by the plan, sized per launch:
   //   per sequence: int prefix[num_seqs + 1] (item prefix sums) and int info[num_seqs]
-  //                 ((L << 7) | row groups);
+  //                 ((L << 7) | row groups); on the wide engines, up to kThreads sequences
+  //                 also int perm[num_seqs]: the sequences in claim order (shortest chunks
+  //                 first), prefix in that order;
   //   sampled (batches whose per-sequence arrays would leave room for one CTA per SM only):
   //                 the same two arrays over the kThreads ranges of `per` sequences that the plan
   //                 threads own -- prefix[kThreads + 1] at each range's first sequence, and info
   //                 of that sequence -- so the size no longer grows with the batch
 };
 
-// Two CTAs share an SM (228 KB of shared memory, 1 KB reserved per CTA) with the plan arrays of
-// up to 256 sequences, and at any batch size with the sampled plan.
-static_assert(sizeof(DecodeSmem<1>) + 2 * 1024 + (2 * 256 + 1) * 4 <= 228 * 1024 / 2, "smem");
-static_assert(sizeof(DecodeSmem<2>) + 2 * 1024 + (2 * 256 + 1) * 4 <= 228 * 1024 / 2, "smem");
-static_assert(sizeof(DecodeSmem<3>) + 2 * 1024 + (2 * 256 + 1) * 4 <= 228 * 1024 / 2, "smem");
+// Two CTAs share an SM (228 KB of shared memory, 1 KB reserved per CTA) with the sorted plan
+// arrays of up to 256 sequences, and at any batch size with the sampled plan.
+static_assert(sizeof(DecodeSmem<1>) + 2 * 1024 + (3 * 256 + 1) * 4 <= 228 * 1024 / 2, "smem");
+static_assert(sizeof(DecodeSmem<2>) + 2 * 1024 + (3 * 256 + 1) * 4 <= 228 * 1024 / 2, "smem");
+static_assert(sizeof(DecodeSmem<3>) + 2 * 1024 + (3 * 256 + 1) * 4 <= 228 * 1024 / 2, "smem");
+// Claim order of a batch of up to kThreads sequences on the wide (spec-verify) engines: by the
+// length of their chunks, in tiles (capped at kSortKeys), shortest first, ties by index; with
+// chunks of about the same length at the end of the work, the CTAs finish together.  Measured:
+// the spec part of config 4 4 % faster.  The single-plane decode engines keep index order: the
+// same order, permuted on the host, made config 2 3.4 % faster, but the sort in the plan cost
+// about as much as it saved there.
+constexpr int kSortKeys = 32;
+constexpr int kWarps = kThreads / 32;
+static_assert(kSortKeys * kWarps == kThreads, "one (key, warp) count per thread");
 // sequences per range of the sampled plan, at most: they fit the lanes of the producer warp
 constexpr int kMaxPlanPer = (kMaxSeqs + kThreads - 1) / kThreads;
 static_assert(kMaxPlanPer <= 32 && 2 * kThreads + 1 <= 2 * 256 + 1, "sampled plan");
@@ -193,8 +204,8 @@ struct Cursor {
 // to find its sequence.
 template <int NT, bool kSampled>
 __device__ __forceinline__ void cursor_set(Cursor<NT>& P, int item, const DecodeParams& p,
-                                           const int* prefix, const int* info, int per,
-                                           int total_items, int CT, int B) {
+                                           const int* prefix, const int* info, const int* perm,
+                                           int per, int total_items, int CT, int B) {
   constexpr int R = DecodeSmem<NT>::R;
   P.item = item;
   if (item >= total_items) return;
@@ -206,11 +217,11 @@ __device__ __forceinline__ void cursor_set(Cursor<NT>& P, int item, const Decode
   }
   int b, L, nrg, r;
   if (!kSampled || per == 1) {  // the range is one sequence
-    b = lo;
+    b = kSampled || perm == nullptr ? lo : perm[lo];
     const int inf = info[b];
     L = inf >> 7;
     nrg = inf & 127;
-    r = item - prefix[b];
+    r = item - prefix[lo];
   } else {
     const int lane = threadIdx.x & 31;
     const int bl = lo * per + lane;
@@ -377,6 +388,10 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
   const int B = p.num_seqs;
   int* prefix = reinterpret_cast<int*>(&sm + 1);
   int* info = prefix + (kSampled ? kThreads : B) + 1;
+  // per-sequence plan of up to kThreads sequences on the wide (spec-verify) engines: claim order
+  // sorted (perm after info)
+  const bool sorted_plan = !kSampled && NT > 1 && B <= kThreads;
+  int* perm = sorted_plan ? info + B : nullptr;
 
   if (tid == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -467,8 +482,8 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
       my_items += (((inf >> 7) + CT - 1) / CT) * p.num_kv_heads * (inf & 127);
     }
   }
-  int total_items;
-  const int base = block_exclusive_scan(my_items, sm.scratch, &total_items);
+  int total_items = 0, base = 0;
+  if (!sorted_plan) base = block_exclusive_scan(my_items, sm.scratch, &total_items);
   if constexpr (kSampled) {
     prefix[tid] = base;
     if (tid == kThreads - 1) prefix[kThreads] = total_items;
@@ -486,6 +501,51 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
         p.plan[2 + B] = total_items;
       }
     }
+    __syncthreads();
+  } else if (sorted_plan) {
+    // sequence tid (one per thread): its key and items; stable counting sort by key through
+    // per-warp ranks and a (key, warp) count table in the K ring (unused until the producer
+    // starts), scanned key-major so that every CTA derives the same order
+    const bool valid = tid < B;
+    int key = kSortKeys;  // past every valid key: threads without a sequence
+    if (valid) {
+      const int inf = info[tid];
+      const int L = inf >> 7;
+      const int nch = (L + CT - 1) / CT;
+      key = L > 0 ? min(((L + nch - 1) / nch + kTile - 1) / kTile, kSortKeys) - 1 : 0;
+    }
+    const unsigned peers = __match_any_sync(0xffffffffu, key);
+    const int rank = __popc(peers & ((1u << lane) - 1));
+    int* counts = reinterpret_cast<int*>(&sm.k[0][0]);
+    counts[tid] = 0;
+    __syncthreads();
+    if (valid && rank == 0) counts[key * kWarps + warp] = __popc(peers);
+    __syncthreads();
+    int nseq;
+    const int first = block_exclusive_scan(counts[tid], sm.scratch, &nseq);
+    counts[tid] = first;
+    __syncthreads();
+    if (valid) perm[counts[key * kWarps + warp] + rank] = tid;
+    __syncthreads();
+    // item prefix in claim order: thread tid holds sorted position tid
+    int sb = 0, scnt = 0;
+    if (valid) {
+      sb = perm[tid];
+      const int inf = info[sb];
+      scnt = ((inf >> 7) + CT - 1) / CT * p.num_kv_heads * (inf & 127);
+    }
+    const int sbase = block_exclusive_scan(scnt, sm.scratch, &total_items);
+    if (valid) prefix[tid] = sbase;
+    if (tid == kThreads - 1) prefix[B] = total_items;
+    if (blockIdx.x == 0) {  // the combine kernel reads each sequence's first item after this launch
+      if (valid) p.plan[2 + sb] = sbase;
+      if (tid == 0) {
+        p.plan[0] = CT;
+        p.plan[1] = total_items;
+        p.plan[2 + B] = total_items;
+      }
+    }
+    fence_proxy_async_smem();  // the count table's stores come before the ring's TMA writes
     __syncthreads();
   } else {
     {
@@ -548,8 +608,8 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
       }
       ids[0] = __shfl_sync(0xffffffffu, ids[0], 0);
       ids[1] = __shfl_sync(0xffffffffu, ids[1], 0);
-      cursor_set<NT, kSampled>(P, ids[0], p, prefix, info, per, total_items, CT, B);
-      cursor_set<NT, kSampled>(Pn, ids[1], p, prefix, info, per, total_items, CT, B);
+      cursor_set<NT, kSampled>(P, ids[0], p, prefix, info, perm, per, total_items, CT, B);
+      cursor_set<NT, kSampled>(Pn, ids[1], p, prefix, info, perm, per, total_items, CT, B);
       if (P.item < total_items) stage_q<NT>(P, p, sm.qstage);
     }
     int stage = 0;
@@ -634,7 +694,7 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
         P = Pn;
         P.nth = nth;
         if (lane == 0) Pn.next = atomicAdd(p.ctrl + 1, 1);
-        if (P.item < total_items) cursor_set<NT, kSampled>(Pn, nxt, p, prefix, info, per, total_items, CT, B);
+        if (P.item < total_items) cursor_set<NT, kSampled>(Pn, nxt, p, prefix, info, perm, per, total_items, CT, B);
         else Pn.item = total_items;
       }
     }
@@ -1084,7 +1144,8 @@ int sm_count() {
 template <int NT>
 size_t decode_smem_bytes(int num_seqs, bool sampled) {
   // + alignment slack, + the per-launch plan arrays (prefix, info)
-  const int plan_ints = sampled ? 2 * kThreads + 1 : 2 * num_seqs + 1;
+  const int plan_ints = sampled ? 2 * kThreads + 1
+                                : (NT > 1 && num_seqs <= kThreads ? 3 : 2) * num_seqs + 1;
   return sizeof(DecodeSmem<NT>) + 1024 + static_cast<size_t>(plan_ints) * sizeof(int);
 }
 
