@@ -53,7 +53,7 @@ constexpr int kMaxBoxes = kTile / 16;
 // An item costs about kItemCostTokens key positions of fixed work (claim, query operand, first
 // tile's exact max, read-out, a partial to combine), so with W key positions per CTA the
 // finishing time ~ W + items * kItemCostTokens + one item's length is least near
-// sqrt(W / kItemCostTokens) items: 16 on 32k-token contexts, 10 on config-2-sized batches, and
+// sqrt(W / kItemCostTokens) items: 16 on 32k-token contexts, 10 on 256 sequences of 512-4096, and
 // at least 6.  Wide row groups have costly item epilogues (24 rows of sums and partials), so
 // they split less.
 constexpr int kItemsPerCta = 16;
@@ -126,9 +126,9 @@ static_assert(sizeof(DecodeSmem<3>) + 2 * 1024 + (3 * 256 + 1) * 4 <= 228 * 1024
 // Claim order of a batch of up to kThreads sequences on the wide (spec-verify) engines: by the
 // length of their chunks, in tiles (capped at kSortKeys), shortest first, ties by index; with
 // chunks of about the same length at the end of the work, the CTAs finish together.  Measured:
-// the spec part of config 4 4 % faster.  The single-plane decode engines keep index order: the
-// same order, permuted on the host, made config 2 3.4 % faster, but the sort in the plan cost
-// about as much as it saved there.
+// 192 verify sequences of 5 rows, 4 % faster.  The single-plane decode engines keep index order:
+// the same order, permuted on the host, made 256 sequences of 512-4096 tokens 3.4 % faster, but
+// the sort in the plan cost about as much as it saved there.
 constexpr int kSortKeys = 32;
 constexpr int kWarps = kThreads / 32;
 static_assert(kSortKeys * kWarps == kThreads, "one (key, warp) count per thread");
