@@ -1,25 +1,29 @@
 """Benchmark of the FP8 PagedAttention hot path (BASELINE.json metric).
 
-Headline workload (a "step"): one paged FP8 decode call over BASELINE config 2 (Qwen3-8B heads
-32 q / 8 kv, 256 sequences, context U[512, 4096], block 256, pool 1.25x, seed 1).  ``value`` is
-the decode's algorithmic HBM throughput (TB/s): every visible K and V byte once, plus q, out,
-block tables and lengths, divided by the device time of the step; the KV working set (~1.2 GB)
-is far larger than L2, so no flush is needed between steps.
+Headline workload (a "step"): one paged FP8 decode call over BASELINE config 5 -- Qwen3-32B heads
+(64 q / 8 kv, head_dim 128), 64 sequences at context 32768, block 256, about 2.1M cached tokens --
+split by kv-head group over the N GPUs of one node, as the reference's tensor-parallel head split
+does: rank r holds kv heads [r*8/N, (r+1)*8/N) and their q heads, with the same lengths and block
+tables on every rank and no collective in the path.  The total work is fixed, so ``scaling`` is
+"strong"; ``value`` is the algorithmic HBM throughput of the whole job (TB/s): the sum over ranks
+of every visible K and V byte once plus q, out, block tables and lengths, divided by the device
+time of the step (max over ranks).  The KV working set (4.3 GB at N=1, 0.54 GB per GPU at N=8) is
+far larger than the 126 MB L2, so no flush is needed between steps.
 
-Multi-GPU (``torchrun ... bench.py --gpus N``): KV-head-group sharding with no collective in the
-path.  Every rank holds a config-2-sized shard (8 kv heads, 32 q heads, its own cache and seed),
-so per-GPU work is fixed ("weak" scaling); the time is the max over ranks.
+Secondary figures on the N=1 line (outside the headline's timed region): config 2 (large-batch
+decode), config 1 (the small reference decode case), config 3 (chunked prefill, TFLOP/s, and its
+K/V store) and config 4 (mixed spec-verify + prefill call), each with its roofline; and
+``reference_gpu``: the reference's own Triton kernels (installed unmodified under baseline/_ref)
+timed on the same inputs and the same GPU, next to ours.
 
-Secondary figures on the same line (not the headline): ``prefill`` = the varlen causal chunked
-prefill of BASELINE config 3 (TFLOP/s of causal-useful FLOPs, L2 flushed before every timed
-call) and ``store`` = the K/V store of the same call's 5.1k new rows (GB/s).
-
-``--impl reference`` times the reference algorithm on the host cores instead (the CPU oracle,
-a torch fp32 restatement of fp8_paged_attention_decode_kernel) on a bounded sample.
+``--impl reference`` times the reference algorithm on the host cores instead (the CPU oracle, a
+torch fp32 restatement of fp8_paged_attention_decode_kernel) on a bounded sample of the headline
+workload; it does not load this repository's CUDA library.
 """
 from __future__ import annotations
 
 import argparse
+import importlib.util
 import json
 import os
 import statistics
@@ -29,11 +33,14 @@ import threading
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
-sys.path.insert(0, os.path.join(ROOT, "my-nano-vllm_b200"))
+PKG = os.path.join(ROOT, "my-nano-vllm_b200")
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")
+sys.path.insert(0, PKG)
 sys.path.insert(0, ROOT)
 
 METRIC = "FP8 paged decode HBM TB/s (% of 8 TB/s); varlen prefill TFLOP/s (% peak)"
-WORKLOAD = "config2: FP8 paged decode, Qwen3-8B heads (32q/8kv, d128), 256 seqs, ctx U[512,4096], block 256"
+WORKLOAD = ("config5: FP8 paged decode, Qwen3-32B heads (64q/8kv, d128), 64 seqs x 32768 ctx, "
+            "block 256, kv-head groups split over the GPUs")
 
 
 def _peaks():
@@ -41,15 +48,18 @@ def _peaks():
     if os.path.exists(path):
         with open(path) as f:
             d = json.load(f)
-        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
-    return 6650.0, 1590.0, "fallback"
+        return (float(d["hbm_gbs"]), float(d["bf16_tflops"]),
+                float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), "measured")
+    return 6650.0, 1590.0, 1400.0, "fallback"
 
 
-def _traffic(kernel: str):
+def _traffic(key: str):
+    """DRAM bytes (read + write) per algorithmic byte of a kernel on a workload, from the ncu
+    capture summarised in profiles/ (scaled to the launch by the caller)."""
     path = os.path.join(ROOT, "profiles", "ncu_traffic.json")
     if os.path.exists(path):
         with open(path) as f:
-            return json.load(f).get(kernel)
+            return json.load(f).get(key)
     return None
 
 
@@ -134,6 +144,7 @@ class ClockSampler:
                 "samples": len(self.samples), "source": "nvml" if self._nvml else "nvidia-smi"}
 
 
+# ------------------------------------------------------------------------------ ranks
 def _dist_init():
     import torch
     import torch.distributed as dist
@@ -148,13 +159,13 @@ def _dist_init():
     return world, rank, local
 
 
-def _max_over_ranks(x: float, world: int) -> float:
+def _reduce(x: float, world: int, op: str) -> float:
     if world == 1:
         return x
     import torch
     import torch.distributed as dist
     t = torch.tensor([x], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX if op == "max" else dist.ReduceOp.SUM)
     return float(t.item())
 
 
@@ -164,7 +175,15 @@ def _barrier(world):
         dist.barrier()
 
 
-def cpu_baseline(case, max_seconds: float = 20.0):
+def _load_workloads():
+    """The seeded input generator, loaded without importing the ``nanovllm_b200`` package's entry
+    points (so the reference leg never maps the CUDA library)."""
+    import nanovllm_b200.workloads as w  # the package __init__ loads nothing
+    return w
+
+
+# ------------------------------------------------------------------------------ CPU leg
+def cpu_baseline(case, max_seconds: float = 20.0, label: str = "config-5"):
     """Time the CPU oracle (torch fp32 restatement of the reference decode) on a bounded sample
     of the same workload: whole sequences in order until ~max_seconds of CPU work."""
     import torch
@@ -190,142 +209,242 @@ def cpu_baseline(case, max_seconds: float = 20.0):
         n += 1
     return {"value": done_bytes / t_total / 1e12, "unit": "TB/s",
             "cores": torch.get_num_threads(), "kind": "port",
-            "sample": f"first {n} of {q.shape[0]} config-2 sequences ({done_bytes / 1e6:.1f} MB "
+            "sample": f"first {n} of {q.shape[0]} {label} sequences ({done_bytes / 1e6:.1f} MB "
                       f"of K/V), torch fp32 oracle, {t_total:.1f} s"}
 
 
 def run_reference(args, world, rank):
-    """--impl reference: the reference algorithm on the host cores (CPU oracle port)."""
-    import torch
+    """--impl reference: the reference algorithm on the host cores (the CPU oracle port; the
+    reference's own path is Triton GPU code with no CPU implementation).  Rank 0 alone runs it;
+    every step is a bounded sample of the headline workload.  This repository's CUDA library is
+    never loaded here."""
     if rank != 0:
         return
-    from nanovllm_b200 import workloads
-    case = workloads.config2("cpu")
+    import torch
+    workloads = _load_workloads()
+    case = workloads.config5("cpu", gpus=1, rank=0, batch=8)
+    per_step = max(0.5, min(3.0, args.cpu_seconds / max(1, args.steps)))
     for _ in range(args.warmup):
-        pass
-    steps = []
-    for _ in range(max(1, min(args.steps, 3))):
-        r = cpu_baseline(case, max_seconds=15.0)
-        steps.append(r)
+        cpu_baseline(case, max_seconds=0.2)
+    steps = [cpu_baseline(case, max_seconds=per_step) for _ in range(args.steps)]
+    assert "nanovllm_b200._lib" not in sys.modules, "the reference leg must not load libfp8attn.so"
     value = statistics.median(s["value"] for s in steps)
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "TB/s",
             "n_gpus": world, "steps": len(steps), "warmup": args.warmup,
-            "ms_per_step": None, "higher_is_better": True, "scaling": "weak",
+            "ms_per_step": None, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "parallelism": f"kv-head-shard{world}",
-                       "note": "bounded sample per step; see cpu_baseline.sample"},
+            "config": {"workload": WORKLOAD, "parallelism": f"kv-head-split{world}",
+                       "note": "host cores; each step a bounded sample of whole config-5 "
+                               "sequences (see cpu_baseline.sample)"},
             "cpu_baseline": dict(steps[-1], value=value),
             "e2e": {"value": value, "unit": "TB/s", "h2d_bytes_per_step": 0,
-                    "d2h_bytes_per_step": 0}}
+                    "d2h_bytes_per_step": 0},
+            "library_loaded": False}
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------------------------ GPU helpers
 def _flush_l2(buf):
     buf.add_(1)  # writes 256 MB, twice the 126 MB L2
 
 
-def secondary(dev, hbm_peak, bf16_peak):
-    """Config-3 prefill (tensor bound) and its K/V store (HBM bound), CUDA-event timed per call
-    with L2 flushed in between.  FP8 dense peak = 2 x the measured bf16 GEMM peak (the e4m3
-    tensor rate is twice the bf16 rate on sm_100a)."""
+def _time_calls(fn, iters=10, warm=3, flush=None):
+    """Median CUDA-event time (ms) of ``fn`` on the current stream, L2 flushed before each call
+    when ``flush`` is given."""
     import torch
-    from nanovllm_b200 import fp8_prefill_attention, store_kvcache, workloads
+    for _ in range(warm):
+        fn()
+    ts = []
+    for _ in range(iters):
+        if flush is not None:
+            _flush_l2(flush)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        b.synchronize()
+        ts.append(a.elapsed_time(b))
+    return statistics.median(ts)
+
+
+def _fp8_peak(dev):
+    """Dense e4m3 GEMM rate of this GPU (cuBLASLt through torch._scaled_mm, 8192^3, best of 10):
+    the tensor roofline of the prefill, measured here because the driver's file holds bf16 only."""
+    import torch
+    try:
+        n = 8192
+        a = torch.randn(n, n, device=dev).to(torch.float8_e4m3fn)
+        b = torch.randn(n, n, device=dev).to(torch.float8_e4m3fn).t()
+        one = torch.ones((), device=dev)
+        f = lambda: torch._scaled_mm(a, b, scale_a=one, scale_b=one, out_dtype=torch.bfloat16)
+        f()
+        ms = min(_time_calls(f, iters=1, warm=0) for _ in range(10))
+        return 2 * n ** 3 / (ms * 1e-3) / 1e12
+    except Exception:
+        return None
+
+
+def _reference_module():
+    """The reference's own entry points from its unmodified install under baseline/_ref, or the
+    reason they cannot be loaded."""
+    if not os.path.isdir(os.path.join(REF_DIR, "nanovllm")):
+        return None, "baseline/_ref is not installed"
+    if REF_DIR not in sys.path:
+        sys.path.insert(0, REF_DIR)
+    try:
+        from nanovllm.kernels import fp8_attention as rk
+        from nanovllm.layers import attention as ra
+        return {"decode": rk.fp8_decode_attention, "prefill": rk.fp8_prefill_attention,
+                "store": ra.store_kvcache}, None
+    except Exception as e:  # pragma: no cover - depends on the box
+        return None, f"{type(e).__name__}: {e}"
+
+
+def _maxdiff(a, b):
+    return float((a.float() - b.float()).abs().max())
+
+
+def secondary(dev, peaks, with_reference: bool):
+    """Configs 2, 1, 3 (+ store) and 4 on one GPU, each timed with CUDA events after warm-up, and
+    the reference's Triton kernels on the same inputs where ``with_reference``."""
+    import torch
+    from nanovllm_b200 import fp8_decode_attention, fp8_prefill_attention, store_kvcache
+    workloads = _load_workloads()
+    hbm_peak, bf16_peak = peaks[0], peaks[1]
+    flush = torch.empty(64 << 20, dtype=torch.float32, device=dev)
+    ref, ref_err = _reference_module() if with_reference else (None, "not requested")
+    out = {}
+    refgpu = {"source": "baseline/_ref (unmodified reference, stock entry points), same inputs, "
+                        "same GPU, CUDA events, median"}
+    if ref is None:
+        refgpu["unavailable"] = ref_err
+
+    def ref_time(name, fn, ours_ms, ours_out=None, iters=5, warm=2, flush_l2=None):
+        if ref is None:
+            return
+        try:
+            r_ms = _time_calls(fn, iters=iters, warm=warm, flush=flush_l2)
+            entry = {"ms": r_ms, "ours_ms": ours_ms, "speedup": r_ms / ours_ms}
+            if ours_out is not None:
+                entry["max_abs_diff_vs_ours"] = _maxdiff(fn(), ours_out)
+            refgpu[name] = entry
+        except Exception as e:  # pragma: no cover
+            refgpu[name] = {"unavailable": f"{type(e).__name__}: {e}"}
+
+    fp8_peak = _fp8_peak(dev)
+    fp8_kind = "measured e4m3 GEMM (torch._scaled_mm)"
+    if fp8_peak is None:
+        fp8_peak, fp8_kind = 2 * bf16_peak, "2 x measured bf16 GEMM"
+
+    # ---- decode: config 2 (HBM bound, 1.2 GB) and config 1 (9 MB, latency bound)
+    for name, make, l2 in (("config2", workloads.config2, "inputs larger than L2"),
+                           ("config1", workloads.config1, "flushed before each call")):
+        c = make(dev)
+        args = (c.q, c.k_cache, c.v_cache, c.block_tables, c.context_lens, c.scale)
+        fl = flush if name == "config1" else None
+        ms = _time_calls(lambda: fp8_decode_attention(*args), iters=20, warm=5, flush=fl)
+        nbytes = c.kv_bytes()
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        out[name] = {"ms": ms, "tb_s": gbs / 1e3, "bytes": nbytes, "l2": l2,
+                     "tokens_per_s": c.q.shape[0] / (ms * 1e-3),
+                     "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm_peak,
+                                  "unit": "GB/s", "frac": gbs / hbm_peak}}
+        if ref is not None:
+            ours = fp8_decode_attention(*args)
+            ref_time(f"decode_{name}", lambda: ref["decode"](*args), ms, ours, flush_l2=fl)
+        del c, args
+        torch.cuda.empty_cache()
+
+    # ---- config 3: chunked prefill (tensor bound) and its K/V store (HBM bound)
     c = workloads.config3(dev)
     flops = c.causal_flops()
     n = c.new_k.shape[0]
     store_bytes = n * (2 * 8 * 128 * 2 + 2 * 8 * 128 + 4)
-    flush = torch.empty(64 << 20, dtype=torch.float32, device=dev)
-
-    def timed(fn, iters=10, warm=3):
-        for _ in range(warm):
-            fn()
-        ts = []
-        for _ in range(iters):
-            _flush_l2(flush)
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record()
-            fn()
-            b.record()
-            b.synchronize()
-            ts.append(a.elapsed_time(b))
-        return statistics.median(ts)
-
-    # the store is ~10 us of device work: time a CUDA graph of the call so that the host-side
-    # launch (the Python wrapper) is not measured
     store_kvcache(c.new_k, c.new_v, c.k, c.v, c.slot_mapping)
     torch.cuda.synchronize()
+    # the store is ~10 us of device work: time a CUDA graph of the call so that the host-side
+    # launch (the Python wrapper) is not measured
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph):
         store_kvcache(c.new_k, c.new_v, c.k, c.v, c.slot_mapping)
-    st_ms = timed(graph.replay)
+    st_ms = _time_calls(graph.replay, flush=flush)
     del graph
-    pf_ms = timed(lambda: fp8_prefill_attention(
+    pf = lambda: fp8_prefill_attention(
         c.q, c.k, c.v, block_tables=c.block_tables, cu_seqlens_q=c.cu_seqlens_q,
         cu_seqlens_k=c.cu_seqlens_k, max_seqlen_q=c.max_seqlen_q, max_seqlen_k=c.max_seqlen_k,
-        softmax_scale=c.scale))
+        softmax_scale=c.scale)
+    pf_ms = _time_calls(pf, flush=flush)
     tflops = flops / (pf_ms * 1e-3) / 1e12
-    fp8_peak = 2 * bf16_peak
-    return {
-        "prefill": {"workload": "config3: 16 seqs, new U[128,512], cached prefix U[0,3584], "
-                                "Qwen3-8B heads, paged block 256",
-                    "ms": pf_ms, "tflops": tflops, "causal_flops": flops,
-                    "roofline": {"bound": "tensor", "achieved": tflops, "peak": fp8_peak,
-                                 "unit": "TFLOP/s", "frac": tflops / fp8_peak,
-                                 "peak_note": "e4m3 dense = 2 x measured bf16 GEMM"},
-                    "l2": "flushed before each call"},
-        "store": {"ms": st_ms, "gbs": store_bytes / (st_ms * 1e-3) / 1e9, "rows": n,
-                  "timing": "CUDA-graph replay, L2 flushed before each call",
-                  "bytes": store_bytes, "frac": store_bytes / (st_ms * 1e-3) / 1e9 / hbm_peak},
-    }
+    out["config3_prefill"] = {
+        "workload": "16 seqs, new U[128,512], cached prefix U[0,3584], Qwen3-8B heads, paged "
+                    "block 256", "ms": pf_ms, "tflops": tflops, "causal_flops": flops,
+        "tokens_per_s": int(c.q.shape[0]) / (pf_ms * 1e-3), "l2": "flushed before each call",
+        "roofline": {"bound": "tensor", "achieved": tflops, "peak": fp8_peak, "unit": "TFLOP/s",
+                     "frac": tflops / fp8_peak, "peak_kind": fp8_kind,
+                     "frac_of_bf16_sustained": tflops / peaks[2]}}
+    sgbs = store_bytes / (st_ms * 1e-3) / 1e9
+    out["config3_store"] = {"ms": st_ms, "gbs": sgbs, "rows": n, "bytes": store_bytes,
+                            "timing": "CUDA-graph replay, L2 flushed before each call",
+                            "roofline": {"bound": "hbm", "achieved": sgbs, "peak": hbm_peak,
+                                         "unit": "GB/s", "frac": sgbs / hbm_peak}}
+    if ref is not None:
+        ours = pf()
+        ref_time("prefill_config3", lambda: ref["prefill"](
+            c.q, c.k, c.v, block_tables=c.block_tables, cu_seqlens_q=c.cu_seqlens_q,
+            cu_seqlens_k=c.cu_seqlens_k, max_seqlen_q=c.max_seqlen_q,
+            max_seqlen_k=c.max_seqlen_k, softmax_scale=c.scale), pf_ms, ours, iters=3, warm=1,
+            flush_l2=flush)
+        kc2, vc2 = c.k.clone(), c.v.clone()
+        ref_time("store_config3", lambda: ref["store"](c.new_k, c.new_v, kc2, vc2,
+                                                       c.slot_mapping), st_ms, flush_l2=flush)
+        refgpu["store_config3"]["bytes_equal_to_ours"] = bool(
+            torch.equal(kc2.view(torch.uint8), c.k.view(torch.uint8)) and
+            torch.equal(vc2.view(torch.uint8), c.v.view(torch.uint8)))
+        del kc2, vc2
+    del c
+    torch.cuda.empty_cache()
+
+    # ---- config 4: one mixed call (192 spec-verify sequences of 5 rows + 2 fresh 512-row chunks)
+    c = workloads.config4(dev)
+    store_kvcache(c.new_k, c.new_v, c.k, c.v, c.slot_mapping)
+    cq, ck = c.cu_seqlens_q.tolist(), c.cu_seqlens_k.tolist()
+    nks = [ck[i + 1] - ck[i] for i in range(len(ck) - 1)]
+    nqs = [cq[i + 1] - cq[i] for i in range(len(cq) - 1)]
+    spec_bytes = sum(nk * 8 * 128 * 2 + 2 * nq * 32 * 128 * 2 for nk, nq in zip(nks, nqs) if nq <= 16)
+    mixed = lambda: fp8_prefill_attention(
+        c.q, c.k, c.v, block_tables=c.block_tables, cu_seqlens_q=c.cu_seqlens_q,
+        cu_seqlens_k=c.cu_seqlens_k, max_seqlen_q=c.max_seqlen_q, max_seqlen_k=c.max_seqlen_k,
+        softmax_scale=c.scale)
+    m_ms = _time_calls(mixed, iters=10, warm=3)
+    gbs = spec_bytes / (m_ms * 1e-3) / 1e9
+    out["config4_mixed"] = {
+        "workload": "192 spec-verify seqs (1+4 rows, ctx U[1024,8187]) + 2 fresh 512-token "
+                    "chunks, one prefill call, Qwen3-8B heads, paged block 256",
+        "ms": m_ms, "tokens_per_s": int(c.q.shape[0]) / (m_ms * 1e-3), "spec_bytes": spec_bytes,
+        "l2": "inputs larger than L2",
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s",
+                     "frac": gbs / hbm_peak,
+                     "note": "spec-part bytes over the whole call's time (the two fresh chunks "
+                             "run in the same call)"}}
+    if ref is not None:
+        ours = mixed()
+        ref_time("mixed_config4", lambda: ref["prefill"](
+            c.q, c.k, c.v, block_tables=c.block_tables, cu_seqlens_q=c.cu_seqlens_q,
+            cu_seqlens_k=c.cu_seqlens_k, max_seqlen_q=c.max_seqlen_q,
+            max_seqlen_k=c.max_seqlen_k, softmax_scale=c.scale), m_ms, ours, iters=2, warm=1)
+    del c
+    torch.cuda.empty_cache()
+    return out, refgpu
 
 
-def run_ours(args, world, rank, local):
+def _e2e(case, steps, warmup, world, stream):
+    """The headline call through the public API with host buffers: every step copies its inputs
+    (q, block tables, lengths) from pinned host memory and its output back.  The copies run on a
+    second stream with double-buffered device inputs (events order them), so step i+1's upload
+    and step i's download overlap a kernel; all of them are inside the timed region."""
     import torch
-    from nanovllm_b200 import fp8_decode_attention, workloads
-    from nanovllm_b200.fp8_attention import device_error
-    dev = torch.device("cuda", local)
-    torch.cuda.set_device(dev)
-    hbm_peak, bf16_peak, peak_kind = _peaks()
-
-    # rank r: its own config-2-sized shard (weak scaling)
-    case = workloads.decode_case(256, 32, 8, 512, 4096, seed=1 + 1000 * rank, device=dev,
-                                 pool_factor=1.25)
-    step_bytes = case.kv_bytes()
-    stream = torch.cuda.current_stream(dev)
-
-    def step():
-        return fp8_decode_attention(case.q, case.k_cache, case.v_cache, case.block_tables,
-                                    case.context_lens, case.scale)
-
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-    _barrier(world)
-    torch.cuda.synchronize()
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-          for _ in range(args.steps)]
-    with ClockSampler(local) as clk:
-        t_start = torch.cuda.Event(enable_timing=True)
-        t_end = torch.cuda.Event(enable_timing=True)
-        t_start.record(stream)
-        for s, e in ev:
-            s.record(stream)
-            step()
-            e.record(stream)
-        t_end.record(stream)
-        torch.cuda.synchronize()
-        if not clk.samples:  # nvidia-smi fallback: make sure at least one sample is taken
-            time.sleep(0.25)
-    total_ms = t_start.elapsed_time(t_end)
-    per_launch_ms = statistics.mean(s.elapsed_time(e) for s, e in ev)
-    total_ms = _max_over_ranks(total_ms, world)
-    per_launch_ms = _max_over_ranks(per_launch_ms, world)
-    err = device_error(dev)
-
-    # ---- end to end through the public API with host buffers: every step copies its inputs
-    # (q, block tables, lengths) from pinned host memory and its output back.  The copies run on a
-    # second stream with double-buffered device inputs (events order them), so step i+1's
-    # upload and step i's download overlap a kernel; all of them are inside the timed region.
+    from nanovllm_b200 import fp8_decode_attention
+    dev = case.q.device
     q_h = case.q.cpu().pin_memory()
     bt_h = case.block_tables.cpu().pin_memory()
     ctx_h = case.context_lens.cpu().pin_memory()
@@ -360,7 +479,7 @@ def run_ours(args, world, rank, local):
             out_h[b].copy_(o, non_blocking=True)
             ev_free[b].record(copy_stream)
 
-    def e2e_loop(n):
+    def loop(n):
         upload(0)
         for i in range(n):
             if i + 1 < n:
@@ -368,48 +487,108 @@ def run_ours(args, world, rank, local):
             run(i % 2)
         stream.wait_stream(copy_stream)
 
-    e2e_loop(args.warmup)
+    loop(warmup)
     torch.cuda.synchronize()
     _barrier(world)
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record(stream)
     copy_stream.wait_event(a)  # the first upload starts inside the timed region
-    e2e_loop(args.steps)
+    loop(steps)
     b.record(stream)
     torch.cuda.synchronize()
-    e2e_ms = _max_over_ranks(a.elapsed_time(b), world)
+    return _reduce(a.elapsed_time(b), world, "max"), h2d, d2h
 
+
+def run_ours(args, world, rank, local):
+    import torch
+    from nanovllm_b200 import _lib, fp8_decode_attention
+    from nanovllm_b200.fp8_attention import device_error
+    workloads = _load_workloads()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    peaks = _peaks()
+    hbm_peak = peaks[0]
+    if 8 % world:
+        raise SystemExit(f"config 5's 8 kv heads do not split over {world} GPUs")
+
+    # rank r: its kv-head group of config 5 (strong scaling: the total work is fixed)
+    case = workloads.config5(dev, gpus=world, rank=rank, batch=args.batch)
+    step_bytes = case.kv_bytes()
+    total_bytes = _reduce(float(step_bytes), world, "sum")
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        return fp8_decode_attention(case.q, case.k_cache, case.v_cache, case.block_tables,
+                                    case.context_lens, case.scale)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    _barrier(world)
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    with ClockSampler(local) as clk:
+        t_start = torch.cuda.Event(enable_timing=True)
+        t_end = torch.cuda.Event(enable_timing=True)
+        t_start.record(stream)
+        for s, e in ev:
+            s.record(stream)
+            step()
+            e.record(stream)
+        t_end.record(stream)
+        torch.cuda.synchronize()
+        if not clk.samples:  # nvidia-smi fallback: make sure at least one sample is taken
+            time.sleep(0.25)
+    total_ms = _reduce(t_start.elapsed_time(t_end), world, "max")
+    per_launch_ms = statistics.mean(s.elapsed_time(e) for s, e in ev)
+    per_launch_max = _reduce(per_launch_ms, world, "max")
+    err = int(_reduce(float(device_error(dev)), world, "max"))
+
+    e2e_ms, h2d, d2h = _e2e(case, args.steps, args.warmup, world, stream)
+    h2d = int(_reduce(float(h2d), world, "sum"))
+    d2h = int(_reduce(float(d2h), world, "sum"))
+    ctas = int(_lib.lib.fp8attn_decode_ctas(case.q.shape[0], case.q.shape[1],
+                                            case.k_cache.shape[2], 1))
     if rank != 0:
         return
     ms = total_ms / args.steps
-    value = world * step_bytes / (ms * 1e-3) / 1e12
-    achieved_gbs = step_bytes / (per_launch_ms * 1e-3) / 1e9
-    e2e_val = world * step_bytes / (e2e_ms / args.steps * 1e-3) / 1e12
+    value = total_bytes / (ms * 1e-3) / 1e12
+    achieved_gbs = step_bytes / (per_launch_ms * 1e-3) / 1e9  # rank 0's decode + combine launches
+    tr = _traffic("decode_config5")
     line = {
         "metric": METRIC, "value": value, "unit": "TB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "e4m3",
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "e4m3",
         "data": "synthetic",
-        "config": {"workload": WORKLOAD, "parallelism": f"kv-head-shard{world}",
-                   "bytes_per_step_per_gpu": step_bytes,
-                   "l2": "inputs larger than L2 (1.2 GB of K/V per step)",
-                   "fraction_of_8TBs": value / world / 8.0},
+        "config": {"workload": WORKLOAD, "parallelism": f"kv-head-split{world}",
+                   "kv_heads_per_gpu": 8 // world, "q_heads_per_gpu": 64 // world,
+                   "batch": int(case.q.shape[0]), "context": 32768,
+                   "bytes_per_step": int(total_bytes), "bytes_per_step_rank0": step_bytes,
+                   "l2": "inputs larger than L2 (K/V per GPU per step > 126 MB)",
+                   "fraction_of_8TBs_per_gpu": value / world / 8.0,
+                   "max_gpu_step_ms": per_launch_max},
         "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": hbm_peak, "unit": "GB/s",
-                     "frac": achieved_gbs / hbm_peak, "peak_kind": peak_kind,
-                     "traffic": _traffic("decode_kernel")},
-        "e2e": {"value": e2e_val, "unit": "TB/s", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h},
+                     "frac": achieved_gbs / hbm_peak, "peak_kind": peaks[3],
+                     "kernel": "decode_kernel + combine_kernel (rank 0, per step)",
+                     "traffic": (int(tr * step_bytes) if tr is not None else None)},
+        "e2e": {"value": total_bytes / (e2e_ms / args.steps * 1e-3) / 1e12, "unit": "TB/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": 2 * args.steps,  # decode + split-KV combine per step
-        "decode_ctas": int(__import__("nanovllm_b200._lib", fromlist=["lib"]).lib.fp8attn_decode_ctas(256, 32, 8, 1)),
+        "decode_ctas": ctas,
         "clocks": clk.summary(),
         "device_error": err,
     }
-    if world == 1:
-        # outside the headline's timed region; a paged prefill call launches 3 kernels (the
-        # split-KV engine for short sequences + its combine, then the prefill engine), a store 1
-        line.update(secondary(dev, hbm_peak, bf16_peak))
-    if not args.no_cpu_baseline and world == 1:
-        line["cpu_baseline"] = cpu_baseline(case, max_seconds=args.cpu_seconds)
+    if world == 1 and args.batch == 64:
+        del case
+        torch.cuda.empty_cache()
+        sec, refgpu = secondary(dev, peaks, not args.no_reference_gpu)
+        line.update(sec)
+        line["reference_gpu"] = refgpu
+        line["device_error"] = max(line["device_error"], device_error(dev))
+        if not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(workloads.config5("cpu", batch=8),
+                                                max_seconds=args.cpu_seconds)
     print(json.dumps(line), flush=True)
 
 
@@ -420,7 +599,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-reference-gpu", action="store_true",
+                    help="skip timing the reference's Triton kernels on the GPU")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--batch", type=int, default=64,
+                    help="config-5 sequences (64 = the benchmark; fewer for profile captures, "
+                         "which then skip the secondary figures)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world, rank, local = _dist_init() if args.impl == "ours" else (

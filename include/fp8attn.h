@@ -134,9 +134,13 @@ FP8ATTN_API int fp8attn_decode_ctas(int num_seqs, int num_heads, int num_kv_head
  *     with the device current.
  *   - Zero state: the array starts zeroed; its work counters (bytes 4..11) must be zero when a
  *     launch starts, and every launch leaves them zero.  Device error codes are recorded in its
- *     first word and are not reported by this call.
+ *     first word, which this call does not read (it never synchronises): read it with
+ *     fp8attn_noalloc_read_error.
  *   - One scratch per device: calls whose kernels may overlap (other streams, other host threads,
  *     other processes sharing the context) race on it and give wrong results.  Serialise them.
+ *   - The resolved address is kept for the life of the process: after cudaDeviceReset (or any
+ *     other teardown of the device's primary context) this entry point must not be called again
+ *     on that device.
  */
 #define FP8ATTN_NOALLOC_SCRATCH_BYTES (32LL << 20)
 FP8ATTN_API int fp8attn_decode_noalloc(void* out, const void* q, int64_t q_row_stride,
@@ -146,9 +150,34 @@ FP8ATTN_API int fp8attn_decode_noalloc(void* out, const void* q, int64_t q_row_s
                    int num_kv_heads, int head_dim, int64_t num_blocks, int block_size,
                    float softmax_scale, void* stream);
 
-/* Tuning knob (process-wide): minimum key positions per split-KV work item, a multiple of 128
- * (default 128).  Returns the previous value; other values are rejected with -1. */
+/* Device error word of fp8attn_decode_noalloc's scratch on the current device, copied into *dst
+ * (host or device memory) in stream order: *dst holds it once `stream` has reached this point
+ * (synchronise the stream, or wait on an event recorded after this call, before reading it).
+ * clear != 0 also zeroes the word, after the copy.  Diagnostics: no counterpart in the reference. */
+FP8ATTN_API int fp8attn_noalloc_read_error(int32_t* dst, int clear, void* stream);
+
+/* Device error word of a workspace (the int32 at FP8ATTN_WS_ERROR_OFFSET: 0 = none, 1 = a bounded
+ * wait timed out, 2 = bad block, 3 = tensor-memory allocation, 4 = workspace too small), copied
+ * into *dst in stream order as above, so a host can check a step without a blocking read on the
+ * hot path; clear != 0 zeroes it after the copy.  Diagnostics: no counterpart in the reference. */
+FP8ATTN_API int fp8attn_read_error(const void* workspace, int32_t* dst, int clear, void* stream);
+
+/* Tuning knob (process-wide, atomic): minimum key positions per split-KV work item, a multiple of
+ * 128 (default 128).  Returns the previous value; other values are rejected with -1.  Calls that
+ * are already launched keep the value they were planned with. */
 FP8ATTN_API int fp8attn_set_decode_min_chunk(int tokens);
+
+/*
+ * Self-checks of device-side mechanisms (no counterpart in the reference; used by the tests).
+ *   fp8attn_diag_wait_timeout: num_ctas CTAs each claim one work item from the control block at
+ *     `workspace` (ints: [0] error word, [1] next item, [2] CTAs finished, zeroed by the caller)
+ *     and wait on an mbarrier that nothing arrives on, with the library's bounded wait given a
+ *     limit of limit_ns: every wait must give up, record 1 (wait timed out) in the error word and
+ *     let the launch finish with [1] and [2] back at zero.
+ *   fp8attn_diag_exp2: poly[i] = the prefill softmax's FMA-pipe 2^x(i), mufu[i] = ex2.approx(x[i]).
+ */
+FP8ATTN_API int fp8attn_diag_wait_timeout(void* workspace, int64_t limit_ns, int num_ctas, void* stream);
+FP8ATTN_API int fp8attn_diag_exp2(const float* x, float* poly, float* mufu, int64_t n, void* stream);
 
 #ifdef __cplusplus
 }

@@ -3,6 +3,7 @@
 #include <cstdarg>
 #include <cstdint>
 #include <cstdio>
+#include <atomic>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -14,7 +15,7 @@
 namespace {
 
 thread_local std::string g_last_error;
-int g_min_chunk = 128;
+std::atomic<int> g_min_chunk{128};
 
 int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
 int fail(int code, const char* fmt, ...) {
@@ -156,9 +157,7 @@ int fp8attn_decode_ctas(int num_seqs, int num_heads, int num_kv_heads, int max_s
 
 int fp8attn_set_decode_min_chunk(int tokens) {
   if (tokens < fp8attn::kDecodeTile || tokens % fp8attn::kDecodeTile != 0) return -1;
-  const int prev = g_min_chunk;
-  g_min_chunk = tokens;
-  return prev;
+  return g_min_chunk.exchange(tokens);
 }
 
 int fp8attn_store_kvcache(const void* key, int64_t key_row_stride, const void* value,
@@ -228,7 +227,7 @@ static int run_decode_engine(fp8attn::DecodeParams& p, const EnginePlan& e, cons
   p.partials = reinterpret_cast<float*>(ws + fp8attn::kCtrlInts * 4 + fp8attn::kPlanInts * 4);
   p.max_items = static_cast<int>(fp8attn::decode_max_items(pairs, grid));
   p.max_rowgroups = e.max_rowgroups;
-  p.min_chunk = g_min_chunk;
+  p.min_chunk = g_min_chunk.load();
   p.box_rows = box_rows_for(p.block_size);
   CUtensorMap tmk, tmv;
   const int64_t rows = p.num_blocks * p.block_size;
@@ -381,6 +380,19 @@ int fp8attn_prefill(void* out, const void* q, int64_t q_row_stride, const void* 
   return FP8ATTN_OK;
 }
 
+int fp8attn_read_error(const void* workspace, int32_t* dst, int clear, void* stream) {
+  if (workspace == nullptr || dst == nullptr) return fail(FP8ATTN_EINVAL, "null pointer argument");
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* word = static_cast<uint8_t*>(const_cast<void*>(workspace)) + FP8ATTN_WS_ERROR_OFFSET;
+  cudaError_t e = cudaMemcpyAsync(dst, word, sizeof(int32_t), cudaMemcpyDefault, st);
+  if (e != cudaSuccess) return cuda_fail(e, "error word copy");
+  if (clear) {
+    e = cudaMemsetAsync(word, 0, sizeof(int32_t), st);
+    if (e != cudaSuccess) return cuda_fail(e, "error word clear");
+  }
+  return FP8ATTN_OK;
+}
+
 }  // extern "C"
 
 // ---------------------------------------------------------------- decode without allocation
@@ -437,6 +449,14 @@ int fp8attn_decode_noalloc(void* out, const void* q, int64_t q_row_stride, const
                         block_tables_stride, max_num_blocks, context_lens, num_seqs, num_heads,
                         num_kv_heads, head_dim, num_blocks, block_size, softmax_scale, scratch,
                         FP8ATTN_NOALLOC_SCRATCH_BYTES, stream);
+}
+
+int fp8attn_noalloc_read_error(int32_t* dst, int clear, void* stream) {
+  if (dst == nullptr) return fail(FP8ATTN_EINVAL, "null destination");
+  void* scratch = nullptr;
+  const int rc = noalloc_scratch(&scratch);
+  if (rc) return rc;
+  return fp8attn_read_error(scratch, dst, clear, stream);
 }
 
 }  // extern "C"

@@ -76,9 +76,11 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Bounded wait for the phase with the given parity to complete.  Returns false (and records
-// kDevErrWaitTimeout in *err) when the wall-clock bound is exceeded.  The clock is read only
-// every 1024 polls: reading %globaltimer is slow, and a wait that completes must not pay for it.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+// kDevErrWaitTimeout in *err) when more than limit_ns of wall-clock time pass.  The clock is read
+// only every 1024 polls: reading %globaltimer is slow, and a wait that completes must not pay
+// for it.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, int* err,
+                                              unsigned long long limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   unsigned long long t0 = 0;
   for (uint32_t polls = 1;; ++polls) {
@@ -87,11 +89,29 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
       const unsigned long long now = globaltimer_ns();
       if (t0 == 0) {
         t0 = now;
-      } else if (now - t0 > kWaitLimitNs) {
+      } else if (now - t0 > limit_ns) {
         if (err) atomicExch(err, kDevErrWaitTimeout);
         return false;
       }
     }
+  }
+}
+
+// The library's waits: bounded by kWaitLimitNs.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+  return mbar_wait_for(bar, parity, err, kWaitLimitNs);
+}
+
+// End of a persistent launch that claimed work from the control block (ctrl[1] = next work item,
+// ctrl[2] = CTAs finished): the last CTA to finish returns both counters to zero, so the next
+// launch on the same workspace starts from a clean state.  Called by one thread per CTA, after
+// every thread of the CTA is done with the counters.
+__device__ __forceinline__ void release_work_counters(int* ctrl) {
+  __threadfence();
+  const int done = atomicAdd(ctrl + 2, 1);
+  if (done == static_cast<int>(gridDim.x) - 1) {
+    atomicExch(ctrl + 1, 0);
+    atomicExch(ctrl + 2, 0);
   }
 }
 

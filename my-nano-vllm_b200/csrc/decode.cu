@@ -1036,14 +1036,7 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
   __syncthreads();
   tc::fence_after_sync();
   if (warp == kMmaWarp) tc::tmem_dealloc(tmem, kTmemCols);
-  if (tid == 0) {
-    __threadfence();
-    const int done = atomicAdd(p.ctrl + 2, 1);
-    if (done == static_cast<int>(gridDim.x) - 1) {
-      atomicExch(p.ctrl + 1, 0);
-      atomicExch(p.ctrl + 2, 0);
-    }
-  }
+  if (tid == 0) release_work_counters(p.ctrl);
 }
 
 // Combines the split-KV partials of every (sequence, kv head, row group) with more than one

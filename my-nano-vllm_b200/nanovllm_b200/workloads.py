@@ -92,11 +92,48 @@ def config2(device="cpu"):
     return decode_case(256, 32, 8, 512, 4096, seed=1, device=device, pool_factor=1.25)
 
 
-def config5(device="cpu", gpus=1, rank=0):
-    """Long-context decode, Qwen3-32B heads (64 q / 8 kv), 64 sequences at 32768, KV heads split
-    across ``gpus`` ranks: rank r holds kv heads [r*8/g, (r+1)*8/g) and their q heads."""
-    kvh = 8 // gpus
-    return decode_case(64, 64 // gpus, kvh, 32768, 32768, seed=4 + 100 * rank, device=device)
+def _normal_e4m3_heads(pool, block_size, kv_heads, seed, device) -> torch.Tensor:
+    """Paged cache [pool, block_size, len(kv_heads), 128] whose head slice i holds the N(0,1)
+    e4m3 values of global kv head kv_heads[i], drawn from its own seeded generator: a rank's
+    shard of the cache is then the same bytes as the matching slice of the unsharded cache."""
+    out = torch.empty((pool, block_size, len(kv_heads), HEAD_DIM), dtype=torch.float8_e4m3fn,
+                      device=device)
+    for i, h in enumerate(kv_heads):
+        out[:, :, i].copy_(_normal_e4m3((pool, block_size, HEAD_DIM), seed * 1000 + h, device))
+    return out
+
+
+def sharded_decode_case(batch, num_heads, num_kv_heads, lens, seed, device="cpu", gpus=1, rank=0,
+                        block_size=256, pool_factor=1.0) -> DecodeCase:
+    """Rank ``rank`` of ``gpus``'s part of one decode batch split by kv-head group (the reference's
+    tensor-parallel head split, nanovllm/engine/model_runner.py:111, nanovllm/models/qwen3.py:53-59):
+    kv heads [r*KVH/g, (r+1)*KVH/g) and their q heads.  Lengths and block tables are the same on
+    every rank; q and the caches are the matching slices of the unsharded batch (every kv head's
+    bytes come from its own generator), so the ranks' outputs concatenated along the head axis are
+    the unsharded problem's."""
+    from .shard import kv_head_range, q_head_range
+    gen = torch.Generator().manual_seed(seed)
+    tables, pool = _tables(lens, block_size, pool_factor, gen)
+    q = torch.randn(batch, num_heads, HEAD_DIM, generator=gen).to(torch.bfloat16)
+    k0, k1 = kv_head_range(num_kv_heads, rank, gpus)
+    h0, h1 = q_head_range(num_heads, num_kv_heads, rank, gpus)
+    heads = list(range(k0, k1))
+    kc = _normal_e4m3_heads(pool, block_size, heads, seed * 7 + 1, device)
+    vc = _normal_e4m3_heads(pool, block_size, heads, seed * 7 + 2, device)
+    return DecodeCase(q[:, h0:h1].contiguous().to(device), kc, vc, tables.to(device),
+                      torch.tensor(lens, dtype=torch.int32).to(device),
+                      meta=dict(batch=batch, num_heads=h1 - h0, num_kv_heads=k1 - k0,
+                                block_size=block_size, pool_blocks=pool, seed=seed, gpus=gpus,
+                                rank=rank, kv_heads=(k0, k1), q_heads=(h0, h1)))
+
+
+def config5(device="cpu", gpus=1, rank=0, batch=64):
+    """Long-context decode, Qwen3-32B heads (64 q / 8 kv), 64 sequences at 32768 (128 blocks of
+    256 each), KV heads split across ``gpus`` ranks: rank r holds kv heads [r*8/g, (r+1)*8/g) and
+    their q heads.  A smaller ``batch`` gives the same geometry over fewer sequences (tests and
+    profile captures), with a pool of just their blocks."""
+    return sharded_decode_case(batch, 64, 8, [32768] * batch, seed=4, device=device, gpus=gpus,
+                               rank=rank)
 
 
 @dataclass

@@ -24,3 +24,6 @@ def test_reference_arm_json_line():
     assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["cores"] >= 1
     assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["e2e"]["d2h_bytes_per_step"] == 0
     assert "workload" in line["config"]
+    # the reference leg never maps this repository's CUDA library
+    assert line["library_loaded"] is False
+    assert line["scaling"] == "strong" and line["config"]["workload"].startswith("config5")

@@ -71,3 +71,22 @@ def test_head_ranges():
         shard.kv_head_range(8, 0, 3)
     with pytest.raises(ValueError):
         shard.kv_head_range(8, 2, 2)
+
+
+def test_config5_shards_are_slices_of_the_unsharded_batch():
+    """Every rank's config-5 inputs are the matching slices of the one-GPU batch: same block
+    tables and lengths, its own q heads and kv heads (generated per kv head)."""
+    from nanovllm_b200 import workloads
+    full = workloads.config5("cpu", gpus=1, rank=0, batch=1)
+    for world in (2, 4, 8):
+        for rank in (0, world - 1):
+            part = workloads.config5("cpu", gpus=world, rank=rank, batch=1)
+            k0, k1 = shard.kv_head_range(8, rank, world)
+            h0, h1 = shard.q_head_range(64, 8, rank, world)
+            assert torch.equal(part.block_tables, full.block_tables)
+            assert torch.equal(part.context_lens, full.context_lens)
+            assert torch.equal(part.q, full.q[:, h0:h1])
+            assert torch.equal(part.k_cache.view(torch.uint8),
+                               full.k_cache.view(torch.uint8)[:, :, k0:k1])
+            assert torch.equal(part.v_cache.view(torch.uint8),
+                               full.v_cache.view(torch.uint8)[:, :, k0:k1])

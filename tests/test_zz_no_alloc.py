@@ -1,14 +1,14 @@
 """fp8attn_decode_noalloc (no counterpart in the reference): the decode entry point whose split-KV
-scratch is the library's static device array.  Called through the C-ABI and compared with
-fp8attn_decode (caller workspace) within the attention tolerance, on two consecutive calls so that
-the second call meets the scratch the first one left behind.  The file name sorts last so the
-suite also runs it after every other test."""
+scratch is the library's static device array, for hosts that cannot allocate device memory on the
+decode path.  Called through the C-ABI and compared with fp8attn_decode (caller workspace): both
+run the same kernels with the same plan, so the outputs must be bit-identical, on consecutive calls
+(the later ones meet the scratch the earlier ones left behind).  After every call the scratch's
+error word must read 0, and the device's free memory must not move across calls.  The file name
+sorts last so the suite also runs it after every other test."""
 import ctypes
 
 import pytest
 import torch
-
-from helpers import assert_close
 
 pytestmark = pytest.mark.gpu
 
@@ -23,16 +23,36 @@ def _noalloc(c, out):
         ctypes.c_float(c.scale), torch.cuda.current_stream().cuda_stream)
 
 
+def _scratch_error():
+    from nanovllm_b200 import _lib
+    host = torch.full((1,), -1, dtype=torch.int32).pin_memory()
+    _lib.check(_lib.lib.fp8attn_noalloc_read_error(host.data_ptr(), 0,
+                                                   torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    return int(host[0])
+
+
 @pytest.mark.parametrize("config", ["config1", "config2"])
 def test_noalloc_matches_workspace_entry(config):
     from nanovllm_b200 import _lib, fp8_decode_attention, workloads
     c = getattr(workloads, config)("cuda")
     ref = fp8_decode_attention(c.q, c.k_cache, c.v_cache, c.block_tables, c.context_lens, c.scale)
-    for call in range(2):
-        out = torch.full_like(c.q, float("nan"))
+    outs = [torch.full_like(c.q, float("nan")) for _ in range(3)]
+    torch.cuda.synchronize()
+    free = []
+    errors = []
+    for out in outs:  # nothing in this loop allocates device memory but the calls under test
+        free.append(torch.cuda.mem_get_info()[0])
         _lib.check(_noalloc(c, out))
         torch.cuda.synchronize()
-        assert_close(out, ref, what=f"{config} no-alloc call {call}")
+        errors.append(_scratch_error())
+    free.append(torch.cuda.mem_get_info()[0])
+    assert errors == [0, 0, 0], errors
+    # the first call may load the library's module on this device; later calls allocate nothing
+    assert free[1] == free[2] == free[3], free
+    for call, out in enumerate(outs):
+        assert torch.equal(out.view(torch.int16), ref.view(torch.int16)), \
+            f"{config} no-alloc call {call} differs from fp8attn_decode"
 
 
 def test_noalloc_rejects_shapes_beyond_its_scratch():
