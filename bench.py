@@ -23,7 +23,6 @@ workload; it does not load this repository's CUDA library.
 from __future__ import annotations
 
 import argparse
-import importlib.util
 import json
 import os
 import statistics
@@ -258,6 +257,9 @@ def _time_calls(fn, iters=10, warm=3, flush=None):
     for _ in range(iters):
         if flush is not None:
             _flush_l2(flush)
+        # keep the GPU busy while the host enqueues the call, so that the events bracket device
+        # work only (not the host-side launch of a short call)
+        torch.cuda._sleep(200000)
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
         fn()
@@ -304,12 +306,47 @@ def _maxdiff(a, b):
     return float((a.float() - b.float()).abs().max())
 
 
-def secondary(dev, peaks, with_reference: bool):
+PARTS = ("config2", "config1", "config3", "store", "config4")
+
+
+def _store_sets(c, nsets, dev):
+    """``nsets`` independent copies of config 3's store inputs (new K/V rows drawn from their own
+    seeds, the same slot mapping, each set with its own caches): back-to-back stores over them
+    touch more than the L2 holds, so each call streams from HBM like a fresh one."""
+    import torch
+    sets = []
+    n, kvh = c.new_k.shape[0], c.new_k.shape[1]
+    for i in range(nsets):
+        g = torch.Generator(device=dev).manual_seed(1000 + i)
+        k = torch.randn(n, kvh, 128, generator=g, device=dev).to(torch.bfloat16)
+        v = torch.randn(n, kvh, 128, generator=g, device=dev).to(torch.bfloat16)
+        sets.append((k, v, torch.empty_like(c.k), torch.empty_like(c.v), c.slot_mapping))
+    return sets
+
+
+def _time_graph_calls(fn_all, ncalls, iters=20, warm=3):
+    """Per-call device time (ms) of a CUDA graph of ``ncalls`` back-to-back calls: the median
+    over replays of the graph's CUDA-event time, divided by ``ncalls``.  Short calls (~10 us) are
+    timed this way because a single call is near the event timer's resolution."""
+    import torch
+    fn_all()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        fn_all()
+    ms = _time_calls(graph.replay, iters=iters, warm=warm) / ncalls
+    del graph
+    return ms
+
+
+def secondary(dev, peaks, with_reference: bool, only=None):
     """Configs 2, 1, 3 (+ store) and 4 on one GPU, each timed with CUDA events after warm-up, and
-    the reference's Triton kernels on the same inputs where ``with_reference``."""
+    the reference's Triton kernels on the same inputs where ``with_reference``.  ``only`` names a
+    subset of PARTS (profile captures run one part by itself)."""
     import torch
     from nanovllm_b200 import fp8_decode_attention, fp8_prefill_attention, store_kvcache
     workloads = _load_workloads()
+    parts = set(only or PARTS)
     hbm_peak, bf16_peak = peaks[0], peaks[1]
     flush = torch.empty(64 << 20, dtype=torch.float32, device=dev)
     ref, ref_err = _reference_module() if with_reference else (None, "not requested")
@@ -319,11 +356,14 @@ def secondary(dev, peaks, with_reference: bool):
     if ref is None:
         refgpu["unavailable"] = ref_err
 
-    def ref_time(name, fn, ours_ms, ours_out=None, iters=5, warm=2, flush_l2=None):
+    def ref_time(name, fn, ours_ms, ours_out=None, iters=5, warm=2, flush_l2=None, ncalls=None):
         if ref is None:
             return
         try:
-            r_ms = _time_calls(fn, iters=iters, warm=warm, flush=flush_l2)
+            if ncalls is not None:
+                r_ms = _time_graph_calls(fn, ncalls)
+            else:
+                r_ms = _time_calls(fn, iters=iters, warm=warm, flush=flush_l2)
             entry = {"ms": r_ms, "ours_ms": ours_ms, "speedup": r_ms / ours_ms}
             if ours_out is not None:
                 entry["max_abs_diff_vs_ours"] = _maxdiff(fn(), ours_out)
@@ -331,14 +371,17 @@ def secondary(dev, peaks, with_reference: bool):
         except Exception as e:  # pragma: no cover
             refgpu[name] = {"unavailable": f"{type(e).__name__}: {e}"}
 
-    fp8_peak = _fp8_peak(dev)
-    fp8_kind = "measured e4m3 GEMM (torch._scaled_mm)"
+    fp8_peak, fp8_kind = None, "measured e4m3 GEMM (torch._scaled_mm)"
+    if "config3" in parts:
+        fp8_peak = _fp8_peak(dev)
     if fp8_peak is None:
         fp8_peak, fp8_kind = 2 * bf16_peak, "2 x measured bf16 GEMM"
 
     # ---- decode: config 2 (HBM bound, 1.2 GB) and config 1 (9 MB, latency bound)
     for name, make, l2 in (("config2", workloads.config2, "inputs larger than L2"),
                            ("config1", workloads.config1, "flushed before each call")):
+        if name not in parts:
+            continue
         c = make(dev)
         args = (c.q, c.k_cache, c.v_cache, c.block_tables, c.context_lens, c.scale)
         fl = flush if name == "config1" else None
@@ -356,84 +399,93 @@ def secondary(dev, peaks, with_reference: bool):
         torch.cuda.empty_cache()
 
     # ---- config 3: chunked prefill (tensor bound) and its K/V store (HBM bound)
-    c = workloads.config3(dev)
-    flops = c.causal_flops()
-    n = c.new_k.shape[0]
-    store_bytes = n * (2 * 8 * 128 * 2 + 2 * 8 * 128 + 4)
-    store_kvcache(c.new_k, c.new_v, c.k, c.v, c.slot_mapping)
-    torch.cuda.synchronize()
-    # the store is ~10 us of device work: time a CUDA graph of the call so that the host-side
-    # launch (the Python wrapper) is not measured
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
+    if parts & {"config3", "store"}:
+        c = workloads.config3(dev)
         store_kvcache(c.new_k, c.new_v, c.k, c.v, c.slot_mapping)
-    st_ms = _time_calls(graph.replay, flush=flush)
-    del graph
-    pf = lambda: fp8_prefill_attention(
-        c.q, c.k, c.v, block_tables=c.block_tables, cu_seqlens_q=c.cu_seqlens_q,
-        cu_seqlens_k=c.cu_seqlens_k, max_seqlen_q=c.max_seqlen_q, max_seqlen_k=c.max_seqlen_k,
-        softmax_scale=c.scale)
-    pf_ms = _time_calls(pf, flush=flush)
-    tflops = flops / (pf_ms * 1e-3) / 1e12
-    out["config3_prefill"] = {
-        "workload": "16 seqs, new U[128,512], cached prefix U[0,3584], Qwen3-8B heads, paged "
-                    "block 256", "ms": pf_ms, "tflops": tflops, "causal_flops": flops,
-        "tokens_per_s": int(c.q.shape[0]) / (pf_ms * 1e-3), "l2": "flushed before each call",
-        "roofline": {"bound": "tensor", "achieved": tflops, "peak": fp8_peak, "unit": "TFLOP/s",
-                     "frac": tflops / fp8_peak, "peak_kind": fp8_kind,
-                     "frac_of_bf16_sustained": tflops / peaks[2]}}
-    sgbs = store_bytes / (st_ms * 1e-3) / 1e9
-    out["config3_store"] = {"ms": st_ms, "gbs": sgbs, "rows": n, "bytes": store_bytes,
-                            "timing": "CUDA-graph replay, L2 flushed before each call",
-                            "roofline": {"bound": "hbm", "achieved": sgbs, "peak": hbm_peak,
-                                         "unit": "GB/s", "frac": sgbs / hbm_peak}}
-    if ref is not None:
-        ours = pf()
-        ref_time("prefill_config3", lambda: ref["prefill"](
+        torch.cuda.synchronize()
+    if "store" in parts:
+        n = c.new_k.shape[0]
+        store_bytes = n * (2 * 8 * 128 * 2 + 2 * 8 * 128 + 4)
+        sets = _store_sets(c, 8, dev)
+        st_ms = _time_graph_calls(lambda: [store_kvcache(*x) for x in sets], len(sets))
+        sgbs = store_bytes / (st_ms * 1e-3) / 1e9
+        out["config3_store"] = {
+            "ms": st_ms, "gbs": sgbs, "rows": n, "bytes": store_bytes,
+            "timing": "CUDA graph of 8 back-to-back calls on 8 independent input sets "
+                      "(300 MB in all, more than L2), per-call time",
+            "roofline": {"bound": "hbm", "achieved": sgbs, "peak": hbm_peak, "unit": "GB/s",
+                         "frac": sgbs / hbm_peak}}
+        if ref is not None:
+            ref_sets = [(k, v, kc.clone(), vc.clone(), sl) for k, v, kc, vc, sl in sets]
+            ref_time("store_config3", lambda: [ref["store"](*x) for x in ref_sets], st_ms,
+                     ncalls=len(ref_sets))
+            if "store_config3" in refgpu and "ms" in refgpu["store_config3"]:
+                refgpu["store_config3"]["bytes_equal_to_ours"] = all(
+                    torch.equal(a[2].view(torch.uint8), b[2].view(torch.uint8)) and
+                    torch.equal(a[3].view(torch.uint8), b[3].view(torch.uint8))
+                    for a, b in zip(sets, ref_sets))
+            del ref_sets
+        del sets
+        torch.cuda.empty_cache()
+    if "config3" in parts:
+        flops = c.causal_flops()
+        pf = lambda: fp8_prefill_attention(
             c.q, c.k, c.v, block_tables=c.block_tables, cu_seqlens_q=c.cu_seqlens_q,
             cu_seqlens_k=c.cu_seqlens_k, max_seqlen_q=c.max_seqlen_q,
-            max_seqlen_k=c.max_seqlen_k, softmax_scale=c.scale), pf_ms, ours, iters=3, warm=1,
-            flush_l2=flush)
-        kc2, vc2 = c.k.clone(), c.v.clone()
-        ref_time("store_config3", lambda: ref["store"](c.new_k, c.new_v, kc2, vc2,
-                                                       c.slot_mapping), st_ms, flush_l2=flush)
-        refgpu["store_config3"]["bytes_equal_to_ours"] = bool(
-            torch.equal(kc2.view(torch.uint8), c.k.view(torch.uint8)) and
-            torch.equal(vc2.view(torch.uint8), c.v.view(torch.uint8)))
-        del kc2, vc2
-    del c
-    torch.cuda.empty_cache()
+            max_seqlen_k=c.max_seqlen_k, softmax_scale=c.scale)
+        pf_ms = _time_calls(pf, flush=flush)
+        tflops = flops / (pf_ms * 1e-3) / 1e12
+        out["config3_prefill"] = {
+            "workload": "16 seqs, new U[128,512], cached prefix U[0,3584], Qwen3-8B heads, paged "
+                        "block 256", "ms": pf_ms, "tflops": tflops, "causal_flops": flops,
+            "tokens_per_s": int(c.q.shape[0]) / (pf_ms * 1e-3), "l2": "flushed before each call",
+            "roofline": {"bound": "tensor", "achieved": tflops, "peak": fp8_peak,
+                         "unit": "TFLOP/s", "frac": tflops / fp8_peak, "peak_kind": fp8_kind,
+                         "frac_of_bf16_sustained": tflops / peaks[2]}}
+        if ref is not None:
+            ours = pf()
+            ref_time("prefill_config3", lambda: ref["prefill"](
+                c.q, c.k, c.v, block_tables=c.block_tables, cu_seqlens_q=c.cu_seqlens_q,
+                cu_seqlens_k=c.cu_seqlens_k, max_seqlen_q=c.max_seqlen_q,
+                max_seqlen_k=c.max_seqlen_k, softmax_scale=c.scale), pf_ms, ours, iters=3,
+                warm=1, flush_l2=flush)
+    if parts & {"config3", "store"}:
+        del c
+        torch.cuda.empty_cache()
 
     # ---- config 4: one mixed call (192 spec-verify sequences of 5 rows + 2 fresh 512-row chunks)
-    c = workloads.config4(dev)
-    store_kvcache(c.new_k, c.new_v, c.k, c.v, c.slot_mapping)
-    cq, ck = c.cu_seqlens_q.tolist(), c.cu_seqlens_k.tolist()
-    nks = [ck[i + 1] - ck[i] for i in range(len(ck) - 1)]
-    nqs = [cq[i + 1] - cq[i] for i in range(len(cq) - 1)]
-    spec_bytes = sum(nk * 8 * 128 * 2 + 2 * nq * 32 * 128 * 2 for nk, nq in zip(nks, nqs) if nq <= 16)
-    mixed = lambda: fp8_prefill_attention(
-        c.q, c.k, c.v, block_tables=c.block_tables, cu_seqlens_q=c.cu_seqlens_q,
-        cu_seqlens_k=c.cu_seqlens_k, max_seqlen_q=c.max_seqlen_q, max_seqlen_k=c.max_seqlen_k,
-        softmax_scale=c.scale)
-    m_ms = _time_calls(mixed, iters=10, warm=3)
-    gbs = spec_bytes / (m_ms * 1e-3) / 1e9
-    out["config4_mixed"] = {
-        "workload": "192 spec-verify seqs (1+4 rows, ctx U[1024,8187]) + 2 fresh 512-token "
-                    "chunks, one prefill call, Qwen3-8B heads, paged block 256",
-        "ms": m_ms, "tokens_per_s": int(c.q.shape[0]) / (m_ms * 1e-3), "spec_bytes": spec_bytes,
-        "l2": "inputs larger than L2",
-        "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s",
-                     "frac": gbs / hbm_peak,
-                     "note": "spec-part bytes over the whole call's time (the two fresh chunks "
-                             "run in the same call)"}}
-    if ref is not None:
-        ours = mixed()
-        ref_time("mixed_config4", lambda: ref["prefill"](
+    if "config4" in parts:
+        c = workloads.config4(dev)
+        store_kvcache(c.new_k, c.new_v, c.k, c.v, c.slot_mapping)
+        cq, ck = c.cu_seqlens_q.tolist(), c.cu_seqlens_k.tolist()
+        nks = [ck[i + 1] - ck[i] for i in range(len(ck) - 1)]
+        nqs = [cq[i + 1] - cq[i] for i in range(len(cq) - 1)]
+        spec_bytes = sum(nk * 8 * 128 * 2 + 2 * nq * 32 * 128 * 2
+                         for nk, nq in zip(nks, nqs) if nq <= 16)
+        mixed = lambda: fp8_prefill_attention(
             c.q, c.k, c.v, block_tables=c.block_tables, cu_seqlens_q=c.cu_seqlens_q,
             cu_seqlens_k=c.cu_seqlens_k, max_seqlen_q=c.max_seqlen_q,
-            max_seqlen_k=c.max_seqlen_k, softmax_scale=c.scale), m_ms, ours, iters=2, warm=1)
-    del c
-    torch.cuda.empty_cache()
+            max_seqlen_k=c.max_seqlen_k, softmax_scale=c.scale)
+        m_ms = _time_calls(mixed, iters=10, warm=3)
+        gbs = spec_bytes / (m_ms * 1e-3) / 1e9
+        out["config4_mixed"] = {
+            "workload": "192 spec-verify seqs (1+4 rows, ctx U[1024,8187]) + 2 fresh 512-token "
+                        "chunks, one prefill call, Qwen3-8B heads, paged block 256",
+            "ms": m_ms, "tokens_per_s": int(c.q.shape[0]) / (m_ms * 1e-3),
+            "spec_bytes": spec_bytes, "l2": "inputs larger than L2",
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s",
+                         "frac": gbs / hbm_peak,
+                         "note": "spec-part bytes over the whole call's time (the two fresh "
+                                 "chunks run in the same call)"}}
+        if ref is not None:
+            ours = mixed()
+            ref_time("mixed_config4", lambda: ref["prefill"](
+                c.q, c.k, c.v, block_tables=c.block_tables, cu_seqlens_q=c.cu_seqlens_q,
+                cu_seqlens_k=c.cu_seqlens_k, max_seqlen_q=c.max_seqlen_q,
+                max_seqlen_k=c.max_seqlen_k, softmax_scale=c.scale), m_ms, ours, iters=2,
+                warm=1)
+        del c
+        torch.cuda.empty_cache()
     return out, refgpu
 
 
@@ -579,6 +631,18 @@ def run_ours(args, world, rank, local):
         "clocks": clk.summary(),
         "device_error": err,
     }
+    if world == 1 and args.batch == 64 and not args.no_reference_gpu:
+        ref, why = _reference_module()
+        if ref is None:
+            line["reference_gpu_decode_config5"] = {"unavailable": why}
+        else:  # the reference's own Triton decode on the headline inputs (same GPU)
+            args5 = (case.q, case.k_cache, case.v_cache, case.block_tables, case.context_lens,
+                     case.scale)
+            ours = step()
+            r_ms = _time_calls(lambda: ref["decode"](*args5), iters=5, warm=2)
+            line["reference_gpu_decode_config5"] = {
+                "ms": r_ms, "ours_ms": ms, "speedup": r_ms / ms,
+                "max_abs_diff_vs_ours": _maxdiff(ref["decode"](*args5), ours)}
     if world == 1 and args.batch == 64:
         del case
         torch.cuda.empty_cache()
@@ -605,6 +669,9 @@ def main():
     ap.add_argument("--batch", type=int, default=64,
                     help="config-5 sequences (64 = the benchmark; fewer for profile captures, "
                          "which then skip the secondary figures)")
+    ap.add_argument("--only", default=None,
+                    help="comma-separated secondary parts (%s) to run alone on one GPU, "
+                         "without the headline (profile captures)" % ",".join(PARTS))
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world, rank, local = _dist_init() if args.impl == "ours" else (
@@ -612,6 +679,15 @@ def main():
     try:
         if args.impl == "reference":
             run_reference(args, world, rank)
+        elif args.only:
+            import torch
+            from nanovllm_b200.fp8_attention import device_error
+            only = args.only.split(",")
+            assert set(only) <= set(PARTS), only
+            torch.cuda.set_device(0)
+            sec, _ = secondary(torch.device("cuda", 0), _peaks(), False, only)
+            sec["device_error"] = device_error()
+            print(json.dumps(sec), flush=True)
         else:
             run_ours(args, world, rank, local)
     finally:

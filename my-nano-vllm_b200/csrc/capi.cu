@@ -240,6 +240,58 @@ static int run_decode_engine(fp8attn::DecodeParams& p, const EnginePlan& e, cons
   return FP8ATTN_OK;
 }
 
+static int launch_prefill_engine(void* out, const void* q, int64_t q_row_stride, const void* k,
+                                 const void* v, int64_t kv_row_stride, const float* k_scale,
+                                 const float* v_scale, const int32_t* block_tables,
+                                 int64_t block_tables_stride, int max_num_blocks,
+                                 const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k,
+                                 int num_seqs, int max_seqlen_q, int num_heads, int num_kv_heads,
+                                 int group, bool paged, int64_t num_blocks, int block_size,
+                                 int min_q, float scale_log2, void* workspace, cudaStream_t st) {
+  const int head_dim = fp8attn::kHeadDim;
+  fp8attn::PrefillParams pp{};
+  pp.out = static_cast<uint16_t*>(out);
+  pp.out_row_stride = static_cast<int64_t>(num_heads) * head_dim;
+  pp.q = static_cast<const uint16_t*>(q);
+  pp.q_row_stride = q_row_stride;
+  pp.k = static_cast<const uint8_t*>(k);
+  pp.v = static_cast<const uint8_t*>(v);
+  pp.kv_row_stride = paged ? static_cast<int64_t>(num_kv_heads) * head_dim : kv_row_stride;
+  pp.k_scale = k_scale;
+  pp.v_scale = v_scale;
+  pp.block_tables = block_tables;
+  pp.bt_stride = block_tables_stride;
+  pp.max_blocks = max_num_blocks;
+  pp.cu_q = cu_seqlens_q;
+  pp.cu_k = cu_seqlens_k;
+  pp.num_seqs = num_seqs;
+  pp.max_seqlen_q = max_seqlen_q;
+  pp.num_heads = num_heads;
+  pp.num_kv_heads = num_kv_heads;
+  pp.group = group;
+  pp.block_size = paged ? block_size : 1;
+  pp.num_blocks = num_blocks;
+  pp.min_q = min_q;
+  pp.scale_log2 = scale_log2;
+  pp.err = static_cast<int*>(workspace);
+  const cudaError_t e = fp8attn::launch_prefill(pp, st);
+  if (e != cudaSuccess) return cuda_fail(e, "prefill launch");
+  return FP8ATTN_OK;
+}
+
+int fp8attn_read_error(const void* workspace, int32_t* dst, int clear, void* stream) {
+  if (workspace == nullptr || dst == nullptr) return fail(FP8ATTN_EINVAL, "null pointer argument");
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* word = static_cast<uint8_t*>(const_cast<void*>(workspace)) + FP8ATTN_WS_ERROR_OFFSET;
+  cudaError_t e = cudaMemcpyAsync(dst, word, sizeof(int32_t), cudaMemcpyDefault, st);
+  if (e != cudaSuccess) return cuda_fail(e, "error word copy");
+  if (clear) {
+    e = cudaMemsetAsync(word, 0, sizeof(int32_t), st);
+    if (e != cudaSuccess) return cuda_fail(e, "error word clear");
+  }
+  return FP8ATTN_OK;
+}
+
 int fp8attn_decode(void* out, const void* q, int64_t q_row_stride, const void* k_cache,
                    const void* v_cache, const float* k_scale, const float* v_scale,
                    const int32_t* block_tables, int64_t block_tables_stride, int max_num_blocks,
@@ -317,12 +369,21 @@ int fp8attn_prefill(void* out, const void* q, int64_t q_row_stride, const void* 
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   const float scale_log2 = softmax_scale * 1.4426950408889634f;
   int min_q = 1;
+  // speculative-verify sized sequences (paged layout) go to the split-KV decode engine, the
+  // rest to the prefill engine.  The prefill kernel is launched first and the decode engine
+  // after it as a programmatic dependent, so when no sequence is short the engine's set-up and
+  // empty plan overlap the prefill kernel's tail instead of delaying its start.
+  fp8attn::DecodeParams p{};
+  EnginePlan e{};
   if (paged) {
-    // speculative-verify sized sequences: split-KV decode engine
     const int sq = spec_q_max(group);
     const int mq = max_seqlen_q < sq ? max_seqlen_q : sq;
-    const EnginePlan e = plan_engine(group, mq);
-    fp8attn::DecodeParams p{};
+    e = plan_engine(group, mq);
+    const int64_t need = fp8attn::decode_workspace_bytes(num_seqs, num_kv_heads, e.max_rowgroups,
+                                                         e.rows, fp8attn::decode_grid(e.nt));
+    if (workspace == nullptr || workspace_bytes < need)
+      return fail(FP8ATTN_EWORKSPACE, "workspace of %lld bytes is smaller than the %lld needed",
+                  static_cast<long long>(workspace_bytes), static_cast<long long>(need));
     p.out = static_cast<uint16_t*>(out);
     p.out_row_stride = static_cast<int64_t>(num_heads) * head_dim;
     p.q = static_cast<const uint16_t*>(q);
@@ -343,53 +404,19 @@ int fp8attn_prefill(void* out, const void* q, int64_t q_row_stride, const void* 
     p.spec_mode = 1;
     p.spec_q_max = mq;
     p.scale_log2 = scale_log2;
-    rc = run_decode_engine(p, e, k, v, workspace, workspace_bytes, st);
-    if (rc) return rc;
     min_q = mq + 1;
-    if (max_seqlen_q < min_q) return FP8ATTN_OK;  // every sequence was short
   } else if (workspace == nullptr || workspace_bytes < 256) {
     return fail(FP8ATTN_EWORKSPACE, "workspace missing");
   }
-  fp8attn::PrefillParams pp{};
-  pp.out = static_cast<uint16_t*>(out);
-  pp.out_row_stride = static_cast<int64_t>(num_heads) * head_dim;
-  pp.q = static_cast<const uint16_t*>(q);
-  pp.q_row_stride = q_row_stride;
-  pp.k = static_cast<const uint8_t*>(k);
-  pp.v = static_cast<const uint8_t*>(v);
-  pp.kv_row_stride = paged ? static_cast<int64_t>(num_kv_heads) * head_dim : kv_row_stride;
-  pp.k_scale = k_scale;
-  pp.v_scale = v_scale;
-  pp.block_tables = block_tables;
-  pp.bt_stride = block_tables_stride;
-  pp.max_blocks = max_num_blocks;
-  pp.cu_q = cu_seqlens_q;
-  pp.cu_k = cu_seqlens_k;
-  pp.num_seqs = num_seqs;
-  pp.max_seqlen_q = max_seqlen_q;
-  pp.num_heads = num_heads;
-  pp.num_kv_heads = num_kv_heads;
-  pp.group = group;
-  pp.block_size = paged ? block_size : 1;
-  pp.num_blocks = num_blocks;
-  pp.min_q = min_q;
-  pp.scale_log2 = scale_log2;
-  pp.err = static_cast<int*>(workspace);
-  const cudaError_t e = fp8attn::launch_prefill(pp, st);
-  if (e != cudaSuccess) return cuda_fail(e, "prefill launch");
-  return FP8ATTN_OK;
-}
-
-int fp8attn_read_error(const void* workspace, int32_t* dst, int clear, void* stream) {
-  if (workspace == nullptr || dst == nullptr) return fail(FP8ATTN_EINVAL, "null pointer argument");
-  const cudaStream_t st = static_cast<cudaStream_t>(stream);
-  uint8_t* word = static_cast<uint8_t*>(const_cast<void*>(workspace)) + FP8ATTN_WS_ERROR_OFFSET;
-  cudaError_t e = cudaMemcpyAsync(dst, word, sizeof(int32_t), cudaMemcpyDefault, st);
-  if (e != cudaSuccess) return cuda_fail(e, "error word copy");
-  if (clear) {
-    e = cudaMemsetAsync(word, 0, sizeof(int32_t), st);
-    if (e != cudaSuccess) return cuda_fail(e, "error word clear");
+  if (max_seqlen_q >= min_q) {
+    rc = launch_prefill_engine(out, q, q_row_stride, k, v, kv_row_stride, k_scale, v_scale,
+                               block_tables, block_tables_stride, max_num_blocks, cu_seqlens_q,
+                               cu_seqlens_k, num_seqs, max_seqlen_q, num_heads, num_kv_heads,
+                               group, paged, num_blocks, block_size, min_q, scale_log2,
+                               workspace, st);
+    if (rc) return rc;
   }
+  if (paged) return run_decode_engine(p, e, k, v, workspace, workspace_bytes, st);
   return FP8ATTN_OK;
 }
 

@@ -43,11 +43,20 @@ namespace fp8attn {
 namespace {
 
 constexpr int kTile = kDecodeTile;  // key positions per stage
-constexpr int kMaxCtasPerSm = 2;  // the ring is sized so two CTAs share an SM
-constexpr int kProducerWarp = 4;
-constexpr int kMmaWarp = 5;
-constexpr int kThreads = 8 * 32;  // warps 6-7 idle (no role): 2 warps per scheduler, 2 CTAs per SM
-constexpr int kSoftmaxThreads = 128;
+constexpr int kMaxCtasPerSm = 2;  // single-plane engines: two CTAs share an SM
+// Warp roles.  Single-plane engines (NT = 1): softmax warps 0-3, producer warp 4, MMA warp 5;
+// warps 6-7 have no role (two warps per scheduler, which balances the register file so that two
+// CTAs share an SM).  Wide engines (NT > 1: 16 or 24 query rows per item): softmax warps 0-7, two
+// per tensor-memory lane quadrant, each with half of the rows; producer warp 8, MMA warp 9.
+template <int NT>
+struct Roles {
+  static constexpr int kSoftmaxWarps = NT == 1 ? 4 : 8;
+  static constexpr int kProducerWarp = kSoftmaxWarps;
+  static constexpr int kMmaWarp = kSoftmaxWarps + 1;
+  static constexpr int kWarps = NT == 1 ? 8 : 10;
+  static constexpr int kThreads = 32 * kWarps;
+  static constexpr int kSoftmaxThreads = 32 * kSoftmaxWarps;
+};
 constexpr int kMaxBoxes = kTile / 16;
 // Plan target: work items per CTA, at most kItemsPerCta (the bound the workspace is sized for).
 // An item costs about kItemCostTokens key positions of fixed work (claim, query operand, first
@@ -81,7 +90,10 @@ template <int NT>
 struct __align__(1024) DecodeSmem {
   static constexpr int R = 8 * NT;  // query rows per item
   static constexpr int N = 2 * R;   // S / O columns: rows 0..R-1 hi, R..2R-1 lo
-  static constexpr int STAGES = NT == 1 ? 3 : 2;  // two CTAs per SM fit either way
+  // single-plane engines: 3 stages, two CTAs per SM; wide engines: one CTA per SM (10 warps at
+  // up to 204 registers) with 5 stages, which keeps more K/V bytes in flight per SM than two
+  // CTAs with 2 stages each could (measured on 192 verify sequences of 5 rows: 0.86 -> 0.78 ms)
+  static constexpr int STAGES = NT == 1 ? 3 : 5;
   uint8_t k[STAGES][kTile * kHeadDim];  // 16 KB each, 1024-aligned
   uint8_t v[STAGES][kTile * kHeadDim];
   uint8_t q2[2][N * kHeadDim];            // K-major SW128 query operand, by item parity
@@ -90,7 +102,7 @@ struct __align__(1024) DecodeSmem {
   uint8_t qstage[R * 256];                // raw bf16 query rows of the next item (cp.async)
   float alpha[4][R];                      // per-warp copy of a tile's rescale factors (rare)
   float red[2][4][R];                     // cross-warp row maxima, double-buffered by tile
-  alignas(16) int vote[2][4];             // per warp: a score above its row's reference + 2^4
+  alignas(16) int vote[2][8];             // per warp: a score above its row's reference + 2^4
   float redl[2][4][R];                    // an item's per-warp row sums, by item parity
   float mfin[2][R];                       // an item's final reference maxima, by item parity
   alignas(16) int hdr[STAGES][kHdrWords];
@@ -103,7 +115,7 @@ struct __align__(1024) DecodeSmem {
   uint64_t pv_done[2];
   uint64_t q_full[2];
   uint64_t q_empty[2];
-  uint64_t sync128;  // bounded barrier of the 128 softmax threads
+  uint64_t sync128[2];  // bounded barriers of 128 softmax threads (the wide engines' halves)
   uint32_t tmem_base;
   int scratch[16];
   unsigned long long total_work;
@@ -120,9 +132,11 @@ struct __align__(1024) DecodeSmem {
 
 // Two CTAs share an SM (228 KB of shared memory, 1 KB reserved per CTA) with the sorted plan
 // arrays of up to 256 sequences, and at any batch size with the sampled plan.
-static_assert(sizeof(DecodeSmem<1>) + 2 * 1024 + (3 * 256 + 1) * 4 <= 228 * 1024 / 2, "smem");
-static_assert(sizeof(DecodeSmem<2>) + 2 * 1024 + (3 * 256 + 1) * 4 <= 228 * 1024 / 2, "smem");
-static_assert(sizeof(DecodeSmem<3>) + 2 * 1024 + (3 * 256 + 1) * 4 <= 228 * 1024 / 2, "smem");
+static_assert(sizeof(DecodeSmem<1>) + 2 * 1024 + (2 * Roles<1>::kThreads + 1) * 4 <= 228 * 1024 / 2,
+              "smem");
+// The wide engines run one CTA per SM: their ring and the largest plan fit one CTA's limit.
+static_assert(sizeof(DecodeSmem<2>) + 1024 + (3 * kMaxSeqs + 1) * 4 <= 227 * 1024, "smem");
+static_assert(sizeof(DecodeSmem<3>) + 1024 + (3 * kMaxSeqs + 1) * 4 <= 227 * 1024, "smem");
 // Claim order of a batch of up to kThreads sequences on the wide (spec-verify) engines: by the
 // length of their chunks, in tiles (capped at kSortKeys), shortest first, ties by index; with
 // chunks of about the same length at the end of the work, the CTAs finish together.  Measured:
@@ -130,11 +144,12 @@ static_assert(sizeof(DecodeSmem<3>) + 2 * 1024 + (3 * 256 + 1) * 4 <= 228 * 1024
 // the same order, permuted on the host, made 256 sequences of 512-4096 tokens 3.4 % faster, but
 // the sort in the plan cost about as much as it saved there.
 constexpr int kSortKeys = 32;
-constexpr int kWarps = kThreads / 32;
-static_assert(kSortKeys * kWarps == kThreads, "one (key, warp) count per thread");
-// sequences per range of the sampled plan, at most: they fit the lanes of the producer warp
-constexpr int kMaxPlanPer = (kMaxSeqs + kThreads - 1) / kThreads;
-static_assert(kMaxPlanPer <= 32 && 2 * kThreads + 1 <= 2 * 256 + 1, "sampled plan");
+static_assert(kSortKeys * Roles<1>::kWarps == Roles<1>::kThreads &&
+              kSortKeys * Roles<2>::kWarps == Roles<2>::kThreads, "one (key, warp) count per thread");
+// sequences per range of the sampled plan, at most (for the smaller CTA): they fit the lanes of
+// the producer warp
+constexpr int kMaxPlanPer = (kMaxSeqs + Roles<1>::kThreads - 1) / Roles<1>::kThreads;
+static_assert(kMaxPlanPer <= 32, "sampled plan");
 
 __device__ __forceinline__ int seq_len_clamped(const DecodeParams& p, int b, int* nq_out) {
   int L, nq;
@@ -157,7 +172,8 @@ __device__ __forceinline__ int seq_rowgroups(int L, int nq, int group, int R) {
   return L > 0 ? (nq * group + R - 1) / R : 0;
 }
 
-// Block-wide exclusive scan of one int per thread.
+// Block-wide exclusive scan of one int per thread (kThreads threads).
+template <int kThreads>
 __device__ __forceinline__ int block_exclusive_scan(int v, int* smem, int* total) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   int x = v;
@@ -369,9 +385,14 @@ __device__ __forceinline__ void prepare_q(const Cursor<NT>& P, int slot, const D
 }
 
 template <int NT, int RV, bool kSampled>
-__global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
+__global__ void __launch_bounds__(Roles<NT>::kThreads, NT == 1 ? kMaxCtasPerSm : 1)
     decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                   const DecodeParams p) {
+  constexpr int kThreads = Roles<NT>::kThreads;
+  constexpr int kWarps = Roles<NT>::kWarps;
+  constexpr int kProducerWarp = Roles<NT>::kProducerWarp;
+  constexpr int kMmaWarp = Roles<NT>::kMmaWarp;
+  constexpr int kSoftmaxThreads = Roles<NT>::kSoftmaxThreads;
   using Smem = DecodeSmem<NT>;
   constexpr int R = Smem::R;
   constexpr int N = Smem::N;
@@ -408,7 +429,8 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
       mbar_init(&sm.p_full[i], kSoftmaxThreads);
       mbar_init(&sm.pv_done[i], 1);
     }
-    mbar_init(&sm.sync128, kSoftmaxThreads);
+    mbar_init(&sm.sync128[0], 128);
+    mbar_init(&sm.sync128[1], 128);
     fence_mbar_init();
     sm.total_work = 0;
   }
@@ -483,7 +505,7 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
     }
   }
   int total_items = 0, base = 0;
-  if (!sorted_plan) base = block_exclusive_scan(my_items, sm.scratch, &total_items);
+  if (!sorted_plan) base = block_exclusive_scan<kThreads>(my_items, sm.scratch, &total_items);
   if constexpr (kSampled) {
     prefix[tid] = base;
     if (tid == kThreads - 1) prefix[kThreads] = total_items;
@@ -522,7 +544,7 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
     if (valid && rank == 0) counts[key * kWarps + warp] = __popc(peers);
     __syncthreads();
     int nseq;
-    const int first = block_exclusive_scan(counts[tid], sm.scratch, &nseq);
+    const int first = block_exclusive_scan<kThreads>(counts[tid], sm.scratch, &nseq);
     counts[tid] = first;
     __syncthreads();
     if (valid) perm[counts[key * kWarps + warp] + rank] = tid;
@@ -534,7 +556,7 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
       const int inf = info[sb];
       scnt = ((inf >> 7) + CT - 1) / CT * p.num_kv_heads * (inf & 127);
     }
-    const int sbase = block_exclusive_scan(scnt, sm.scratch, &total_items);
+    const int sbase = block_exclusive_scan<kThreads>(scnt, sm.scratch, &total_items);
     if (valid) prefix[tid] = sbase;
     if (tid == kThreads - 1) prefix[B] = total_items;
     if (blockIdx.x == 0) {  // the combine kernel reads each sequence's first item after this launch
@@ -770,265 +792,516 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm)
       if (pend) issue_pv(pend_stage, j - 1, pend_first, pend_ob);
     }
     __syncwarp();
-  } else if (fits && warp < 4) {
-    // ============================================================ softmax warps 0-3
-    // thread r: token row r of S^T and dim row r of O^T.  Per row q of the row group (the first
-    // RV are live): m_ref[q] = reference max (log2 units, uniform over the 128 threads), l_part[q]
-    // = this thread's share of the row sum, both relative to m_ref.
-    const int r = tid;
-    const uint32_t lane_base = static_cast<uint32_t>(32 * warp) << 16;
-    const bool kscaled = p.k_scale != nullptr;
-    const bool vscaled = p.v_scale != nullptr;
-    const int box_shift = 31 - __clz(p.box_rows);
-    constexpr float kRescaleLog2 = 4.f;  // P = 16 * 2^(s - m_ref) <= 256 < 448 (e4m3 max)
-    constexpr float kPScale = 16.f;
-    float m_ref[RV], l_part[RV];
-    // up to 8 live rows keep their score multiplier and causal limit in registers
-    constexpr bool kRowRegs = RV <= 8;
-    float cs_r[kRowRegs ? RV : 1];
-    int rows_i = 0, qrow_lo = 0;  // the item's live rows; spec mode: (nk - nq) G + rg R
-    int kvh = 0;
-    int stage = 0, j = 0, sync_uses = 0, item_first_tile = 0;
-    uint32_t phase = 0;
-    int qcount[2] = {0, 0};
-    auto sync = [&]() -> bool {
-      mbar_arrive(&sm.sync128);
-      return mbar_wait(&sm.sync128, (sync_uses++) & 1, p.ctrl);
-    };
-    auto wait_pv = [&](int t) -> bool {
-      const int b = t & 1;
-      if (!mbar_wait(&sm.pv_done[b], (t >> 1) & 1, p.ctrl)) return false;
-      tc::fence_after_sync();
-      return true;
-    };
-    const uint32_t o_base = tmem + lane_base + 2 * N;  // O of an item: o_base + (item parity) N
-    int nitem = 0;  // items started
-    // the item whose read-out is deferred to the next tile (its last PV is then normally done,
-    // and its row-sum exchange rides on that tile's barrier)
-    bool pend_ep = false;
-    int pend_j = 0, pend_ob = 0, pend_slot = 0, pend_item = 0;
-    auto finish = [&]() -> bool {
-      if (!wait_pv(pend_j)) return false;
-      float o[RV];
-#pragma unroll
-      for (int q = 0; q < RV; ++q) o[q] = 0.f;
-#pragma unroll
-      for (int c = 0; c < N; c += 16) {
-        float o16[16];
-        tc::ld16(o_base + pend_ob * N + c, o16);
-        tc::wait_ld();
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int q = (c + i) % R;
-          if (q < RV) o[q] += o16[i];
-        }
-      }
-      tc::fence_before_sync();
-      const ItemInfo ii = sm.iinfo[pend_slot];
-      const int rows = ii.rows, nchunks = ii.nchunks, rg = ii.rg, qrow0 = ii.qrow0;
-      const int d = r;  // output dim
-#pragma unroll
-      for (int q = 0; q < RV; ++q) {
-        if (q >= rows) break;
-        const float lsum = sm.redl[pend_ob][0][q] + sm.redl[pend_ob][1][q] +
-                           sm.redl[pend_ob][2][q] + sm.redl[pend_ob][3][q];
-        if (nchunks == 1) {
-          const int rr = rg * R + q;
-          const int jj = rr / G, hh = ii.kvh * G + (rr - jj * G);
-          __nv_bfloat16 v = out_round(o[q] / fmaxf(lsum, 1e-10f));
-          p.out[static_cast<int64_t>(qrow0 + jj) * p.out_row_stride + hh * kHeadDim + d] =
-              *reinterpret_cast<uint16_t*>(&v);
-        } else {
-          float* part = p.partials + (static_cast<int64_t>(pend_item) * R + q) * (kHeadDim + 4);
-          part[d] = o[q];
-          if (d == 0) {
-            // a chunk whose rows saw no key position carries no weight in the combine
-            part[kHeadDim] = lsum > 0.f ? sm.mfin[pend_ob][q] : -INFINITY;
-            part[kHeadDim + 1] = lsum;
-          }
-        }
-      }
-      mbar_arrive(&sm.q_empty[pend_slot]);
-      pend_ep = false;
-      return true;
-    };
-    while (true) {
-      if (!mbar_wait(&sm.kv_full[stage], phase, p.ctrl)) break;
-      // everything this tile needs from its header, read now: once P is handed over, the PV
-      // completes, the stage is released and the producer rewrites the header
-      const int4 hw = *reinterpret_cast<const int4*>(&sm.hdr[stage][0]);
-      const int item = hw.x;
-      if (item < 0) break;
-      const int tok0 = hw.y, nvalid = hw.z, flags = hw.w & 15, slot = hw.w >> 4;
-      const int slot0 = sm.hdr[stage][kHdrSlot0 + (r >> box_shift)];
-      const bool valid = r < nvalid && slot0 >= 0;
-      if (flags & kFirst) {
-        if (!mbar_wait(&sm.q_full[slot], qcount[slot] & 1, p.ctrl)) break;
-        qcount[slot]++;
-        ++nitem;
-        item_first_tile = j;
-        kvh = sm.iinfo[slot].kvh;
-        rows_i = sm.iinfo[slot].rows;
-        // spec mode: row q = rg R + q of the sequence (token (rg R + q) / G) sees key positions
-        // <= mbase + token, i.e. position pos is visible to rows q >= (pos - mbase) G - rg R
-        qrow_lo = p.spec_mode ? sm.iinfo[slot].mbase * G + sm.iinfo[slot].rg * R : 0;
-#pragma unroll
-        for (int q = 0; q < RV; ++q) {
-          m_ref[q] = -INFINITY;
-          l_part[q] = 0.f;
-          if constexpr (kRowRegs) cs_r[q] = sm.qscale[slot][q];
-        }
-      }
-      float ks = 1.f, lv = 0.f;
-      if ((kscaled || vscaled) && valid) {
-        const int64_t idx = (static_cast<int64_t>(slot0) + (r & (p.box_rows - 1))) * p.num_kv_heads + kvh;
-        if (kscaled) ks = __ldg(p.k_scale + idx);
-        if (vscaled) lv = lg2(__ldg(p.v_scale + idx));
-      }
-      // ---------------------------------------------------- scores of this token row
-      const int sb = j & 1;
-      if (!mbar_wait(&sm.s_full[sb], (j >> 1) & 1, p.ctrl)) break;
-      tc::fence_after_sync();
-      float x[N];
-#pragma unroll
-      for (int c = 0; c < N; c += 16) {
-        float v16[16];
-        tc::ld16(tmem + lane_base + sb * N + c, v16);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) x[c + i] = v16[i];
-      }
-      tc::wait_ld();
-      tc::fence_before_sync();
-      mbar_arrive(&sm.s_empty[sb]);
-      const int pos = tok0 + r;
-      // rows [qmin, rows_i) see this thread's key position (all live rows outside spec mode)
-      const int qmin = !valid ? INT_MAX : (p.spec_mode ? pos * G - qrow_lo : INT_MIN);
-      float xs[RV];  // score (log2 units) + log2 of the value scale: P's exponent
-      bool over = false;  // a score the current reference cannot take (P would pass 256)
-#pragma unroll
-      for (int q = 0; q < RV; ++q) {
-        float csq;
-        if constexpr (kRowRegs) {
-          csq = cs_r[kRowRegs ? q : 0];
-        } else {
-          const float4 c4 = *reinterpret_cast<const float4*>(&sm.qscale[slot][q & ~3]);
-          csq = (q & 3) == 0 ? c4.x : (q & 3) == 1 ? c4.y : (q & 3) == 2 ? c4.z : c4.w;
-        }
-        float sc = (x[q] + x[R + q]) * csq * ks;
-        if (!(q >= qmin && q < rows_i)) sc = -INFINITY;
-        xs[q] = sc + lv;
-        over |= xs[q] > m_ref[q] + kRescaleLog2;
-      }
-      // one vote per warp; the exact per-row maxima are exchanged only when some warp needs a
-      // new reference (an item's first tile, and rare growth after it)
-      const bool wover = __any_sync(0xffffffffu, over);
-      if (lane == 0) sm.vote[sb][warp] = wover ? 1 : 0;
-      if (!sync()) break;
-      const int4 votes = *reinterpret_cast<const int4*>(&sm.vote[sb][0]);
-      uint32_t resc = 0;  // rows whose reference moved (uniform); factors in this warp's alpha row
-      if (votes.x | votes.y | votes.z | votes.w) {
-#pragma unroll
-        for (int q = 0; q < RV; ++q) {
-          const int wm = __reduce_max_sync(0xffffffffu, f2ord(xs[q]));
-          if (lane == 0) sm.red[sb][warp][q] = ord2f(wm);
-        }
-        if (!sync()) break;
-#pragma unroll
-        for (int q = 0; q < RV; ++q) {
-          const float tmax = fmaxf(fmaxf(sm.red[sb][0][q], sm.red[sb][1][q]),
-                                   fmaxf(sm.red[sb][2][q], sm.red[sb][3][q]));
-          if (tmax > m_ref[q] + kRescaleLog2) {
-            const float a = m_ref[q] == -INFINITY ? 0.f : ex2(m_ref[q] - tmax);
-            m_ref[q] = tmax;
-            l_part[q] *= a;
-            resc |= 1u << q;
-            if (lane == 0) sm.alpha[warp][q] = a;
-          }
-        }
-      }
-      // ---------------------------------------------------- P and row sums
-#pragma unroll
-      for (int q = 0; q < RV; ++q) {
-        const float m_use = m_ref[q] == -INFINITY ? 0.f : m_ref[q];
-        const float pe = kPScale * ex2(xs[q] - m_use);
-        l_part[q] += vscaled ? kPScale * ex2(xs[q] - lv - m_use) : pe;
-        xs[q] = pe;
-      }
-      // P^T row r: 2R bytes, hi rows then lo rows, as 16-byte planes of 16 columns
-      uint32_t words[R / 2];
-#pragma unroll
-      for (int w = 0; w < R / 2; ++w) words[w] = 0u;
-#pragma unroll
-      for (int w = 0; w < RV / 4; ++w) {
-        const uint32_t a = pack_f16x2(xs[4 * w], xs[4 * w + 1]);
-        const uint32_t b = pack_f16x2(xs[4 * w + 2], xs[4 * w + 3]);
-        uint32_t ah, al, bh, bl;
-        split_f16x2_e4m3(a, ah, al);
-        split_f16x2_e4m3(b, bh, bl);
-        words[w] = ah | (bh << 16);
-        words[R / 4 + w] = al | (bl << 16);
-      }
-      // O rescale (rare): O must be quiescent, i.e. the previous tile's PV done
-      if (resc && j > item_first_tile) {
-        __syncwarp();
-        if (!wait_pv(j - 1)) break;
-#pragma unroll
+  } else if (fits && warp < Roles<NT>::kSoftmaxWarps) {
+    if constexpr (NT == 1) {
+      // ============================================================ softmax warps 0-3
+      // thread r: token row r of S^T and dim row r of O^T.  Per row q of the row group (the first
+      // RV are live): m_ref[q] = reference max (log2 units, uniform over the 128 threads), l_part[q]
+      // = this thread's share of the row sum, both relative to m_ref.
+      const int r = tid;
+      const uint32_t lane_base = static_cast<uint32_t>(32 * warp) << 16;
+      const bool kscaled = p.k_scale != nullptr;
+      const bool vscaled = p.v_scale != nullptr;
+      const int box_shift = 31 - __clz(p.box_rows);
+      constexpr float kRescaleLog2 = 4.f;  // P = 16 * 2^(s - m_ref) <= 256 < 448 (e4m3 max)
+      constexpr float kPScale = 16.f;
+      float m_ref[RV], l_part[RV];
+      // up to 8 live rows keep their score multiplier and causal limit in registers
+      constexpr bool kRowRegs = RV <= 8;
+      float cs_r[kRowRegs ? RV : 1];
+      int rows_i = 0, qrow_lo = 0;  // the item's live rows; spec mode: (nk - nq) G + rg R
+      int kvh = 0;
+      int stage = 0, j = 0, sync_uses = 0, item_first_tile = 0;
+      uint32_t phase = 0;
+      int qcount[2] = {0, 0};
+      auto sync = [&]() -> bool {
+        mbar_arrive(&sm.sync128[0]);
+        return mbar_wait(&sm.sync128[0], (sync_uses++) & 1, p.ctrl);
+      };
+      auto wait_pv = [&](int t) -> bool {
+        const int b = t & 1;
+        if (!mbar_wait(&sm.pv_done[b], (t >> 1) & 1, p.ctrl)) return false;
+        tc::fence_after_sync();
+        return true;
+      };
+      const uint32_t o_base = tmem + lane_base + 2 * N;  // O of an item: o_base + (item parity) N
+      int nitem = 0;  // items started
+      // the item whose read-out is deferred to the next tile (its last PV is then normally done,
+      // and its row-sum exchange rides on that tile's barrier)
+      bool pend_ep = false;
+      int pend_j = 0, pend_ob = 0, pend_slot = 0, pend_item = 0;
+      auto finish = [&]() -> bool {
+        if (!wait_pv(pend_j)) return false;
+        float o[RV];
+  #pragma unroll
+        for (int q = 0; q < RV; ++q) o[q] = 0.f;
+  #pragma unroll
         for (int c = 0; c < N; c += 16) {
           float o16[16];
-          const uint32_t o_cur = o_base + ((nitem - 1) & 1) * N;
-          tc::ld16(o_cur + c, o16);
+          tc::ld16(o_base + pend_ob * N + c, o16);
           tc::wait_ld();
-#pragma unroll
+  #pragma unroll
           for (int i = 0; i < 16; ++i) {
             const int q = (c + i) % R;
-            if (q < RV && ((resc >> q) & 1u)) o16[i] *= sm.alpha[warp][q];
+            if (q < RV) o[q] += o16[i];
           }
-          tc::st16(o_cur + c, o16);
         }
-        tc::wait_st();
-      }
-      // P buffer sb was last read by PV_{j-2}
-      if (j >= 2 && !wait_pv(j - 2)) break;
-#pragma unroll
-      for (int plane = 0; plane < NT; ++plane)
-        *reinterpret_cast<uint4*>(&sm.p2[sb][plane][r * 16]) =
-            make_uint4(words[4 * plane], words[4 * plane + 1], words[4 * plane + 2], words[4 * plane + 3]);
-      if (!valid) {  // masked rows may hold any bytes (NaN codes): zero V's row
-        uint4* vrow = reinterpret_cast<uint4*>(&sm.v[stage][r * 128]);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) vrow[i] = make_uint4(0, 0, 0, 0);
-      }
-      fence_proxy_async_smem();
-      tc::fence_before_sync();
-      mbar_arrive(&sm.p_full[sb]);
-
-      // the previous item's read-out (its sums were exchanged at this tile's barrier)
-      if (pend_ep && !finish()) break;
-      if (flags & kLast) {
-        // park the item: per-warp row sums and the final maxima, read out one tile later
-        const int ob = (nitem - 1) & 1;
-#pragma unroll
+        tc::fence_before_sync();
+        const ItemInfo ii = sm.iinfo[pend_slot];
+        const int rows = ii.rows, nchunks = ii.nchunks, rg = ii.rg, qrow0 = ii.qrow0;
+        const int d = r;  // output dim
+  #pragma unroll
         for (int q = 0; q < RV; ++q) {
-          float l = l_part[q];
-#pragma unroll
-          for (int off = 16; off > 0; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
-          if (lane == 0) sm.redl[ob][warp][q] = l;
-          if (tid == 0) sm.mfin[ob][q] = m_ref[q];
+          if (q >= rows) break;
+          const float lsum = sm.redl[pend_ob][0][q] + sm.redl[pend_ob][1][q] +
+                             sm.redl[pend_ob][2][q] + sm.redl[pend_ob][3][q];
+          if (nchunks == 1) {
+            const int rr = rg * R + q;
+            const int jj = rr / G, hh = ii.kvh * G + (rr - jj * G);
+            __nv_bfloat16 v = out_round(o[q] / fmaxf(lsum, 1e-10f));
+            p.out[static_cast<int64_t>(qrow0 + jj) * p.out_row_stride + hh * kHeadDim + d] =
+                *reinterpret_cast<uint16_t*>(&v);
+          } else {
+            float* part = p.partials + (static_cast<int64_t>(pend_item) * R + q) * (kHeadDim + 4);
+            part[d] = o[q];
+            if (d == 0) {
+              // a chunk whose rows saw no key position carries no weight in the combine
+              part[kHeadDim] = lsum > 0.f ? sm.mfin[pend_ob][q] : -INFINITY;
+              part[kHeadDim + 1] = lsum;
+            }
+          }
         }
-        pend_ep = true;
-        pend_j = j;
-        pend_ob = ob;
-        pend_slot = slot;
-        pend_item = item;
-        if constexpr (NT > 1) {  // wide row groups: read out at once (registers are scarce)
-          if (!sync() || !finish()) break;
+        mbar_arrive(&sm.q_empty[pend_slot]);
+        pend_ep = false;
+        return true;
+      };
+      while (true) {
+        if (!mbar_wait(&sm.kv_full[stage], phase, p.ctrl)) break;
+        // everything this tile needs from its header, read now: once P is handed over, the PV
+        // completes, the stage is released and the producer rewrites the header
+        const int4 hw = *reinterpret_cast<const int4*>(&sm.hdr[stage][0]);
+        const int item = hw.x;
+        if (item < 0) break;
+        const int tok0 = hw.y, nvalid = hw.z, flags = hw.w & 15, slot = hw.w >> 4;
+        const int slot0 = sm.hdr[stage][kHdrSlot0 + (r >> box_shift)];
+        const bool valid = r < nvalid && slot0 >= 0;
+        if (flags & kFirst) {
+          if (!mbar_wait(&sm.q_full[slot], qcount[slot] & 1, p.ctrl)) break;
+          qcount[slot]++;
+          ++nitem;
+          item_first_tile = j;
+          kvh = sm.iinfo[slot].kvh;
+          rows_i = sm.iinfo[slot].rows;
+          // spec mode: row q = rg R + q of the sequence (token (rg R + q) / G) sees key positions
+          // <= mbase + token, i.e. position pos is visible to rows q >= (pos - mbase) G - rg R
+          qrow_lo = p.spec_mode ? sm.iinfo[slot].mbase * G + sm.iinfo[slot].rg * R : 0;
+  #pragma unroll
+          for (int q = 0; q < RV; ++q) {
+            m_ref[q] = -INFINITY;
+            l_part[q] = 0.f;
+            if constexpr (kRowRegs) cs_r[q] = sm.qscale[slot][q];
+          }
         }
+        float ks = 1.f, lv = 0.f;
+        if ((kscaled || vscaled) && valid) {
+          const int64_t idx = (static_cast<int64_t>(slot0) + (r & (p.box_rows - 1))) * p.num_kv_heads + kvh;
+          if (kscaled) ks = __ldg(p.k_scale + idx);
+          if (vscaled) lv = lg2(__ldg(p.v_scale + idx));
+        }
+        // ---------------------------------------------------- scores of this token row
+        const int sb = j & 1;
+        if (!mbar_wait(&sm.s_full[sb], (j >> 1) & 1, p.ctrl)) break;
+        tc::fence_after_sync();
+        float x[N];
+  #pragma unroll
+        for (int c = 0; c < N; c += 16) {
+          float v16[16];
+          tc::ld16(tmem + lane_base + sb * N + c, v16);
+  #pragma unroll
+          for (int i = 0; i < 16; ++i) x[c + i] = v16[i];
+        }
+        tc::wait_ld();
+        tc::fence_before_sync();
+        mbar_arrive(&sm.s_empty[sb]);
+        const int pos = tok0 + r;
+        // rows [qmin, rows_i) see this thread's key position (all live rows outside spec mode)
+        const int qmin = !valid ? INT_MAX : (p.spec_mode ? pos * G - qrow_lo : INT_MIN);
+        float xs[RV];  // score (log2 units) + log2 of the value scale: P's exponent
+        bool over = false;  // a score the current reference cannot take (P would pass 256)
+  #pragma unroll
+        for (int q = 0; q < RV; ++q) {
+          float csq;
+          if constexpr (kRowRegs) {
+            csq = cs_r[kRowRegs ? q : 0];
+          } else {
+            const float4 c4 = *reinterpret_cast<const float4*>(&sm.qscale[slot][q & ~3]);
+            csq = (q & 3) == 0 ? c4.x : (q & 3) == 1 ? c4.y : (q & 3) == 2 ? c4.z : c4.w;
+          }
+          float sc = (x[q] + x[R + q]) * csq * ks;
+          if (!(q >= qmin && q < rows_i)) sc = -INFINITY;
+          xs[q] = sc + lv;
+          over |= xs[q] > m_ref[q] + kRescaleLog2;
+        }
+        // one vote per warp; the exact per-row maxima are exchanged only when some warp needs a
+        // new reference (an item's first tile, and rare growth after it)
+        const bool wover = __any_sync(0xffffffffu, over);
+        if (lane == 0) sm.vote[sb][warp] = wover ? 1 : 0;
+        if (!sync()) break;
+        const int4 votes = *reinterpret_cast<const int4*>(&sm.vote[sb][0]);
+        uint32_t resc = 0;  // rows whose reference moved (uniform); factors in this warp's alpha row
+        if (votes.x | votes.y | votes.z | votes.w) {
+  #pragma unroll
+          for (int q = 0; q < RV; ++q) {
+            const int wm = __reduce_max_sync(0xffffffffu, f2ord(xs[q]));
+            if (lane == 0) sm.red[sb][warp][q] = ord2f(wm);
+          }
+          if (!sync()) break;
+  #pragma unroll
+          for (int q = 0; q < RV; ++q) {
+            const float tmax = fmaxf(fmaxf(sm.red[sb][0][q], sm.red[sb][1][q]),
+                                     fmaxf(sm.red[sb][2][q], sm.red[sb][3][q]));
+            if (tmax > m_ref[q] + kRescaleLog2) {
+              const float a = m_ref[q] == -INFINITY ? 0.f : ex2(m_ref[q] - tmax);
+              m_ref[q] = tmax;
+              l_part[q] *= a;
+              resc |= 1u << q;
+              if (lane == 0) sm.alpha[warp][q] = a;
+            }
+          }
+        }
+        // ---------------------------------------------------- P and row sums
+  #pragma unroll
+        for (int q = 0; q < RV; ++q) {
+          const float m_use = m_ref[q] == -INFINITY ? 0.f : m_ref[q];
+          const float pe = kPScale * ex2(xs[q] - m_use);
+          l_part[q] += vscaled ? kPScale * ex2(xs[q] - lv - m_use) : pe;
+          xs[q] = pe;
+        }
+        // P^T row r: 2R bytes, hi rows then lo rows, as 16-byte planes of 16 columns
+        uint32_t words[R / 2];
+  #pragma unroll
+        for (int w = 0; w < R / 2; ++w) words[w] = 0u;
+  #pragma unroll
+        for (int w = 0; w < RV / 4; ++w) {
+          const uint32_t a = pack_f16x2(xs[4 * w], xs[4 * w + 1]);
+          const uint32_t b = pack_f16x2(xs[4 * w + 2], xs[4 * w + 3]);
+          uint32_t ah, al, bh, bl;
+          split_f16x2_e4m3(a, ah, al);
+          split_f16x2_e4m3(b, bh, bl);
+          words[w] = ah | (bh << 16);
+          words[R / 4 + w] = al | (bl << 16);
+        }
+        // O rescale (rare): O must be quiescent, i.e. the previous tile's PV done
+        if (resc && j > item_first_tile) {
+          __syncwarp();
+          if (!wait_pv(j - 1)) break;
+  #pragma unroll
+          for (int c = 0; c < N; c += 16) {
+            float o16[16];
+            const uint32_t o_cur = o_base + ((nitem - 1) & 1) * N;
+            tc::ld16(o_cur + c, o16);
+            tc::wait_ld();
+  #pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const int q = (c + i) % R;
+              if (q < RV && ((resc >> q) & 1u)) o16[i] *= sm.alpha[warp][q];
+            }
+            tc::st16(o_cur + c, o16);
+          }
+          tc::wait_st();
+        }
+        // P buffer sb was last read by PV_{j-2}
+        if (j >= 2 && !wait_pv(j - 2)) break;
+  #pragma unroll
+        for (int plane = 0; plane < NT; ++plane)
+          *reinterpret_cast<uint4*>(&sm.p2[sb][plane][r * 16]) =
+              make_uint4(words[4 * plane], words[4 * plane + 1], words[4 * plane + 2], words[4 * plane + 3]);
+        if (!valid) {  // masked rows may hold any bytes (NaN codes): zero V's row
+          uint4* vrow = reinterpret_cast<uint4*>(&sm.v[stage][r * 128]);
+  #pragma unroll
+          for (int i = 0; i < 8; ++i) vrow[i] = make_uint4(0, 0, 0, 0);
+        }
+        fence_proxy_async_smem();
+        tc::fence_before_sync();
+        mbar_arrive(&sm.p_full[sb]);
+
+        // the previous item's read-out (its sums were exchanged at this tile's barrier)
+        if (pend_ep && !finish()) break;
+        if (flags & kLast) {
+          // park the item: per-warp row sums and the final maxima, read out one tile later
+          const int ob = (nitem - 1) & 1;
+  #pragma unroll
+          for (int q = 0; q < RV; ++q) {
+            float l = l_part[q];
+  #pragma unroll
+            for (int off = 16; off > 0; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
+            if (lane == 0) sm.redl[ob][warp][q] = l;
+            if (tid == 0) sm.mfin[ob][q] = m_ref[q];
+          }
+          pend_ep = true;
+          pend_j = j;
+          pend_ob = ob;
+          pend_slot = slot;
+          pend_item = item;
+          if constexpr (NT > 1) {  // wide row groups: read out at once (registers are scarce)
+            if (!sync() || !finish()) break;
+          }
+        }
+        ++j;
+        if (++stage == kStages) { stage = 0; phase ^= 1; }
       }
-      ++j;
-      if (++stage == kStages) { stage = 0; phase ^= 1; }
+      // the last item's read-out (a barrier first: every warp has parked its sums)
+      if (pend_ep && sync()) finish();
+  
+    } else {
+      // ============================================================ softmax, wide row groups
+      // NT > 1 (16 or 24 query rows per item): 8 warps.  Warp w owns token rows 32 (w & 3) .. + 31
+      // of S^T (and dim rows of O^T: its tensor-memory lane quadrant) and the query rows
+      // [h RH, (h + 1) RH) of the row group, h = w >> 2, so every thread handles RH = RV / 2 rows.
+      // The two halves never exchange anything: each has its own 128-thread barrier, its own
+      // rows' maxima, sums and read-out; they meet only on the tile barriers of the pipeline.
+      constexpr int RH = RV / 2;
+      static_assert(RH == 8 || RH == 12, "rows per half");
+      const int quad = warp & 3, half = warp >> 2;
+      const int qb = half * RH;  // this half's first row
+      const int r = tid & 127;
+      const uint32_t lane_base = static_cast<uint32_t>(32 * quad) << 16;
+      const bool kscaled = p.k_scale != nullptr;
+      const bool vscaled = p.v_scale != nullptr;
+      const int box_shift = 31 - __clz(p.box_rows);
+      constexpr float kRescaleLog2 = 4.f;  // P = 16 * 2^(s - m_ref) <= 256 < 448 (e4m3 max)
+      constexpr float kPScale = 16.f;
+      float m_ref[RH], l_part[RH];
+      int rows_i = 0, qrow_lo = 0, kvh = 0;
+      int stage = 0, j = 0, sync_uses = 0, item_first_tile = 0, nitem = 0;
+      uint32_t phase = 0;
+      int qcount[2] = {0, 0};
+      auto sync = [&]() -> bool {  // the 128 threads of this half
+        mbar_arrive(&sm.sync128[half]);
+        return mbar_wait(&sm.sync128[half], (sync_uses++) & 1, p.ctrl);
+      };
+      auto wait_pv = [&](int t) -> bool {
+        const int b = t & 1;
+        if (!mbar_wait(&sm.pv_done[b], (t >> 1) & 1, p.ctrl)) return false;
+        tc::fence_after_sync();
+        return true;
+      };
+      // RH consecutive tensor-memory columns of this thread's lane: one 8-column access (RH = 8,
+      // columns at multiples of 8) or three 4-column ones (RH = 12, columns at multiples of 4)
+      auto ld_rows = [&](uint32_t taddr, float (&v)[RH]) {
+        if constexpr (RH == 8) {
+          tc::ld8(taddr, v);
+        } else {
+#pragma unroll
+          for (int k = 0; k < RH / 4; ++k) {
+            float a[4];
+            tc::ld4(taddr + 4 * k, a);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) v[4 * k + i] = a[i];
+          }
+        }
+      };
+      auto st_rows = [&](uint32_t taddr, const float (&v)[RH]) {
+        if constexpr (RH == 8) {
+          tc::st8(taddr, v);
+        } else {
+#pragma unroll
+          for (int k = 0; k < RH / 4; ++k) {
+            const float a[4] = {v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]};
+            tc::st4(taddr + 4 * k, a);
+          }
+        }
+      };
+      const uint32_t o_base = tmem + lane_base + 2 * N;  // O of an item: o_base + (item parity) N
+      while (true) {
+        if (!mbar_wait(&sm.kv_full[stage], phase, p.ctrl)) break;
+        const int4 hw = *reinterpret_cast<const int4*>(&sm.hdr[stage][0]);
+        const int item = hw.x;
+        if (item < 0) break;
+        const int tok0 = hw.y, nvalid = hw.z, flags = hw.w & 15, slot = hw.w >> 4;
+        const int slot0 = sm.hdr[stage][kHdrSlot0 + (r >> box_shift)];
+        const bool valid = r < nvalid && slot0 >= 0;
+        if (flags & kFirst) {
+          if (!mbar_wait(&sm.q_full[slot], qcount[slot] & 1, p.ctrl)) break;
+          qcount[slot]++;
+          ++nitem;
+          item_first_tile = j;
+          kvh = sm.iinfo[slot].kvh;
+          rows_i = sm.iinfo[slot].rows;
+          qrow_lo = p.spec_mode ? sm.iinfo[slot].mbase * G + sm.iinfo[slot].rg * R : 0;
+#pragma unroll
+          for (int i = 0; i < RH; ++i) {
+            m_ref[i] = -INFINITY;
+            l_part[i] = 0.f;
+          }
+        }
+        float ks = 1.f, lv = 0.f;
+        if ((kscaled || vscaled) && valid) {
+          const int64_t idx = (static_cast<int64_t>(slot0) + (r & (p.box_rows - 1))) * p.num_kv_heads + kvh;
+          if (kscaled) ks = __ldg(p.k_scale + idx);
+          if (vscaled) lv = lg2(__ldg(p.v_scale + idx));
+        }
+        // ---------------------------------------------------- scores of this half's rows
+        const int sb = j & 1;
+        if (!mbar_wait(&sm.s_full[sb], (j >> 1) & 1, p.ctrl)) break;
+        tc::fence_after_sync();
+        float xs[RH];
+        {
+          float xh[RH], xl[RH];
+          ld_rows(tmem + lane_base + sb * N + qb, xh);
+          ld_rows(tmem + lane_base + sb * N + R + qb, xl);
+          tc::wait_ld();
+          tc::fence_before_sync();
+          mbar_arrive(&sm.s_empty[sb]);
+          const int pos = tok0 + r;
+          // rows [qmin, rows_i) see this thread's key position (all live rows outside spec mode)
+          const int qmin = !valid ? INT_MAX : (p.spec_mode ? pos * G - qrow_lo : INT_MIN);
+#pragma unroll
+          for (int i = 0; i < RH; i += 4) {
+            const float4 c4 = *reinterpret_cast<const float4*>(&sm.qscale[slot][qb + i]);
+            const float cs4[4] = {c4.x, c4.y, c4.z, c4.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const int q = qb + i + k;
+              float sc = (xh[i + k] + xl[i + k]) * cs4[k] * ks;
+              if (!(q >= qmin && q < rows_i)) sc = -INFINITY;
+              xs[i + k] = sc + lv;
+            }
+          }
+        }
+        bool over = false;  // a score the current reference cannot take (P would pass 256)
+#pragma unroll
+        for (int i = 0; i < RH; ++i) over |= xs[i] > m_ref[i] + kRescaleLog2;
+        // one vote per warp; this half's exact per-row maxima are exchanged only when one of its
+        // warps needs a new reference (an item's first tile, and rare growth after it)
+        const bool wover = __any_sync(0xffffffffu, over);
+        if (lane == 0) sm.vote[sb][warp] = wover ? 1 : 0;
+        if (!sync()) break;
+        const int4 votes = *reinterpret_cast<const int4*>(&sm.vote[sb][4 * half]);
+        uint32_t resc = 0;  // this half's rows whose reference moved (bit i: row qb + i)
+        if (votes.x | votes.y | votes.z | votes.w) {
+#pragma unroll
+          for (int i = 0; i < RH; ++i) {
+            const int wm = __reduce_max_sync(0xffffffffu, f2ord(xs[i]));
+            if (lane == 0) sm.red[sb][quad][qb + i] = ord2f(wm);
+          }
+          if (!sync()) break;
+#pragma unroll
+          for (int i = 0; i < RH; ++i) {
+            const int q = qb + i;
+            const float tmax = fmaxf(fmaxf(sm.red[sb][0][q], sm.red[sb][1][q]),
+                                     fmaxf(sm.red[sb][2][q], sm.red[sb][3][q]));
+            if (tmax > m_ref[i] + kRescaleLog2) {
+              const float a = m_ref[i] == -INFINITY ? 0.f : ex2(m_ref[i] - tmax);
+              m_ref[i] = tmax;
+              l_part[i] *= a;
+              resc |= 1u << i;
+              if (lane == 0) sm.alpha[quad][q] = a;
+            }
+          }
+        }
+        // ---------------------------------------------------- P and row sums
+#pragma unroll
+        for (int i = 0; i < RH; ++i) {
+          const float m_use = m_ref[i] == -INFINITY ? 0.f : m_ref[i];
+          const float pe = kPScale * ex2(xs[i] - m_use);
+          l_part[i] += vscaled ? kPScale * ex2(xs[i] - lv - m_use) : pe;
+          xs[i] = pe;
+        }
+        uint32_t whi[RH / 4], wlo[RH / 4];  // this half's hi and lo bytes of P^T row r
+#pragma unroll
+        for (int w = 0; w < RH / 4; ++w) {
+          const uint32_t a = pack_f16x2(xs[4 * w], xs[4 * w + 1]);
+          const uint32_t b = pack_f16x2(xs[4 * w + 2], xs[4 * w + 3]);
+          uint32_t ah, al, bh, bl;
+          split_f16x2_e4m3(a, ah, al);
+          split_f16x2_e4m3(b, bh, bl);
+          whi[w] = ah | (bh << 16);
+          wlo[w] = al | (bl << 16);
+        }
+        // O rescale (rare): O must be quiescent, i.e. the previous tile's PV done; this thread's
+        // dim row, this half's hi and lo columns
+        if (__any_sync(0xffffffffu, resc != 0) && j > item_first_tile) {
+          if (!wait_pv(j - 1)) break;
+          const uint32_t o_cur = o_base + ((nitem - 1) & 1) * N;
+#pragma unroll
+          for (int plane = 0; plane < 2; ++plane) {
+            float o[RH];
+            ld_rows(o_cur + plane * R + qb, o);
+            tc::wait_ld();
+#pragma unroll
+            for (int i = 0; i < RH; ++i)
+              if ((resc >> i) & 1u) o[i] *= sm.alpha[quad][qb + i];
+            st_rows(o_cur + plane * R + qb, o);
+          }
+          tc::wait_st();
+        }
+        // P buffer sb was last read by PV_{j-2}
+        if (j >= 2 && !wait_pv(j - 2)) break;
+#pragma unroll
+        for (int w = 0; w < RH / 4; ++w) {
+          const int bh = qb + 4 * w, bl = R + qb + 4 * w;  // byte offsets in the 2R-byte row
+          *reinterpret_cast<uint32_t*>(&sm.p2[sb][bh >> 4][r * 16 + (bh & 15)]) = whi[w];
+          *reinterpret_cast<uint32_t*>(&sm.p2[sb][bl >> 4][r * 16 + (bl & 15)]) = wlo[w];
+        }
+        if (!valid && half == 0) {  // masked rows may hold any bytes (NaN codes): zero V's row
+          uint4* vrow = reinterpret_cast<uint4*>(&sm.v[stage][r * 128]);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) vrow[i] = make_uint4(0, 0, 0, 0);
+        }
+        fence_proxy_async_smem();
+        tc::fence_before_sync();
+        mbar_arrive(&sm.p_full[sb]);
+
+        if (flags & kLast) {
+          // the item's read-out, at once: this half's row sums (per quadrant) and final maxima,
+          // a barrier, then its rows of O once the last PV is done
+          const int ob = (nitem - 1) & 1;
+#pragma unroll
+          for (int i = 0; i < RH; ++i) {
+            float l = l_part[i];
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
+            if (lane == 0) sm.redl[ob][quad][qb + i] = l;
+            if (r == 0) sm.mfin[ob][qb + i] = m_ref[i];
+          }
+          if (!sync() || !wait_pv(j)) break;
+          const ItemInfo ii = sm.iinfo[slot];
+          float oh[RH], ol[RH];
+          ld_rows(o_base + ob * N + qb, oh);
+          ld_rows(o_base + ob * N + R + qb, ol);
+          tc::wait_ld();
+          tc::fence_before_sync();
+          const int d = r;  // output dim
+#pragma unroll
+          for (int i = 0; i < RH; ++i) {
+            const int q = qb + i;
+            if (q >= ii.rows) break;
+            const float o = oh[i] + ol[i];
+            const float lsum = sm.redl[ob][0][q] + sm.redl[ob][1][q] + sm.redl[ob][2][q] +
+                               sm.redl[ob][3][q];
+            if (ii.nchunks == 1) {
+              const int rr = ii.rg * R + q;
+              const int jj = rr / G, hh = ii.kvh * G + (rr - jj * G);
+              __nv_bfloat16 v = out_round(o / fmaxf(lsum, 1e-10f));
+              p.out[static_cast<int64_t>(ii.qrow0 + jj) * p.out_row_stride + hh * kHeadDim + d] =
+                  *reinterpret_cast<uint16_t*>(&v);
+            } else {
+              float* part = p.partials + (static_cast<int64_t>(item) * R + q) * (kHeadDim + 4);
+              part[d] = o;
+              if (d == 0) {
+                // a chunk whose rows saw no key position carries no weight in the combine
+                part[kHeadDim] = lsum > 0.f ? sm.mfin[ob][q] : -INFINITY;
+                part[kHeadDim + 1] = lsum;
+              }
+            }
+          }
+          mbar_arrive(&sm.q_empty[slot]);
+        }
+        ++j;
+        if (++stage == kStages) { stage = 0; phase ^= 1; }
+      }
     }
-    // the last item's read-out (a barrier first: every warp has parked its sums)
-    if (pend_ep && sync()) finish();
   }
 
   // ---------------------------------------------------------------- teardown
@@ -1137,6 +1410,7 @@ int sm_count() {
 template <int NT>
 size_t decode_smem_bytes(int num_seqs, bool sampled) {
   // + alignment slack, + the per-launch plan arrays (prefix, info)
+  constexpr int kThreads = Roles<NT>::kThreads;
   const int plan_ints = sampled ? 2 * kThreads + 1
                                 : (NT > 1 && num_seqs <= kThreads ? 3 : 2) * num_seqs + 1;
   return sizeof(DecodeSmem<NT>) + 1024 + static_cast<size_t>(plan_ints) * sizeof(int);
@@ -1150,9 +1424,10 @@ struct DecodeShape {
   size_t smem;
 };
 
-// The launch of this batch: the per-sequence plan while two CTAs still fit on an SM with it,
-// else the sampled one; a persistent grid of as many CTAs as fit on every SM (at most
-// kMaxCtasPerSm; tensor memory per CTA is at most 256 columns, so it never limits).
+// The launch of this batch: the per-sequence plan while the engine's CTAs per SM (two for the
+// single-plane engines, one for the wide ones) still fit with it, else the sampled one; a
+// persistent grid of as many CTAs as fit on every SM (at most kMaxCtasPerSm; tensor memory per
+// CTA is at most 256 columns, so it never limits).
 template <int NT, int RV>
 DecodeShape decode_shape(int num_seqs) {
   static bool configured[64] = {false};
@@ -1176,7 +1451,7 @@ DecodeShape decode_shape(int num_seqs) {
   cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
   cudaDeviceGetAttribute(&resv, cudaDevAttrReservedSharedMemoryPerBlock, dev);
   const bool sampled = static_cast<int>(decode_smem_bytes<NT>(num_seqs, false)) + resv >
-                       smem_sm / kMaxCtasPerSm;
+                       smem_sm / (NT == 1 ? kMaxCtasPerSm : 1);
   DecodeShape sh;
   sh.fn = sampled ? decode_kernel<NT, RV, true> : decode_kernel<NT, RV, false>;
   sh.smem = decode_smem_bytes<NT>(num_seqs, sampled);
@@ -1184,7 +1459,7 @@ DecodeShape decode_shape(int num_seqs) {
   cudaFuncGetAttributes(&fa, sh.fn);
   const int per_cta_smem = static_cast<int>(sh.smem) + resv;
   int occ = per_cta_smem > 0 ? smem_sm / per_cta_smem : 1;
-  const int by_regs = fa.numRegs > 0 ? 65536 / (fa.numRegs * kThreads) : 1;
+  const int by_regs = fa.numRegs > 0 ? 65536 / (fa.numRegs * Roles<NT>::kThreads) : 1;
   occ = occ < by_regs ? occ : by_regs;
   occ = occ < 1 ? 1 : (occ > kMaxCtasPerSm ? kMaxCtasPerSm : occ);
   sh.grid = sm_count() * occ;
@@ -1230,7 +1505,7 @@ void launch_variant(const DecodeParams& p, const CUtensorMap& tmk, const CUtenso
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cudaLaunchConfig_t dcfg = {};
   dcfg.gridDim = dim3(sh.grid);
-  dcfg.blockDim = dim3(kThreads);
+  dcfg.blockDim = dim3(Roles<NT>::kThreads);
   dcfg.dynamicSmemBytes = sh.smem;
   dcfg.stream = stream;
   dcfg.attrs = attr;

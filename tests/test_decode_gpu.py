@@ -129,14 +129,15 @@ def test_decode_large_batches(bs, hq, kvh):
     _no_device_error()
 
 
-def test_decode_two_ctas_per_sm_at_every_batch_size():
-    """The persistent grid keeps two CTAs on every SM from 1 to 2048 sequences, for each engine
-    variant (decode GQA 4 and 8; spec verify of 4 and 5 query rows): the in-kernel plan switches
-    to per-range arrays before its shared memory would push the second CTA off."""
+def test_decode_ctas_per_sm_at_every_batch_size():
+    """The persistent grid keeps its CTAs on every SM from 1 to 2048 sequences, for each engine
+    variant: two per SM for the single-plane engines (decode GQA 4 and 8) -- the in-kernel plan
+    switches to per-range arrays before its shared memory would push the second CTA off -- and
+    one per SM for the wide spec-verify engines (4 and 5 query rows of GQA 4: 16 and 20 rows)."""
     sms = torch.cuda.get_device_properties(0).multi_processor_count
     for bs in [1, 256, 511, 512, 1000, 1919, 1920, 2048]:
-        for hq, kvh, mq in [(32, 8, 1), (64, 8, 1), (32, 8, 4), (32, 8, 5)]:
-            assert _lib().fp8attn_decode_ctas(bs, hq, kvh, mq) == 2 * sms, (bs, hq, kvh, mq)
+        for hq, kvh, mq, per_sm in [(32, 8, 1, 2), (64, 8, 1, 2), (32, 8, 4, 1), (32, 8, 5, 1)]:
+            assert _lib().fp8attn_decode_ctas(bs, hq, kvh, mq) == per_sm * sms, (bs, hq, kvh, mq)
 
 
 def test_decode_nan_bytes_beyond_context_are_ignored():
