@@ -306,7 +306,7 @@ def _maxdiff(a, b):
     return float((a.float() - b.float()).abs().max())
 
 
-PARTS = ("config2", "config1", "config3", "store", "config4")
+PARTS = ("config2", "config1", "config3", "store", "config4", "epilogue")
 
 
 def _store_sets(c, nsets, dev):
@@ -485,6 +485,56 @@ def secondary(dev, peaks, with_reference: bool, only=None):
                 max_seqlen_k=c.max_seqlen_k, softmax_scale=c.scale), m_ms, ours, iters=2,
                 warm=1)
         del c
+        torch.cuda.empty_cache()
+    # ---- the fused attention-input epilogue (q/k norm + rope + K/V store) on config 3's new rows
+    if "epilogue" in parts:
+        from nanovllm_b200.qk_epilogue import qk_norm_rope_store
+        c = workloads.config3(dev)
+        n, hq, kvh = c.q.shape[0], 32, 8
+        g = torch.Generator(device=dev).manual_seed(77)
+        qkvs = [torch.randn(n, (hq + 2 * kvh) * 128, generator=g, device=dev).to(torch.bfloat16)
+                for _ in range(8)]
+        qw = (torch.randn(128, generator=g, device=dev) * 0.2 + 1).to(torch.bfloat16)
+        kw = (torch.randn(128, generator=g, device=dev) * 0.2 + 1).to(torch.bfloat16)
+        pos = torch.randint(0, 40960, (n,), generator=g, device=dev)
+        inv_freq = 1.0 / (1000000.0 ** (torch.arange(0, 128, 2, dtype=torch.float) / 128))
+        freqs = torch.einsum("i,j -> ij", torch.arange(40960, dtype=torch.float), inv_freq)
+        cos_sin = torch.cat((freqs.cos(), freqs.sin()), dim=-1).unsqueeze_(1).to(dev)
+        caches = [(torch.empty_like(c.k), torch.empty_like(c.v)) for _ in range(8)]
+        ep_ms = _time_graph_calls(lambda: [qk_norm_rope_store(
+            x, pos, qw, kw, 1e-6, cos_sin, hq, kvh, kc, vc, c.slot_mapping)
+            for x, (kc, vc) in zip(qkvs, caches)], 8)
+        ep_bytes = n * ((hq + 2 * kvh) * 256 + hq * 256 + 2 * kvh * 128 + 8 + 4 + 512)
+        gbs = ep_bytes / (ep_ms * 1e-3) / 1e9
+        out["epilogue_config3"] = {
+            "workload": "q/k RMSNorm + RoPE + K/V e4m3 store of config 3's 5,561 new rows "
+                        "(Qwen3-8B heads), one kernel", "ms": ep_ms, "bytes": ep_bytes,
+            "timing": "CUDA graph of 8 back-to-back calls on 8 independent input sets, per call",
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s",
+                         "frac": gbs / hbm_peak}}
+        if ref is not None:
+            try:
+                from nanovllm.layers.layernorm import RMSNorm
+                from nanovllm.layers.rotary_embedding import get_rope
+                rope = get_rope(128, 128, 40960, 1000000.0).to(dev)
+                qn, kn = RMSNorm(128).to(dev), RMSNorm(128).to(dev)
+                with torch.no_grad():
+                    qn.weight.copy_(qw.float())
+                    kn.weight.copy_(kw.float())
+                qn, kn = qn.to(torch.bfloat16), kn.to(torch.bfloat16)
+
+                def ref_chain():
+                    with torch.no_grad():
+                        for x, (kc, vc) in zip(qkvs, caches):
+                            q, k, v = x.split([hq * 128, kvh * 128, kvh * 128], dim=-1)
+                            q3, k3 = rope(pos, qn(q.reshape(-1, hq, 128)),
+                                          kn(k.reshape(-1, kvh, 128)))
+                            ref["store"](k3, v.reshape(-1, kvh, 128), kc, vc, c.slot_mapping)
+                ref_chain()  # compiles the reference's functions outside the timing
+                ref_time("epilogue_config3", ref_chain, ep_ms, ncalls=8)
+            except Exception as e:  # pragma: no cover
+                refgpu["epilogue_config3"] = {"unavailable": f"{type(e).__name__}: {e}"}
+        del c, qkvs, caches
         torch.cuda.empty_cache()
     return out, refgpu
 

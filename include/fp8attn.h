@@ -70,6 +70,34 @@ FP8ATTN_API int fp8attn_store_kvcache(const void* key, int64_t key_row_stride, c
                           void* stream);
 
 /*
+ * Fused attention-input epilogue: q_norm / k_norm (RMSNorm over each head's 128 values), rotary
+ * embedding of q and k, and the K/V store of fp8attn_store_kvcache, in one kernel.  Replaces, for
+ * the q, k, v split of the QKV projection's output, the chain RMSNorm.rms_forward
+ * (nanovllm/layers/layernorm.py:16-26) -> RotaryEmbedding.forward
+ * (nanovllm/layers/rotary_embedding.py:37-47) -> store_kvcache (nanovllm/layers/attention.py:33-40)
+ * that Qwen3Attention.forward runs (nanovllm/models/qwen3.py:102-111).
+ * qkv: bf16 [num_tokens, row] (row = qkv_row_stride elements): num_heads q heads, then
+ *      num_kv_heads k heads, then num_kv_heads v heads, 128 values each.
+ * positions: int64 [num_tokens] (clamped to [0, max_position)); q_weight, k_weight: bf16 [128];
+ * cos_sin: fp32 [max_position, 128], per position the cos of the 64 rotary frequencies, then
+ *      their sin (the reference's cos_sin_cache).
+ * q_out: bf16 [num_tokens, num_heads, 128] (normalised, rotated q); k_out: the same for k
+ *      ([num_tokens, num_kv_heads, 128]) or NULL.
+ * Caches, scales, slot_mapping, num_slots and scaled as in fp8attn_store_kvcache: the rotated K and
+ * the raw V rows of tokens with a valid slot go to the caches.
+ * Arithmetic: r = rsqrt(sum(x^2)/128 + eps), n = bf16((x r) w), then the rotation of n in fp32
+ * rounded to bf16, then the e4m3 cast.
+ */
+FP8ATTN_API int fp8attn_qk_norm_rope_store(const void* qkv, int64_t qkv_row_stride,
+                               const int64_t* positions, const void* q_weight,
+                               const void* k_weight, float eps, const float* cos_sin,
+                               int64_t max_position, void* q_out, void* k_out, void* k_cache,
+                               void* v_cache, float* k_scale, float* v_scale,
+                               const int32_t* slot_mapping, int64_t num_tokens, int num_heads,
+                               int num_kv_heads, int head_dim, int64_t num_slots, int scaled,
+                               void* stream);
+
+/*
  * Workspace needed by fp8attn_decode (max_seqlen_q = 1) or fp8attn_prefill (its max_seqlen_q)
  * on the current device.  The workspace must be zero-filled before its first use; every call
  * leaves its counters at zero again.  One workspace must not be used by two calls that can run

@@ -279,6 +279,58 @@ static int launch_prefill_engine(void* out, const void* q, int64_t q_row_stride,
   return FP8ATTN_OK;
 }
 
+int fp8attn_qk_norm_rope_store(const void* qkv, int64_t qkv_row_stride, const int64_t* positions,
+                               const void* q_weight, const void* k_weight, float eps,
+                               const float* cos_sin, int64_t max_position, void* q_out, void* k_out,
+                               void* k_cache, void* v_cache, float* k_scale, float* v_scale,
+                               const int32_t* slot_mapping, int64_t num_tokens, int num_heads,
+                               int num_kv_heads, int head_dim, int64_t num_slots, int scaled,
+                               void* stream) {
+  if (head_dim != fp8attn::kHeadDim)
+    return fail(FP8ATTN_EINVAL, "head_dim must be 128 (got %d)", head_dim);
+  if (num_tokens < 0 || num_heads <= 0 || num_kv_heads <= 0 || num_slots < 0 || max_position <= 0)
+    return fail(FP8ATTN_EINVAL, "bad sizes");
+  if (num_tokens == 0) return FP8ATTN_OK;
+  if (!qkv || !positions || !q_weight || !k_weight || !cos_sin || !q_out || !k_cache ||
+      !v_cache || !slot_mapping)
+    return fail(FP8ATTN_EINVAL, "null pointer argument");
+  if ((reinterpret_cast<uintptr_t>(qkv) & 7) || qkv_row_stride % 4 != 0 ||
+      qkv_row_stride < static_cast<int64_t>(num_heads + 2 * num_kv_heads) * head_dim)
+    return fail(FP8ATTN_EINVAL, "qkv must be 8-byte aligned with rows of (Hq + 2 KVH) * 128");
+  if ((reinterpret_cast<uintptr_t>(q_out) & 7) || (k_out && (reinterpret_cast<uintptr_t>(k_out) & 7)) ||
+      (reinterpret_cast<uintptr_t>(q_weight) & 7) || (reinterpret_cast<uintptr_t>(k_weight) & 7) ||
+      (reinterpret_cast<uintptr_t>(cos_sin) & 15) || (reinterpret_cast<uintptr_t>(k_cache) & 3) ||
+      (reinterpret_cast<uintptr_t>(v_cache) & 3))
+    return fail(FP8ATTN_EINVAL, "misaligned pointer argument");
+  if ((k_scale == nullptr) != (v_scale == nullptr))
+    return fail(FP8ATTN_EINVAL, "k_scale and v_scale must both be given or both be null");
+  if (scaled && k_scale == nullptr) return fail(FP8ATTN_EINVAL, "scaled mode needs scale arrays");
+  fp8attn::QkNormParams p;
+  p.qkv = static_cast<const uint16_t*>(qkv);
+  p.qkv_row_stride = qkv_row_stride;
+  p.positions = positions;
+  p.q_weight = static_cast<const uint16_t*>(q_weight);
+  p.k_weight = static_cast<const uint16_t*>(k_weight);
+  p.cos_sin = cos_sin;
+  p.max_position = max_position;
+  p.eps = eps;
+  p.q_out = static_cast<uint16_t*>(q_out);
+  p.k_out = static_cast<uint16_t*>(k_out);
+  p.k_cache = static_cast<uint8_t*>(k_cache);
+  p.v_cache = static_cast<uint8_t*>(v_cache);
+  p.k_scale = k_scale;
+  p.v_scale = v_scale;
+  p.slot_mapping = slot_mapping;
+  p.num_tokens = num_tokens;
+  p.num_slots = num_slots;
+  p.num_heads = num_heads;
+  p.num_kv_heads = num_kv_heads;
+  p.scaled = scaled ? 1 : 0;
+  const cudaError_t e = fp8attn::launch_qk_norm_rope_store(p, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "q/k norm + rope + store launch");
+  return FP8ATTN_OK;
+}
+
 int fp8attn_read_error(const void* workspace, int32_t* dst, int clear, void* stream) {
   if (workspace == nullptr || dst == nullptr) return fail(FP8ATTN_EINVAL, "null pointer argument");
   const cudaStream_t st = static_cast<cudaStream_t>(stream);

@@ -25,6 +25,31 @@ struct StoreParams {
 };
 cudaError_t launch_store(const StoreParams& p, cudaStream_t stream);
 
+// ------------------------------------------------------------------ q/k norm + rope + store
+struct QkNormParams {
+  const uint16_t* qkv;  // bf16 [N, row stride]: q heads, k heads, v heads of 128 each
+  int64_t qkv_row_stride;  // elements
+  const int64_t* positions;  // [N], clamped to [0, max_position)
+  const uint16_t* q_weight;  // bf16 [128] (q_norm), [128] (k_norm)
+  const uint16_t* k_weight;
+  const float* cos_sin;  // fp32 [max_position, 128]: cos of the 64 frequencies, then sin
+  int64_t max_position;
+  float eps;
+  uint16_t* q_out;  // bf16 [N, Hq, 128]
+  uint16_t* k_out;  // bf16 [N, KVH, 128] or null
+  uint8_t* k_cache;  // e4m3 [num_slots, KVH, 128]
+  uint8_t* v_cache;
+  float* k_scale;  // fp32 [num_slots, KVH] or null
+  float* v_scale;
+  const int32_t* slot_mapping;  // [N]; -1 (or out of range): not stored
+  int64_t num_tokens;
+  int64_t num_slots;
+  int num_heads;
+  int num_kv_heads;
+  int scaled;
+};
+cudaError_t launch_qk_norm_rope_store(const QkNormParams& p, cudaStream_t stream);
+
 // ------------------------------------------------------------------ decode engine
 // Control block at the head of the decode workspace (ints):
 //   [0] sticky device error code, [1] next work item, [2] CTAs finished.

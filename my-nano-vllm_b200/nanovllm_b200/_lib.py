@@ -56,6 +56,9 @@ def _load() -> ctypes.CDLL:
     lib.fp8attn_diag_wait_timeout.argtypes = [vp, i64, i32, vp]
     lib.fp8attn_diag_exp2.restype = i32
     lib.fp8attn_diag_exp2.argtypes = [vp, vp, vp, i64, vp]
+    lib.fp8attn_qk_norm_rope_store.restype = i32
+    lib.fp8attn_qk_norm_rope_store.argtypes = [vp, i64, vp, vp, vp, f32, vp, i64, vp, vp, vp, vp,
+                                               vp, vp, vp, i64, i32, i32, i32, i64, i32, vp]
     lib.fp8attn_prefill.restype = i32
     lib.fp8attn_prefill.argtypes = [vp, vp, i64, vp, vp, i64, vp, vp, vp, i64, i32, vp, vp, i32,
                                     i32, i32, i32, i32, i32, i64, i32, f32, vp, i64, vp]

@@ -20,7 +20,7 @@ CSRC = os.path.join(ROOT, "csrc")
 INCLUDE = os.path.join(os.path.dirname(ROOT), "include")
 LIB_PATH = os.path.join(PKG_DIR, "libfp8attn.so")
 
-SOURCES = ["capi.cu", "store.cu", "decode.cu", "prefill.cu", "diag.cu"]
+SOURCES = ["capi.cu", "store.cu", "decode.cu", "prefill.cu", "diag.cu", "qknorm.cu"]
 HEADERS = ["common.cuh", "kernels.h", "tcgen05.cuh"]
 
 NVCC_FLAGS = [

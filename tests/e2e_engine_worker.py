@@ -8,7 +8,9 @@ MODE ``reference``: the engine's own Triton kernels; the sampled tokens and the 
 step are written to RECORD.pt.  MODE ``b200``: ``nanovllm_b200.patch.install()`` first, the tokens
 of RECORD.pt are replayed in place of sampling (teacher forcing, so both runs schedule the same
 batches: chunked prefill over a cached prefix, n-gram speculative verification, CUDA-graph decode)
-and the logits are written to RECORD.pt.b200.
+and the logits are written to RECORD.pt.b200.  MODE ``b200fused``: the same, and the fused q/k
+norm + rope + K/V store epilogue (``nanovllm_b200.qk_epilogue.install()``) in place of the model's
+norm, rotary and store steps; logits to RECORD.pt.b200fused.
 
 The sampler is replaced in both modes by an eager restatement of the reference's (temperature,
 softmax, exponential race; nanovllm/layers/sampler.py) so no compilation is needed.
@@ -31,15 +33,24 @@ def main(model_dir: str, mode: str, record: str) -> None:
     from nanovllm.layers import sampler as smp
 
     calls = {"store_kvcache": 0, "fp8_decode_attention": 0, "fp8_prefill_attention": 0}
-    if mode == "b200":
+    if mode in ("b200", "b200fused"):
         import nanovllm_b200.patch
         from nanovllm.layers import attention as att
         nanovllm_b200.patch.install()
-        for name in calls:  # count the engine's calls into the library (graph replays excluded)
+        for name in list(calls):  # count the engine's calls into the library (no graph replays)
             def counted(*args, _f=getattr(att, name), _n=name, **kw):
                 calls[_n] += 1
                 return _f(*args, **kw)
             setattr(att, name, counted)
+        if mode == "b200fused":  # also the fused q/k norm + rope + K/V store epilogue
+            from nanovllm_b200 import qk_epilogue
+            qk_epilogue.install()
+            calls["qk_norm_rope_store"] = 0
+
+            def counted_epilogue(*args, _f=qk_epilogue.qk_norm_rope_store, **kw):
+                calls["qk_norm_rope_store"] += 1
+                return _f(*args, **kw)
+            qk_epilogue.qk_norm_rope_store = counted_epilogue
         replay = list(torch.load(record)["tokens"])
     steps, tokens = [], []
     orig_run_model = mr.ModelRunner.run_model
@@ -50,7 +61,7 @@ def main(model_dir: str, mode: str, record: str) -> None:
         return logits
 
     def sample(self, logits, temperatures):
-        if mode == "b200":
+        if mode != "reference":
             return replay.pop(0).to(logits.device)
         probs = torch.softmax(logits.float().div(temperatures.unsqueeze(1)), dim=-1)
         out = probs.div(torch.empty_like(probs).exponential_(1).clamp_min_(1e-10)).argmax(dim=-1)
@@ -73,7 +84,7 @@ def main(model_dir: str, mode: str, record: str) -> None:
         torch.save({"tokens": tokens, "logits": steps}, record)
     else:
         assert not replay, f"{len(replay)} recorded samples were not consumed"
-        torch.save({"logits": steps, "calls": calls}, record + ".b200")
+        torch.save({"logits": steps, "calls": calls}, record + "." + mode)
     # the engine's own exit (registered with atexit) releases its graphs and process group
 
 

@@ -46,20 +46,7 @@ def _run(model_dir, mode, record):
     assert r.returncode == 0, f"{mode} run failed:\n{r.stdout[-3000:]}\n{r.stderr[-6000:]}"
 
 
-def test_generate_drop_in_matches_reference_logits(tmp_path):
-    if not os.path.isdir(os.path.join(REF, "nanovllm")):
-        pytest.skip("reference engine not installed under baseline/_ref")
-    model_dir = str(tmp_path / "qwen3-tiny")
-    _model_dir(model_dir)
-    record = str(tmp_path / "record.pt")
-    _run(model_dir, "reference", record)
-    _run(model_dir, "b200", record)
-    ref = torch.load(record)["logits"]
-    got = torch.load(record + ".b200")
-    ours, calls = got["logits"], got["calls"]
-    # every entry point served the engine: the store, decode (eager and at graph capture) and the
-    # paged prefill (chunked prefill over a cached prefix, speculative verification)
-    assert all(n > 0 for n in calls.values()), calls
+def _compare(ref, ours, what):
     assert len(ref) == len(ours) and len(ref) > 10
     worst, agree, rows = 0.0, 0, 0
     for a, b in zip(ref, ours):
@@ -71,7 +58,44 @@ def test_generate_drop_in_matches_reference_logits(tmp_path):
         rows += a.shape[0]
     # attention differences of ~1e-2 (the kernels' tolerance) move logits by a small fraction
     # of their range; the argmax almost never flips
-    print(f"e2e: {len(ref)} steps, {rows} logit rows, worst |dlogit|/max|logit| {worst:.4f}, "
-          f"argmax agreement {agree / rows:.4f}, library calls {calls}")
+    print(f"e2e {what}: {len(ref)} steps, {rows} logit rows, worst |dlogit|/max|logit| "
+          f"{worst:.4f}, argmax agreement {agree / rows:.4f}")
     assert worst < 0.05, worst
     assert agree / rows > 0.97, agree / rows
+
+
+@pytest.fixture(scope="module")
+def reference_run(tmp_path_factory):
+    if not os.path.isdir(os.path.join(REF, "nanovllm")):
+        pytest.skip("reference engine not installed under baseline/_ref")
+    tmp = tmp_path_factory.mktemp("e2e")
+    model_dir = str(tmp / "qwen3-tiny")
+    _model_dir(model_dir)
+    record = str(tmp / "record.pt")
+    _run(model_dir, "reference", record)
+    return model_dir, record
+
+
+def test_generate_drop_in_matches_reference_logits(reference_run):
+    model_dir, record = reference_run
+    _run(model_dir, "b200", record)
+    ref = torch.load(record)["logits"]
+    got = torch.load(record + ".b200")
+    # every entry point served the engine: the store, decode (eager and at graph capture) and the
+    # paged prefill (chunked prefill over a cached prefix, speculative verification)
+    assert all(n > 0 for n in got["calls"].values()), got["calls"]
+    _compare(ref, got["logits"], f"drop-in, library calls {got['calls']}")
+
+
+def test_generate_with_fused_epilogue_matches_reference_logits(reference_run):
+    """The same run with the fused q/k norm + rope + K/V store epilogue in Qwen3Attention: the
+    store entry point is then never called (the epilogue stores), the attention entry points
+    still are."""
+    model_dir, record = reference_run
+    _run(model_dir, "b200fused", record)
+    ref = torch.load(record)["logits"]
+    got = torch.load(record + ".b200fused")
+    calls = got["calls"]
+    assert calls["store_kvcache"] == 0 and calls["qk_norm_rope_store"] > 0, calls
+    assert calls["fp8_decode_attention"] > 0 and calls["fp8_prefill_attention"] > 0, calls
+    _compare(ref, got["logits"], f"fused epilogue, library calls {calls}")

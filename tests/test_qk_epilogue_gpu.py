@@ -1,0 +1,188 @@
+"""Fused q/k norm + rope + K/V store (fp8attn_qk_norm_rope_store) against the chain it replaces.
+
+* Bit-exact against the reference's own functions run on the same GPU from its unmodified install
+  under baseline/_ref: the compiled RMSNorm (nanovllm/layers/layernorm.py:16-26) on q and k, the
+  compiled RotaryEmbedding (nanovllm/layers/rotary_embedding.py:37-47) and the Triton
+  store_kvcache (nanovllm/layers/attention.py:11-40): q, k and every cache byte identical, over
+  several head geometries, strided qkv rows, slot -1 rows and positions across the table.
+* Against the CPU restatement (oracle/qknorm.py) on the same inputs: q and k nearly all identical
+  and otherwise within the bound one step of a normalised value allows (the restatement's sum of
+  squares and rsqrt are correctly rounded, the GPU's are not), cache bytes equal wherever the k
+  value is; the scaled cache format; no-cache calls.
+"""
+import os
+import sys
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import qknorm as oqk
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+REF = os.path.join(ROOT, "baseline", "_ref")
+
+
+def _inputs(n, hq, kvh, seed, sd=1.0, max_pos=40960, extra_cols=0, block_size=256):
+    g = torch.Generator().manual_seed(seed)
+    width = (hq + 2 * kvh) * 128
+    base = (torch.randn(n, width + extra_cols, generator=g) * sd).to(torch.bfloat16)
+    qkv = base[:, :width]                                   # rows extra_cols apart
+    qw = (torch.randn(128, generator=g) * 0.2 + 1).to(torch.bfloat16)
+    kw = (torch.randn(128, generator=g) * 0.2 + 1).to(torch.bfloat16)
+    pos = torch.randint(0, max_pos, (n,), generator=g)
+    nb = (n + block_size - 1) // block_size + 2
+    slots = torch.randperm(nb * block_size, generator=g)[:n].to(torch.int32)
+    slots[::13] = -1
+    return qkv, qw, kw, pos, slots, nb
+
+
+def _cos_sin(max_pos=40960, base=1000000.0):
+    # the reference's cache: inv_freq = 1 / base^(2i/128), freqs = t * inv_freq, [cos | sin] fp32
+    inv_freq = 1.0 / (base ** (torch.arange(0, 128, 2, dtype=torch.float) / 128))
+    t = torch.arange(max_pos, dtype=torch.float)
+    freqs = torch.einsum("i,j -> ij", t, inv_freq)
+    return torch.cat((freqs.cos(), freqs.sin()), dim=-1).unsqueeze_(1)
+
+
+def _ours(qkv, qw, kw, pos, slots, nb, hq, kvh, cos_sin, k_scale=None, v_scale=None,
+          scaled=False, block_size=256):
+    from nanovllm_b200.qk_epilogue import qk_norm_rope_store
+    kc = torch.full((nb, block_size, kvh, 128), 0x55, dtype=torch.uint8, device="cuda")
+    vc = torch.full_like(kc, 0x55)
+    x = torch.empty_strided(qkv.shape, qkv.stride(), dtype=qkv.dtype, device="cuda")
+    x.copy_(qkv)                                            # keeps the row stride on the device
+    q, k = qk_norm_rope_store(x, pos.cuda(), qw.cuda(), kw.cuda(), 1e-6, cos_sin.cuda(),
+                              hq, kvh, kc.view(torch.float8_e4m3fn), vc.view(torch.float8_e4m3fn),
+                              slots.cuda(), k_scale, v_scale, scaled=scaled, return_k=True)
+    torch.cuda.synchronize()
+    return q.cpu(), k.cpu(), kc.cpu().numpy(), vc.cpu().numpy()
+
+
+@pytest.fixture(scope="module")
+def ref():
+    if not os.path.isdir(os.path.join(REF, "nanovllm")):
+        pytest.skip("the reference is not installed under baseline/_ref")
+    if REF not in sys.path:
+        sys.path.insert(0, REF)
+    # the reference's RMSNorm and RoPE are torch.compile'd; compile them here, for these shapes,
+    # instead of reusing kernels (and launch configurations) another process left in the on-disk
+    # caches: the reduction order of the compiled RMSNorm follows its launch configuration
+    import torch._dynamo
+    import torch._inductor.config as inductor_config
+    inductor_config.fx_graph_cache = False
+    inductor_config.autotune_local_cache = False
+    torch._dynamo.reset()
+    from nanovllm.layers.attention import store_kvcache
+    from nanovllm.layers.layernorm import RMSNorm
+    from nanovllm.layers.rotary_embedding import get_rope
+    return RMSNorm, get_rope, store_kvcache
+
+
+@pytest.mark.parametrize("n,hq,kvh,sd,extra", [(300, 32, 8, 1.0, 0), (1500, 16, 4, 1.0, 8),
+                                               (777, 8, 2, 4.0, 0), (64, 64, 8, 0.3, 4),
+                                               (1, 32, 8, 1.0, 0)])
+def test_bit_exact_against_reference_chain(ref, n, hq, kvh, sd, extra):
+    RMSNorm, get_rope, store_kvcache = ref
+    torch._dynamo.reset()
+    qkv, qw, kw, pos, slots, nb = _inputs(n, hq, kvh, seed=n + hq, sd=sd, extra_cols=extra)
+    rope = get_rope(128, 128, 40960, 1000000.0).to("cuda")
+    qn, kn = RMSNorm(128).cuda(), RMSNorm(128).cuda()
+    with torch.no_grad():
+        qn.weight.copy_(qw.float())
+        kn.weight.copy_(kw.float())
+    qn, kn = qn.to(torch.bfloat16), kn.to(torch.bfloat16)
+    x = qkv.cuda()
+    q, k, v = x.split([hq * 128, kvh * 128, kvh * 128], dim=-1)
+    with torch.no_grad():
+        # run the compiled functions on another shape first, as the engine does (its calls after
+        # the first use the dynamic-shape kernels)
+        w = 3 if n > 3 else 2
+        rope(pos[:w].cuda(), qn(q[:w].reshape(-1, hq, 128)), kn(k[:w].reshape(-1, kvh, 128)))
+        q3, k3 = rope(pos.cuda(), qn(q.reshape(-1, hq, 128)), kn(k.reshape(-1, kvh, 128)))
+    kc = torch.full((nb, 256, kvh, 128), 0x55, dtype=torch.uint8, device="cuda")
+    vc = torch.full_like(kc, 0x55)
+    store_kvcache(k3, v.reshape(-1, kvh, 128), kc.view(torch.float8_e4m3fn),
+                  vc.view(torch.float8_e4m3fn), slots.cuda())
+    torch.cuda.synchronize()
+    oq, ok, okc, ovc = _ours(qkv, qw, kw, pos, slots, nb, hq, kvh, rope.cos_sin_cache.cpu())
+    for name, a, b in (("q", oq, q3.cpu()), ("k", ok, k3.cpu())):
+        bad = (a.view(torch.int16) != b.view(torch.int16)).nonzero()
+        assert bad.numel() == 0, (name, bad.shape[0], bad[:5].tolist(),
+                                  a[tuple(bad[0].tolist())].item(), b[tuple(bad[0].tolist())].item())
+    assert np.array_equal(okc, kc.cpu().numpy()) and np.array_equal(ovc, vc.cpu().numpy())
+
+
+def _close(a: torch.Tensor, b: torch.Tensor, what: str, min_exact=0.999):
+    """a, b: bf16 [N, H, 128].  The restatement's normalised values can differ from the GPU's by
+    one bf16 step (2^-8 relative); the rotation then moves an output by at most 2^-7 of its head's
+    largest value, plus its own rounding.  Nearly all outputs are identical."""
+    af, bf = a.float(), b.float()
+    bound = 2.0 ** -7 * bf.abs().amax(-1, keepdim=True) + 2.0 ** -8 * bf.abs()
+    err = (af - bf).abs()
+    assert bool((err <= bound).all()), f"{what}: max error {float(err.max()):.3e}"
+    exact = float((a.view(torch.int16) == b.view(torch.int16)).float().mean())
+    assert exact >= min_exact, f"{what}: only {exact:.5f} exact"
+
+
+@pytest.mark.parametrize("n,hq,kvh", [(513, 32, 8), (200, 8, 2)])
+def test_against_oracle(n, hq, kvh):
+    qkv, qw, kw, pos, slots, nb = _inputs(n, hq, kvh, seed=7 * n)
+    cs = _cos_sin()
+    oq, ok, okc, ovc = _ours(qkv, qw, kw, pos, slots, nb, hq, kvh, cs)
+    rkc = np.full((nb, 256, kvh, 128), 0x55, dtype=np.uint8)
+    rvc = rkc.copy()
+    rq, rk = oqk.qk_norm_rope_store(qkv, pos, qw, kw, 1e-6, cs, hq, kvh, rkc, rvc, slots.numpy())
+    _close(oq, rq, "q")
+    _close(ok, rk, "k")
+    assert np.array_equal(ovc, rvc)                       # v is stored unchanged in either
+    same_k = (ok.view(torch.int16) == rk.view(torch.int16)).numpy()
+    s = slots.numpy()
+    keep = s >= 0
+    got = okc.reshape(-1, kvh, 128)[s[keep]]
+    exp = rkc.reshape(-1, kvh, 128)[s[keep]]
+    assert np.array_equal(got[same_k[keep]], exp[same_k[keep]])
+
+
+def test_scaled_cache_and_no_cache_calls():
+    from nanovllm_b200.qk_epilogue import qk_norm_rope_store
+    n, hq, kvh = 260, 16, 4
+    qkv, qw, kw, pos, slots, nb = _inputs(n, hq, kvh, seed=99, sd=3.0)
+    cs = _cos_sin()
+    ks = torch.full((nb, 256, kvh), -7.0, device="cuda")
+    vs = torch.full((nb, 256, kvh), -7.0, device="cuda")
+    oq, ok, okc, ovc = _ours(qkv, qw, kw, pos, slots, nb, hq, kvh, cs, ks, vs, scaled=True)
+    # the scaled store of the same rotated k (and raw v) rows, restated on the CPU
+    from oracle import store as ostore
+    rkc = np.full((nb, 256, kvh, 128), 0x55, dtype=np.uint8)
+    rvc = rkc.copy()
+    rks = np.full((nb, 256, kvh), -7.0, dtype=np.float32)
+    rvs = rks.copy()
+    bits = lambda t: t.contiguous().view(torch.int16).numpy().view(np.uint16)
+    v = qkv[:, (hq + kvh) * 128:].reshape(n, kvh, 128)
+    ostore.store_kvcache(bits(ok), bits(v), rkc, rvc, slots.numpy(), rks, rvs, scaled=True)
+    assert np.array_equal(okc, rkc) and np.array_equal(ovc, rvc)
+    assert np.array_equal(ks.cpu().numpy(), rks) and np.array_equal(vs.cpu().numpy(), rvs)
+    # without caches (the engine's warm-up run) q and k are the same and nothing is stored
+    q2, k2 = qk_norm_rope_store(qkv.cuda(), pos.cuda(), qw.cuda(), kw.cuda(), 1e-6, cs.cuda(), hq,
+                                kvh, None, None, None, return_k=True)
+    torch.cuda.synchronize()
+    assert torch.equal(q2.cpu(), oq) and torch.equal(k2.cpu(), ok)
+
+
+def test_bit_exact_on_reference_fixture(golden):
+    """The same inputs as the committed fixture of the reference's own outputs
+    (tests/golden/make_golden_qk.py): q, k and cache bytes identical."""
+    g = golden("qk_epilogue")
+    from helpers import bf16
+    n = g["qkv"].shape[0]
+    hq, kvh = int(g["hq"]), int(g["kvh"])
+    nb, bs = g["k_cache"].shape[:2]
+    oq, ok, okc, ovc = _ours(bf16(g["qkv"]), bf16(g["q_weight"]), bf16(g["k_weight"]),
+                             torch.arange(n), torch.from_numpy(g["slots"]), nb, hq, kvh,
+                             torch.from_numpy(g["cos_sin_rows"]), block_size=bs)
+    assert np.array_equal(oq.view(torch.int16).numpy().view(np.uint16), g["q"])
+    assert np.array_equal(ok.view(torch.int16).numpy().view(np.uint16), g["k"])
+    assert np.array_equal(okc, g["k_cache"]) and np.array_equal(ovc, g["v_cache"])
