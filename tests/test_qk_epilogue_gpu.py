@@ -1,10 +1,12 @@
 """Fused q/k norm + rope + K/V store (fp8attn_qk_norm_rope_store) against the chain it replaces.
 
-* Bit-exact against the reference's own functions run on the same GPU from its unmodified install
-  under baseline/_ref: the compiled RMSNorm (nanovllm/layers/layernorm.py:16-26) on q and k, the
+* Against the reference's own functions run on the same GPU from its unmodified install under
+  baseline/_ref: the compiled RMSNorm (nanovllm/layers/layernorm.py:16-26) on q and k, the
   compiled RotaryEmbedding (nanovllm/layers/rotary_embedding.py:37-47) and the Triton
-  store_kvcache (nanovllm/layers/attention.py:11-40): q, k and every cache byte identical, over
-  several head geometries, strided qkv rows, slot -1 rows and positions across the table.
+  store_kvcache (nanovllm/layers/attention.py:11-40), over several head geometries, strided qkv
+  rows, slot -1 rows and positions across the table: identical bit for bit whenever the compiled
+  RMSNorm runs a one-warp-per-row launch configuration (see the test), and against the committed
+  fixture of the reference's outputs (tests/golden/make_golden_qk.py) identical in every value.
 * Against the CPU restatement (oracle/qknorm.py) on the same inputs: q and k nearly all identical
   and otherwise within the bound one step of a normalised value allows (the restatement's sum of
   squares and rsqrt are correctly rounded, the GPU's are not), cache bytes equal wherever the k
@@ -108,11 +110,23 @@ def test_bit_exact_against_reference_chain(ref, n, hq, kvh, sd, extra):
                   vc.view(torch.float8_e4m3fn), slots.cuda())
     torch.cuda.synchronize()
     oq, ok, okc, ovc = _ours(qkv, qw, kw, pos, slots, nb, hq, kvh, rope.cos_sin_cache.cpu())
+    # The compiled RMSNorm's sum of squares follows its launch configuration, which inductor's
+    # autotuner picks by timing among XBLOCK 1, 8 and 32: with 8 or 32 rows per program a warp
+    # sums one row as 4 values per lane, then lanes 16 -> 1, which is this kernel's order, and
+    # the outputs are identical bit for bit; with 1 row per program (two warps per row) the
+    # order differs and one value in ~10^6 moves by one rounding step.  So: identical up to that
+    # rate, and every other value within what one step of a normalised value allows.
     for name, a, b in (("q", oq, q3.cpu()), ("k", ok, k3.cpu())):
-        bad = (a.view(torch.int16) != b.view(torch.int16)).nonzero()
-        assert bad.numel() == 0, (name, bad.shape[0], bad[:5].tolist(),
-                                  a[tuple(bad[0].tolist())].item(), b[tuple(bad[0].tolist())].item())
-    assert np.array_equal(okc, kc.cpu().numpy()) and np.array_equal(ovc, vc.cpu().numpy())
+        differ = int((a.view(torch.int16) != b.view(torch.int16)).sum())
+        assert differ <= 1e-5 * a.numel(), (name, differ)
+        _close(a, b, name, min_exact=1.0 - 1e-5)
+    same_k = (ok.view(torch.int16) == k3.cpu().view(torch.int16)).numpy()
+    s = slots.numpy()
+    keep = s >= 0
+    assert np.array_equal(ovc, vc.cpu().numpy())
+    got = okc.reshape(-1, kvh, 128)[s[keep]]
+    exp = kc.cpu().numpy().reshape(-1, kvh, 128)[s[keep]]
+    assert np.array_equal(got[same_k[keep]], exp[same_k[keep]])
 
 
 def _close(a: torch.Tensor, b: torch.Tensor, what: str, min_exact=0.999):
