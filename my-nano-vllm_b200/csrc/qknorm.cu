@@ -55,6 +55,10 @@ __device__ __forceinline__ uint2 pack4(const float (&y)[4]) {
 // position, slot and cos/sin row and the task's rows are all loaded before any is used.
 template <int kRowsPerTask>
 __global__ void __launch_bounds__(kQkThreads) qk_norm_rope_store_kernel(const QkNormParams p) {
+  // launched as a programmatic dependent of the previous kernel (the QKV projection): nothing is
+  // read before it ends
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int64_t task = (static_cast<int64_t>(blockIdx.x) * kQkThreads + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   const int heads = p.num_heads + 2 * p.num_kv_heads;
@@ -167,11 +171,17 @@ cudaError_t launch_qk_norm_rope_store(const QkNormParams& p, cudaStream_t stream
   const int rows = small ? 4 : 8;
   const int64_t tasks = p.num_tokens * ((heads + rows - 1) / rows);
   const int64_t blocks = (tasks * 32 + kQkThreads - 1) / kQkThreads;
-  if (small)
-    qk_norm_rope_store_kernel<4><<<static_cast<unsigned>(blocks), kQkThreads, 0, stream>>>(p);
-  else
-    qk_norm_rope_store_kernel<8><<<static_cast<unsigned>(blocks), kQkThreads, 0, stream>>>(p);
-  return cudaGetLastError();
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(blocks));
+  cfg.blockDim = dim3(kQkThreads);
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (small) return cudaLaunchKernelEx(&cfg, qk_norm_rope_store_kernel<4>, p);
+  return cudaLaunchKernelEx(&cfg, qk_norm_rope_store_kernel<8>, p);
 }
 
 }  // namespace fp8attn

@@ -38,6 +38,10 @@ __device__ __forceinline__ void load_unit(const uint16_t* src, uint4& a, uint4& 
 template <bool kVec, int kU>
 __global__ void __launch_bounds__(kStoreThreads)
     store_kernel(const StoreParams p) {
+  // launched as a programmatic dependent of the previous kernel on the stream (the producer of
+  // key/value): the launch and the CTAs' start overlap its tail; nothing is read before it ends
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int kvh = p.num_kv_heads;
   const int chunks_per_row = kvh * 8;  // 16-element chunks per (token, K or V) row
   const int64_t units = p.num_tokens * 2 * chunks_per_row;
@@ -132,11 +136,18 @@ cudaError_t launch_store(const StoreParams& p, cudaStream_t stream) {
                    (p.key_row_stride % 8 == 0) && (p.value_row_stride % 8 == 0);
   constexpr int U = STORE_UNITS;
   const int64_t blocks = (units + U * kStoreThreads - 1) / (U * kStoreThreads);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(blocks));
+  cfg.blockDim = dim3(kStoreThreads);
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
   if (vec)
-    store_kernel<true, U><<<static_cast<unsigned>(blocks), kStoreThreads, 0, stream>>>(p);
-  else
-    store_kernel<false, U><<<static_cast<unsigned>(blocks), kStoreThreads, 0, stream>>>(p);
-  return cudaGetLastError();
+    return cudaLaunchKernelEx(&cfg, store_kernel<true, U>, p);
+  return cudaLaunchKernelEx(&cfg, store_kernel<false, U>, p);
 }
 
 }  // namespace fp8attn
