@@ -20,8 +20,9 @@ CSRC = os.path.join(ROOT, "csrc")
 INCLUDE = os.path.join(os.path.dirname(ROOT), "include")
 LIB_PATH = os.path.join(PKG_DIR, "libfp8attn.so")
 
-SOURCES = ["capi.cu", "store.cu", "decode.cu", "prefill.cu", "diag.cu", "qknorm.cu"]
-HEADERS = ["common.cuh", "kernels.h", "tcgen05.cuh"]
+SOURCES = ["capi.cu", "store.cu", "decode.cu", "prefill.cu", "prefill_persistent.cu", "diag.cu",
+           "qknorm.cu"]
+HEADERS = ["common.cuh", "kernels.h", "tcgen05.cuh", "prefill_common.cuh"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -217,3 +217,54 @@ def test_prefill_scaled_cache():
                    c.max_seqlen_k, c.scale, k_scale=ks, v_scale=vs)
     assert_close(out, _oracle(c, k_scale=ks.cpu(), v_scale=vs.cpu()), what="prefill scaled")
     _no_device_error()
+
+
+def test_prefill_mixed_batch_cuda_graph_replay():
+    """A mixed call (speculative-verify rows and chunked-prefill chunks in one paged prefill)
+    captured once in a CUDA graph and replayed on other batches of the same sequence count and
+    token count: the launches depend on neither the lengths nor max_seqlen_q beyond the cap the
+    caller passes (the prefill grid is persistent and plans its work items on the device, the
+    split-KV engine's width follows min(cap, spec limit)), so one graph serves every such batch."""
+    from nanovllm_b200 import fp8_prefill_attention, store_kvcache, workloads
+    cap = 512
+    batches = [([5, 5, 300, 5, 200, 5], [900, 1700, 0, 2500, 300, 3000]),
+               ([5, 310, 5, 5, 5, 190], [2100, 600, 4000, 10, 700, 0]),
+               ([260, 5, 5, 250, 0, 0], [0, 300, 800, 1200, 50, 0])]
+    cases = [workloads.prefill_case(nqs, pre, 32, 8, seed=61 + i, device="cuda", block_size=256,
+                                    pool_factor=1.2) for i, (nqs, pre) in enumerate(batches)]
+    width = max(c.block_tables.shape[1] for c in cases)
+    pool = max(c.k.shape[0] for c in cases)
+    static = {}
+    for c in cases:  # same cache pool, table width and buffers for every batch
+        bt = torch.full((6, width), -1, dtype=torch.int32, device="cuda")
+        bt[:, :c.block_tables.shape[1]] = c.block_tables
+        c.block_tables = bt
+        k = torch.zeros(pool, 256, 8, 128, dtype=torch.uint8, device="cuda").view(torch.float8_e4m3fn)
+        v = torch.zeros_like(k)
+        k[:c.k.shape[0]] = c.k
+        v[:c.v.shape[0]] = c.v
+        c.k, c.v = k, v
+        store_kvcache(c.new_k, c.new_v, c.k, c.v, c.slot_mapping)
+    assert len({c.q.shape[0] for c in cases}) == 1
+    for name in ("q", "k", "v", "block_tables", "cu_seqlens_q", "cu_seqlens_k"):
+        static[name] = getattr(cases[0], name).clone()
+
+    def call():
+        return fp8_prefill_attention(static["q"], static["k"], static["v"],
+                                     block_tables=static["block_tables"],
+                                     cu_seqlens_q=static["cu_seqlens_q"],
+                                     cu_seqlens_k=static["cu_seqlens_k"], max_seqlen_q=cap,
+                                     max_seqlen_k=8192, softmax_scale=cases[0].scale)
+
+    call()  # the workspace of this shape exists before capture
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        out = call()
+    for c in cases:
+        for name in static:
+            static[name].copy_(getattr(c, name))
+        graph.replay()
+        torch.cuda.synchronize()
+        assert_close(out, _oracle(c), what="mixed batch, graph replay")
+    _no_device_error()
