@@ -223,8 +223,9 @@ def test_prefill_mixed_batch_cuda_graph_replay():
     """A mixed call (speculative-verify rows and chunked-prefill chunks in one paged prefill)
     captured once in a CUDA graph and replayed on other batches of the same sequence count and
     token count: the launches depend on neither the lengths nor max_seqlen_q beyond the cap the
-    caller passes (the prefill grid is persistent and plans its work items on the device, the
-    split-KV engine's width follows min(cap, spec limit)), so one graph serves every such batch."""
+    caller passes (the prefill grid follows the sequence count and the cap, and its CTAs find
+    their work on the device; the split-KV engine's width follows min(cap, spec limit)), so one
+    graph serves every such batch."""
     from nanovllm_b200 import fp8_prefill_attention, store_kvcache, workloads
     cap = 512
     batches = [([5, 5, 300, 5, 200, 5], [900, 1700, 0, 2500, 300, 3000]),
