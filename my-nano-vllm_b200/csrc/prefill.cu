@@ -35,12 +35,14 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
     for (int i = 0; i < kStages; ++i) {
       mbar_init(&sm.kv_full[i], 1);
       mbar_init(&sm.kv_empty[i], 1 + Cfg::kGroupThreads * NG);  // MMA commit, softmax threads
+      mbar_init(&sm.vh_full[i], Cfg::kGroupThreads * NG);
     }
     for (int g = 0; g < NG; ++g) {
       mbar_init(&sm.q_full[g], Cfg::kGroupThreads);
       mbar_init(&sm.s_full[g], 1);
       mbar_init(&sm.p_full[g], Cfg::kGroupThreads);
       mbar_init(&sm.xch[g], Cfg::kGroupThreads);
+      for (int qd = 0; qd < 4; ++qd) mbar_init(&sm.xpair[g][qd], 64);
     }
     fence_mbar_init();
   }
@@ -133,23 +135,25 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
     // thread's MMAs in order.  The stage of tile j-1 is released after every group's PV.
     if (lane == 0 && ntiles > 0) {
       const uint32_t idesc_s = tc::idesc_e4m3(128, 128, false, false);
-      const uint32_t idesc_pv = tc::idesc_e4m3(128, 128, false, true);
+      const uint32_t idesc_pv = tc::idesc_f16(128, 128, false, true);
       bool ok = true;
       for (int g = 0; g < NG && ok; ++g) ok = mbar_wait(&sm.q_full[g], 0, p.err);
       int stage = 0, prev_stage = 0;
       uint32_t phase = 0;
+      // O_g += P_g . V over tile jt (stage st): kind::f16, K = 16 keys per MMA, P_g (f16 pairs)
+      // from S_g's columns, V as f16 (both groups converted their shares: vh_full)
       auto issue_pv = [&](int g, int jt, int st) -> bool {
         if (!mbar_wait(&sm.p_full[g], jt & 1, p.err)) return false;
+        if (g == 0 && !mbar_wait(&sm.vh_full[st], (jt / kStages) & 1, p.err)) return false;
         tc::fence_after_sync();
-        const uint32_t va = smem_u32(&sm.v[st][0]);
-        const uint32_t pt = tmem + 256 * g;  // P_g: 32-key step ks at p_col(32 ks), hi then lo
+        const uint32_t vb = smem_u32(&sm.vh[st][0]);
+        const uint32_t pt = tmem + 256 * g;
 #pragma unroll
-        for (int ks = 0; ks < 4; ++ks) {
-          const uint64_t bd = tc::smem_desc(va + ks * 32 * 128, 0, 1024, tc::kSw128);
-#pragma unroll
-          for (int plane = 0; plane < 2; ++plane)
-            tc::mma_f8_ts(tmem + 256 * g + 128, pt + p_col(32 * ks) + 8 * plane, bd, idesc_pv,
-                          (jt > 0 || ks > 0 || plane > 0) ? 1u : 0u);
+        for (int ks = 0; ks < kBN / 16; ++ks) {
+          // V rows 16 ks .. + 15: two 64-dim blocks kBN * 128 bytes apart, 8-row groups 1 KB apart
+          const uint64_t bd = tc::smem_desc(vb + ks * 16 * 128, kBN * 128, 1024, tc::kSw128);
+          tc::mma_f16_ts(tmem + 256 * g + 128, pt + p_col(16 * ks & ~31) + ((16 * ks) & 16) / 2, bd,
+                         idesc_pv, (jt > 0 || ks > 0) ? 1u : 0u);
         }
         return true;
       };
@@ -210,6 +214,15 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
       xphase ^= 1;
       return done;
     };
+    // the row's exchange: the two warps (column halves) of this row quadrant only
+    uint32_t pphase = 0;
+    uint64_t* const xpair = &sm.xpair[g][warp & 3];
+    auto pair_exchange = [&]() -> bool {
+      mbar_arrive(xpair);
+      const bool done = mbar_wait(xpair, pphase, p.err);
+      pphase ^= 1;
+      return done;
+    };
     // ---- query row -> e4m3 hi / lo, 128B-swizzled K-major rows (this half's dims)
     float cs;
     bool ok = true;
@@ -243,7 +256,7 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
       }
       if (kNH > 1) {
         sm.xq[g][half][r] = amax;
-        ok = exchange();
+        ok = pair_exchange();
         amax = fmaxf(sm.xq[g][0][r], sm.xq[g][1][r]);
       }
       float srow;
@@ -277,6 +290,33 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
       const uint32_t boxmask = sm.tile[stage].boxmask;  // boxes whose block is valid
       // key columns of this tile that can be valid at all (visible, inside this sequence)
       const int col_end = min(kBN, si.vis - j0);
+      // ---- this thread's share of the V tile -> f16 (the PV operand): key row r, dims
+      // cb + g * kConv .. + kConv - 1 (the groups split each half's 64 dims); keys outside the
+      // sequence or in masked blocks, whose bytes may be anything, become zeros
+      {
+        constexpr int kConv = 64 / NG;
+        const bool kv_ok = r < col_end && ((boxmask >> (r >> box_shift)) & 1u);
+        const uint8_t* vrow = &sm.v[stage][r * 128];
+        uint8_t* hrow = &sm.vh[stage][half * kBN * 128 + r * 128];
+#pragma unroll
+        for (int c = 0; c < kConv / 16; ++c) {
+          const int d = g * kConv + 16 * c;  // first dim of the chunk within the half
+          const uint4 x = kv_ok ? *reinterpret_cast<const uint4*>(vrow + ((((cb + d) >> 4) ^ (r & 7)) << 4))
+                                : make_uint4(0, 0, 0, 0);
+          const uint32_t w[4] = {x.x, x.y, x.z, x.w};
+          uint32_t hw[8];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            hw[2 * i] = e4m3x2_to_f16x2(w[i] & 0xFFFFu);
+            hw[2 * i + 1] = e4m3x2_to_f16x2(w[i] >> 16);
+          }
+          const int dc = d >> 3;  // 8-dim (16-byte) chunk of the f16 row
+          *reinterpret_cast<uint4*>(hrow + ((dc ^ (r & 7)) << 4)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+          *reinterpret_cast<uint4*>(hrow + (((dc + 1) ^ (r & 7)) << 4)) = make_uint4(hw[4], hw[5], hw[6], hw[7]);
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&sm.vh_full[stage]);
+      }
       // columns [0, vlim) of this tile are visible to this row.  A tile with a masked block, or
       // any tile of a scaled cache, takes the general path through the column table (uniform
       // across the group's four warps)
@@ -339,7 +379,7 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
       if (!general && tmax != -INFINITY) tmax *= cs;
       if (kNH > 1) {  // the row's other half (its S reads are done once it arrives)
         sm.xmax[g][half][r] = tmax;
-        if (!exchange()) { ok = false; break; }
+        if (!pair_exchange()) { ok = false; break; }
         tmax = fmaxf(sm.xmax[g][0][r], sm.xmax[g][1][r]);
       }
       // lazy rescale: move the reference max only when it grows by more than 2^4, so that
@@ -359,7 +399,7 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
         float v[32];
         tmem_ld32(s_tmem + c0, v);
         tc::wait_ld();
-        uint32_t pw[16];  // hi words 0..7, lo words 8..15 (four e4m3 each)
+        uint32_t pw[16];  // f16 pairs: keys c0 + 2i (low half) and c0 + 2i + 1
         if (!general) {
           // exponent arguments as packed pairs; every third pair (5 of the 16) takes a
           // polynomial on the FMA pipe, the others the MUFU ex2 (whose rate bounds this loop);
@@ -385,15 +425,7 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
               e1 = ex2(a1);
             }
             la[k & 3] = f2_add(la[k & 3], f2_pack(e0, e1));
-            uint32_t h2, l2;
-            split_f16x2_e4m3(pack_f16x2(e0, e1), h2, l2);
-            if (k & 1) {
-              pw[k >> 1] |= h2 << 16;
-              pw[8 + (k >> 1)] |= l2 << 16;
-            } else {
-              pw[k >> 1] = h2;
-              pw[8 + (k >> 1)] = l2;
-            }
+            pw[k] = pack_f16x2(e0, e1);
           }
           float s0, s1;
           f2_unpack(f2_add(f2_add(la[0], la[1]), f2_add(la[2], la[3])), s0, s1);
@@ -410,13 +442,7 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
           }
           l_tile += (la[0] + la[1]) + (la[2] + la[3]);
 #pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            uint32_t ah, al, bh, bl;
-            split_pos_f32x2_e4m3(v[4 * k], v[4 * k + 1], ah, al);
-            split_pos_f32x2_e4m3(v[4 * k + 2], v[4 * k + 3], bh, bl);
-            pw[k] = ah | (bh << 16);
-            pw[8 + k] = al | (bl << 16);
-          }
+          for (int k = 0; k < 16; ++k) pw[k] = pack_f16x2(v[2 * k], v[2 * k + 1]);
         }
         tc::st16u(s_tmem + p_col(c0), pw);
       }
@@ -433,18 +459,6 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
           tc::st16(o_tmem + c0, o16);
         }
       }
-      // V rows of keys outside the sequence (or in masked blocks) may hold any bytes: zero them
-      // (every group does, before its own PV; the bytes written are the same zeros)
-      {
-        const int kr = r;  // this thread also owns key row kr of the tile
-        const bool kv_ok = kr < col_end && ((boxmask >> (kr >> box_shift)) & 1u);
-        if (!kv_ok) {
-          uint4* vrow = reinterpret_cast<uint4*>(&sm.v[stage][kr * 128 + cb]);
-#pragma unroll
-          for (int i = 0; i < kCols / 16; ++i) vrow[i] = make_uint4(0, 0, 0, 0);
-        }
-      }
-      fence_proxy_async_smem();
       tc::wait_st();
       tc::fence_before_sync();
       mbar_arrive(&sm.p_full[g]);
@@ -453,7 +467,7 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
     // ---- epilogue: O / l -> fp16 -> bf16 (the reference's output path)
     if (ntiles > 0 && ok && kNH > 1) {  // the row sum over both halves
       sm.xl[g][half][r] = l;
-      ok = exchange();
+      ok = pair_exchange();
       l = sm.xl[g][0][r] + sm.xl[g][1][r];
     }
     if (row_ok) {

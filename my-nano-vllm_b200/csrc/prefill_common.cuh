@@ -82,6 +82,9 @@ struct __align__(1024) PrefillSmem {
   uint8_t qlo[NG][kBM * 128];
   uint8_t k[kStages][kBN * 128];        // TMA tiles, 128-byte rows, 128B swizzle
   uint8_t v[kStages][kBN * 128];
+  // the V tile as f16, the PV B operand (MN-major, 128B swizzle): two 64-dim halves of kBN key
+  // rows x 128 bytes (per-item kernel)
+  uint8_t vh[kStages][2 * kBN * 128];
   PrefillTile tile[kStages];
   // general-path column table of the group's current tile (thread r fills column r): key and
   // value scales, and a validity bit per column
@@ -89,6 +92,7 @@ struct __align__(1024) PrefillSmem {
   float colv[NG][kBN];
   uint32_t colok[NG][kBN / 32];
   uint64_t kv_full[kStages];
+  uint64_t vh_full[kStages];   // the stage's f16 V written (every softmax thread; per-item kernel)
   uint64_t kv_empty[kStages];  // K and V read by every group's MMAs (one commit), header by the
                                // softmax threads
   // per-row values the two column halves of a group exchange (q amax, tile max, row sum)
@@ -100,6 +104,7 @@ struct __align__(1024) PrefillSmem {
   uint64_t o_full[NG];         // an item's last PV_g done: O_g final
   uint64_t p_full[NG];         // P_g(j) in tensor memory, O_g rescaled, invalid V rows zeroed
   uint64_t xch[NG];            // the group's exchanges (all its softmax threads)
+  uint64_t xpair[NG][4];       // exchanges of one row quadrant's two column-half warps
   uint64_t o_free[NG];         // the group's read-out of an item's O is done
   uint32_t tmem_base;
   int scratch[32];
@@ -176,9 +181,9 @@ __host__ __device__ constexpr int box_rows_of(bool paged, int bs) {
   return paged ? (bs % 128 == 0 ? 128 : bs % 64 == 0 ? 64 : bs % 32 == 0 ? 32 : 16) : kBN;
 }
 
-// Tensor-memory column of the P words of the 32-key chunk at key column c0 (hi: 8 columns, then
-// lo: 8): inside the 64 S columns of the chunk's half, over the first 32, which that half has
-// already read when it writes P.
+// Tensor-memory column of the 16 P words of the 32-key chunk at key column c0 (f16 pairs in key
+// order, or e4m3 hi: 8 columns then lo: 8): inside the 64 S columns of the chunk's half, over the
+// first 32, which that half has already read when it writes P.
 __device__ __forceinline__ constexpr uint32_t p_col(int c0) {
   return static_cast<uint32_t>((c0 & ~63) + ((c0 & 63) >> 1));
 }

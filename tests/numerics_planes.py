@@ -1,9 +1,10 @@
 """Numerics of the tensor-core operand planes of the prefill engine (design check, CPU).
 
 q and P enter the e4m3 tensor-core products either as one e4m3 plane (4 significant bits) or as
-hi + lo planes (hi = e4m3(x), lo = e4m3(x - hi): about 8 bits).  This script emulates the four
-combinations on a benchmark configuration -- exact e4m3 casts of q (after the engine's per-row
-power-of-two scale) and of P = 16 2^(s - m), everything else in fp32, the output through fp16 to
+hi + lo planes (hi = e4m3(x), lo = e4m3(x - hi): about 8 bits); P can also enter an f16 product
+(11 bits) against V converted exactly to f16.  This script emulates these combinations on a
+benchmark configuration -- exact e4m3 casts of q (after the engine's per-row power-of-two scale)
+and e4m3 or f16 casts of P = 16 2^(s - m), everything else in fp32, the output through fp16 to
 bf16 as in the reference (nanovllm/kernels/fp8_attention.py:310-312) -- and prints the error
 against the fp32 reference with the tests' tolerance 2e-2 + 1e-2 |ref|.
 
@@ -28,6 +29,8 @@ def _e4(x):
 
 
 def _planes(x, n):
+    if n == "f16":
+        return x.to(torch.float16).float()
     hi = _e4(x)
     return hi + _e4(x - hi) if n == 2 else hi
 
@@ -67,7 +70,7 @@ def main(name: str) -> None:
     from nanovllm_b200 import workloads
     torch.set_num_threads(os.cpu_count() or 1)
     c = getattr(workloads, name)("cpu")
-    for qp, pp in ((2, 2), (1, 2), (2, 1), (1, 1)):
+    for qp, pp in ((2, "f16"), (2, 2), (1, 2), (2, 1), (1, 1)):
         t = time.time()
         mx, ratio, mean = run(c, qp, pp)
         print(f"{name}: q planes {qp}, P planes {pp}: max abs err {mx:.3e}, max err / tolerance "
