@@ -672,7 +672,7 @@ def run_ours(args, world, rank, local):
                    "max_gpu_step_ms": per_launch_max},
         "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": hbm_peak, "unit": "GB/s",
                      "frac": achieved_gbs / hbm_peak, "peak_kind": peaks[3],
-                     "kernel": "decode_kernel + combine_kernel (rank 0, per step)",
+                     "kernel": "decode_kernel + combine_rows_kernel (rank 0, per step)",
                      "traffic": (int(tr * step_bytes) if tr is not None else None)},
         "e2e": {"value": total_bytes / (e2e_ms / args.steps * 1e-3) / 1e12, "unit": "TB/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},

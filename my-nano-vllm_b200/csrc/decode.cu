@@ -11,7 +11,7 @@
 // sequence lengths (chunk size, item prefix sums in shared memory: per sequence, or for large
 // batches per range of sequences), then a persistent grid pulls items from an atomic counter.
 // An item whose (sequence, kv head, row group) has more than one chunk writes an unnormalised
-// partial (O, reference max, row sum); combine_kernel, launched after, merges them using the
+// partial (O, reference max, row sum); a combine kernel, launched after, merges them using the
 // plan CTA 0 publishes.
 //
 // Two CTAs per SM, eight warps each (warps 6-7 have no role; they balance the register file
@@ -1313,8 +1313,95 @@ __global__ void __launch_bounds__(Roles<NT>::kThreads, NT == 1 ? kMaxCtasPerSm :
 }
 
 // Combines the split-KV partials of every (sequence, kv head, row group) with more than one
-// chunk, using the plan the decode kernel published.  One CTA per pair (grid-strided); thread =
-// output dim.  Partial rows hold O (unnormalised, 128 floats), then the reference max (log2
+// chunk, using the plan the decode kernel published.  Single-plane engines (many chunks per
+// pair): one warp per (pair, row), grid-strided.
+// Partial rows hold O (unnormalised, 128 floats), then the reference max (log2 units) and the
+// row sum.  Lane c takes the (max, sum) of chunks c, c + 32, ...: the row's largest max M comes
+// from a warp reduction and chunk c's weight is 2^(m_c - M); lane l then accumulates output dims
+// 4l .. 4l + 3 over the chunks (one 16-byte load per chunk, all independent), so a pair costs
+// about two L2 round trips.  Launched as a programmatic dependent of the decode kernel: it waits
+// for the decode grid before touching the partials.
+constexpr int kCombineWarps = 8;
+template <int NT>
+__global__ void __launch_bounds__(32 * kCombineWarps)
+    combine_rows_kernel(const DecodeParams p) {
+  constexpr int R = 8 * NT;
+  // a following decode launch may start its setup now; it waits for this grid before any read
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // the decode grid has finished
+  const int G = p.group;
+  const int CT = p.plan[0];
+  const int lane = threadIdx.x & 31;
+  const int64_t nrows = static_cast<int64_t>(p.num_seqs) * p.num_kv_heads * p.max_rowgroups * R;
+  const int64_t w0 = static_cast<int64_t>(blockIdx.x) * kCombineWarps + (threadIdx.x >> 5);
+  const int64_t wstride = static_cast<int64_t>(gridDim.x) * kCombineWarps;
+  for (int64_t w = w0; w < nrows; w += wstride) {
+    const int64_t pi = w / R;
+    const int q = static_cast<int>(w - pi * R);
+    const int b = static_cast<int>(pi / (p.num_kv_heads * p.max_rowgroups));
+    const int rem = static_cast<int>(pi - static_cast<int64_t>(b) * p.num_kv_heads * p.max_rowgroups);
+    const int kvh = rem / p.max_rowgroups, rg = rem - kvh * p.max_rowgroups;
+    int nq;
+    const int L = seq_len_clamped(p, b, &nq);
+    if (L <= 0) continue;
+    const int nrg = (nq * G + R - 1) / R;
+    const int nchunks = (L + CT - 1) / CT;
+    if (rg >= nrg || nchunks <= 1 || q >= min(R, nq * G - rg * R)) continue;
+    const int qrow0 = p.spec_mode ? __ldg(p.cu_q + b) : b;
+    const int64_t first = p.plan[2 + b] + kvh * nrg + rg;
+    const int64_t stride = static_cast<int64_t>(p.num_kv_heads) * nrg;
+    auto part = [&](int c) -> const float* {
+      return p.partials + ((first + c * stride) * R + q) * (kHeadDim + 4);
+    };
+    // the row's largest reference max over its chunks (-inf: no chunk saw a key position)
+    float m_lane = -INFINITY;  // chunk `lane`'s max, kept for the common case of <= 32 chunks
+    float M = -INFINITY;
+    for (int c = lane; c < nchunks; c += 32) {
+      const float m = __ldcg(part(c) + kHeadDim);
+      if (c == lane) m_lane = m;
+      M = fmaxf(M, m);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+    float lsum = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int c0 = 0; c0 < nchunks; c0 += 32) {
+      const int c = c0 + lane;
+      float wl = 0.f;
+      if (c < nchunks) {
+        const float m = c0 == 0 ? m_lane : __ldcg(part(c) + kHeadDim);
+        wl = m == -INFINITY ? 0.f : ex2(m - M);
+        lsum += wl * __ldcg(part(c) + kHeadDim + 1);
+      }
+      const int n = min(32, nchunks - c0);
+#pragma unroll 4
+      for (int i = 0; i < n; ++i) {
+        const float wi = __shfl_sync(0xffffffffu, wl, i);
+        const float4 o = __ldcg(reinterpret_cast<const float4*>(part(c0 + i)) + lane);
+        acc.x += wi * o.x;
+        acc.y += wi * o.y;
+        acc.z += wi * o.z;
+        acc.w += wi * o.w;
+      }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, off);
+    const float inv = 1.f / fmaxf(lsum, 1e-10f);
+    const int rr = rg * R + q;
+    const int jj = rr / G, hh = kvh * G + (rr - jj * G);
+    const __nv_bfloat16 v0 = out_round(acc.x * inv), v1 = out_round(acc.y * inv);
+    const __nv_bfloat16 v2 = out_round(acc.z * inv), v3 = out_round(acc.w * inv);
+    // 2-byte stores: the output row stride carries no alignment guarantee beyond bf16
+    uint16_t* dst = p.out + static_cast<int64_t>(qrow0 + jj) * p.out_row_stride + hh * kHeadDim + 4 * lane;
+    dst[0] = *reinterpret_cast<const uint16_t*>(&v0);
+    dst[1] = *reinterpret_cast<const uint16_t*>(&v1);
+    dst[2] = *reinterpret_cast<const uint16_t*>(&v2);
+    dst[3] = *reinterpret_cast<const uint16_t*>(&v3);
+  }
+}
+
+// Wide engines' combine (few chunks per pair, many rows): one CTA per pair (grid-strided);
+// thread = output dim.  Partial rows hold O (unnormalised, 128 floats), then the reference max (log2
 // units) and the row sum.  Per pair: the (max, sum) of every (row, chunk) are gathered in parallel
 // (per-row maxima by shared-memory atomics on order-preserving ints), their weights computed once,
 // then each thread's partial-O loads are all independent.  Launched as a programmatic dependent
@@ -1322,7 +1409,7 @@ __global__ void __launch_bounds__(Roles<NT>::kThreads, NT == 1 ? kMaxCtasPerSm :
 constexpr int kCombineSlots = 1024;  // (row, chunk) weights staged per round
 template <int NT>
 __global__ void __launch_bounds__(kHeadDim)
-    combine_kernel(const DecodeParams p) {
+    combine_pairs_kernel(const DecodeParams p) {
   constexpr int R = 8 * NT;
   __shared__ int smax[R];
   __shared__ float ssum[R];
@@ -1516,7 +1603,7 @@ void launch_variant(const DecodeParams& p, const CUtensorMap& tmk, const CUtenso
     // each waits (griddepcontrol.wait) for the whole decode grid before reading the partials
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(cgrid);
-    cfg.blockDim = dim3(kHeadDim);
+    cfg.blockDim = dim3(NT == 1 ? 32 * kCombineWarps : kHeadDim);
     cfg.dynamicSmemBytes = 0;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
@@ -1524,7 +1611,8 @@ void launch_variant(const DecodeParams& p, const CUtensorMap& tmk, const CUtenso
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaLaunchKernelEx(&cfg, combine_kernel<NT>, p);
+    if constexpr (NT == 1) cudaLaunchKernelEx(&cfg, combine_rows_kernel<NT>, p);
+    else cudaLaunchKernelEx(&cfg, combine_pairs_kernel<NT>, p);
   }
 }
 }  // namespace
@@ -1532,7 +1620,11 @@ void launch_variant(const DecodeParams& p, const CUtensorMap& tmk, const CUtenso
 cudaError_t launch_decode(const DecodeParams& p, int nt, int rv, const CUtensorMap& tmk,
                           const CUtensorMap& tmv, cudaStream_t stream) {
   const int64_t pairs = static_cast<int64_t>(p.num_seqs) * p.num_kv_heads * p.max_rowgroups;
-  const int cgrid = static_cast<int>(pairs < 16LL * sm_count() ? pairs : 16LL * sm_count());
+  // combine CTAs, at most 16 per SM: single-plane engines one warp per (pair, row),
+  // kCombineWarps per CTA; wide engines one CTA per pair
+  const int64_t cblocks = nt == 1 ? (pairs * decode_rows(nt) + kCombineWarps - 1) / kCombineWarps
+                                  : pairs;
+  const int cgrid = static_cast<int>(cblocks < 16LL * sm_count() ? cblocks : 16LL * sm_count());
   switch (nt) {
     case 1:
       if (rv <= 4) launch_variant<1, 4>(p, tmk, tmv, cgrid, stream);
