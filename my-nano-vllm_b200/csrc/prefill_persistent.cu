@@ -150,6 +150,7 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
     for (int i = 0; i < kStages; ++i) {
       mbar_init(&sm.kv_full[i], 1);
       mbar_init(&sm.kv_empty[i], 1 + Cfg::kGroupThreads * NG);  // MMA commit, softmax threads
+      mbar_init(&sm.vh_full[i], Cfg::kGroupThreads * NG);
     }
     for (int g = 0; g < NG; ++g) {
       mbar_init(&sm.q_full[g], Cfg::kGroupThreads);
@@ -157,6 +158,7 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
       mbar_init(&sm.o_full[g], 1);
       mbar_init(&sm.p_full[g], Cfg::kGroupThreads);
       mbar_init(&sm.xch[g], Cfg::kGroupThreads);
+      for (int qd = 0; qd < 4; ++qd) mbar_init(&sm.xpair[g][qd], 64);
       mbar_init(&sm.o_free[g], Cfg::kGroupThreads);
     }
     fence_mbar_init();
@@ -307,31 +309,34 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
     // thread's MMAs in order.  A tile's stage is released after every group's PV of it.
     if (lane == 0) {
       const uint32_t idesc_s = tc::idesc_e4m3(128, 128, false, false);
-      const uint32_t idesc_pv = tc::idesc_e4m3(128, 128, false, true);
+      const uint32_t idesc_pv = tc::idesc_f16(128, 128, false, true);
       int stage = 0, prev_stage = 0;
-      uint32_t phase = 0;
+      uint32_t phase = 0, prev_phase = 0;
       int pv_count[NG];   // PVs issued per group (parity of p_full)
       int items_done = 0;  // items with key tiles whose O was started (parity of q_full / o_free)
       int q_items = 0;     // items whose q rows were loaded (parity of q_full)
 #pragma unroll
       for (int g = 0; g < NG; ++g) pv_count[g] = 0;
       bool ok = true;
-      auto issue_pv = [&](int g, int jt, int st) -> bool {
+      // O_g += P_g . V over tile jt of the item (stage st, filled in phase ph): kind::f16, K = 16
+      // keys per MMA, P_g (f16 pairs) from S_g's columns, V as f16 (both groups converted their
+      // shares: vh_full)
+      auto issue_pv = [&](int g, int jt, int st, uint32_t ph) -> bool {
         if (!mbar_wait(&sm.p_full[g], pv_count[g] & 1, p.err)) return false;
         // an item's first PV overwrites O: the previous item's read-out must be done
         if (jt == 0 && items_done > 0 && !mbar_wait(&sm.o_free[g], (items_done - 1) & 1, p.err))
           return false;
+        if (g == 0 && !mbar_wait(&sm.vh_full[st], ph, p.err)) return false;
         ++pv_count[g];
         tc::fence_after_sync();
-        const uint32_t va = smem_u32(&sm.v[st][0]);
-        const uint32_t pt = tmem + 256 * g;  // P_g: 32-key step ks at p_col(32 ks), hi then lo
+        const uint32_t vb = smem_u32(&sm.vh[st][0]);
+        const uint32_t pt = tmem + 256 * g;
 #pragma unroll
-        for (int ks = 0; ks < 4; ++ks) {
-          const uint64_t bd = tc::smem_desc(va + ks * 32 * 128, 0, 1024, tc::kSw128);
-#pragma unroll
-          for (int plane = 0; plane < 2; ++plane)
-            tc::mma_f8_ts(tmem + 256 * g + 128, pt + p_col(32 * ks) + 8 * plane, bd, idesc_pv,
-                          (jt > 0 || ks > 0 || plane > 0) ? 1u : 0u);
+        for (int ks = 0; ks < kBN / 16; ++ks) {
+          // V rows 16 ks .. + 15: two 64-dim blocks kBN * 128 bytes apart, 8-row groups 1 KB apart
+          const uint64_t bd = tc::smem_desc(vb + ks * 16 * 128, kBN * 128, 1024, tc::kSw128);
+          tc::mma_f16_ts(tmem + 256 * g + 128, pt + p_col(16 * ks & ~31) + ((16 * ks) & 16) / 2, bd,
+                         idesc_pv, (jt > 0 || ks > 0) ? 1u : 0u);
         }
         return true;
       };
@@ -354,7 +359,7 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
         }
         const uint32_t ka = smem_u32(&sm.k[stage][0]);
         for (int g = 0; g < NG && ok; ++g) {
-          if (j > 0 && !issue_pv(g, j - 1, prev_stage)) { ok = false; break; }
+          if (j > 0 && !issue_pv(g, j - 1, prev_stage, prev_phase)) { ok = false; break; }
           const uint32_t qh = smem_u32(&sm.qhi[g][0]), ql = smem_u32(&sm.qlo[g][0]);
 #pragma unroll
           for (int plane = 0; plane < 2; ++plane)
@@ -370,7 +375,7 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
         if (j > 0) tc::commit(&sm.kv_empty[prev_stage]);
         if (j == nt - 1) {  // the item's last PV, then its O is final
           for (int g = 0; g < NG && ok; ++g) {
-            ok = issue_pv(g, j, stage);
+            ok = issue_pv(g, j, stage, phase);
             if (ok) tc::commit(&sm.o_full[g]);
           }
           if (!ok) break;
@@ -378,6 +383,7 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
           ++items_done;
         }
         prev_stage = stage;
+        prev_phase = phase;
         if (++stage == kStages) { stage = 0; phase ^= 1; }
       }
     }
@@ -405,6 +411,15 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
       mbar_arrive(&sm.xch[g]);
       const bool done = mbar_wait(&sm.xch[g], xphase, p.err);
       xphase ^= 1;
+      return done;
+    };
+    // the row's exchange: the two warps (column halves) of this row quadrant only
+    uint32_t pphase = 0;
+    uint64_t* const xpair = &sm.xpair[g][warp & 3];
+    auto pair_exchange = [&]() -> bool {
+      mbar_arrive(xpair);
+      const bool done = mbar_wait(xpair, pphase, p.err);
+      pphase ^= 1;
       return done;
     };
     bool ok = true;
@@ -449,12 +464,40 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
           uint4* dst = reinterpret_cast<uint4*>(p.out + t.out_off + static_cast<int64_t>(r) * p.out_row_stride + g * 128 + cb);
           for (int i = 0; i < kCols / 8; ++i) dst[i] = make_uint4(0, 0, 0, 0);
         }
+        mbar_arrive(&sm.vh_full[stage]);  // keeps its phases in step with the stage's uses
         mbar_arrive(&sm.kv_empty[stage]);
         if (++stage == kStages) { stage = 0; phase ^= 1; }
         continue;
       }
       // key columns of this tile that can be valid at all (visible, inside this sequence)
       const int col_end = min(kBN, t.vis - j0);
+      // ---- this thread's share of the V tile -> f16 (the PV operand): key row r, dims
+      // cb + g * kConv .. + kConv - 1 (the groups split each half's 64 dims); keys outside the
+      // sequence or in masked blocks, whose bytes may be anything, become zeros
+      {
+        constexpr int kConv = 64 / NG;
+        const bool kv_ok = r < col_end && ((boxmask >> (r >> box_shift)) & 1u);
+        const uint8_t* vrow = &sm.v[stage][r * 128];
+        uint8_t* hrow = &sm.vh[stage][half * kBN * 128 + r * 128];
+#pragma unroll
+        for (int c = 0; c < kConv / 16; ++c) {
+          const int d = g * kConv + 16 * c;  // first dim of the chunk within the half
+          const uint4 x = kv_ok ? *reinterpret_cast<const uint4*>(vrow + ((((cb + d) >> 4) ^ (r & 7)) << 4))
+                                : make_uint4(0, 0, 0, 0);
+          const uint32_t w[4] = {x.x, x.y, x.z, x.w};
+          uint32_t hw[8];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            hw[2 * i] = e4m3x2_to_f16x2(w[i] & 0xFFFFu);
+            hw[2 * i + 1] = e4m3x2_to_f16x2(w[i] >> 16);
+          }
+          const int dc = d >> 3;  // 8-dim (16-byte) chunk of the f16 row
+          *reinterpret_cast<uint4*>(hrow + ((dc ^ (r & 7)) << 4)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+          *reinterpret_cast<uint4*>(hrow + (((dc + 1) ^ (r & 7)) << 4)) = make_uint4(hw[4], hw[5], hw[6], hw[7]);
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&sm.vh_full[stage]);
+      }
       // columns [0, vlim) of this tile are visible to this row.  A tile with a masked block, or
       // any tile of a scaled cache, takes the general path through the column table (uniform
       // across the group's warps)
@@ -521,7 +564,7 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
       if (!general && tmax != -INFINITY) tmax *= cs;
       if (kNH > 1) {  // the row's other half (its S reads are done once it arrives)
         sm.xmax[g][half][r] = tmax;
-        if (!exchange()) { ok = false; break; }
+        if (!pair_exchange()) { ok = false; break; }
         tmax = fmaxf(sm.xmax[g][0][r], sm.xmax[g][1][r]);
       }
       // lazy rescale: move the reference max only when it grows by more than 2^4, so that
@@ -541,7 +584,7 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
         float v[32];
         tmem_ld32(s_tmem + c0, v);
         tc::wait_ld();
-        uint32_t pw[16];  // hi words 0..7, lo words 8..15 (four e4m3 each)
+        uint32_t pw[16];  // f16 pairs: keys c0 + 2i (low half) and c0 + 2i + 1
         if (!general) {
           // exponent arguments as packed pairs; every third pair (5 of the 16) takes a
           // polynomial on the FMA pipe, the others the MUFU ex2 (whose rate bounds this loop);
@@ -567,15 +610,7 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
               e1 = ex2(a1);
             }
             la[k & 3] = f2_add(la[k & 3], f2_pack(e0, e1));
-            uint32_t h2, l2;
-            split_f16x2_e4m3(pack_f16x2(e0, e1), h2, l2);
-            if (k & 1) {
-              pw[k >> 1] |= h2 << 16;
-              pw[8 + (k >> 1)] |= l2 << 16;
-            } else {
-              pw[k >> 1] = h2;
-              pw[8 + (k >> 1)] = l2;
-            }
+            pw[k] = pack_f16x2(e0, e1);
           }
           float s0, s1;
           f2_unpack(f2_add(f2_add(la[0], la[1]), f2_add(la[2], la[3])), s0, s1);
@@ -592,13 +627,7 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
           }
           l_tile += (la[0] + la[1]) + (la[2] + la[3]);
 #pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            uint32_t ah, al, bh, bl;
-            split_pos_f32x2_e4m3(v[4 * k], v[4 * k + 1], ah, al);
-            split_pos_f32x2_e4m3(v[4 * k + 2], v[4 * k + 3], bh, bl);
-            pw[k] = ah | (bh << 16);
-            pw[8 + k] = al | (bl << 16);
-          }
+          for (int k = 0; k < 16; ++k) pw[k] = pack_f16x2(v[2 * k], v[2 * k + 1]);
         }
         tc::st16u(s_tmem + p_col(c0), pw);
       }
@@ -615,18 +644,6 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
           tc::st16(o_tmem + c0, o16);
         }
       }
-      // V rows of keys outside the sequence (or in masked blocks) may hold any bytes: zero them
-      // (every group does, before its own PV; the bytes written are the same zeros)
-      {
-        const int kr = r;  // this thread also owns key row kr of the tile
-        const bool kv_ok = kr < col_end && ((boxmask >> (kr >> box_shift)) & 1u);
-        if (!kv_ok) {
-          uint4* vrow = reinterpret_cast<uint4*>(&sm.v[stage][kr * 128 + cb]);
-#pragma unroll
-          for (int i = 0; i < kCols / 16; ++i) vrow[i] = make_uint4(0, 0, 0, 0);
-        }
-      }
-      fence_proxy_async_smem();
       tc::wait_st();
       tc::fence_before_sync();
       mbar_arrive(&sm.p_full[g]);
@@ -646,7 +663,7 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
       float lsum = l;
       if (kNH > 1) {  // the row sum over both halves
         sm.xl[g][half][r] = l;
-        if (!exchange()) { ok = false; break; }
+        if (!pair_exchange()) { ok = false; break; }
         lsum = sm.xl[g][0][r] + sm.xl[g][1][r];
       }
       if (!mbar_wait(&sm.o_full[g], o_waits & 1, p.err)) { ok = false; break; }  // O final
