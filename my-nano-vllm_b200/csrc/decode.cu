@@ -53,10 +53,11 @@ struct Roles {
   static constexpr int kSoftmaxWarps = NT == 1 ? 4 : 8;
   static constexpr int kProducerWarp = kSoftmaxWarps;
   static constexpr int kMmaWarp = kSoftmaxWarps + 1;
-  // single-plane engines: the PV products are issued by their own thread (warp 6), the S
-  // products by the MMA warp; wide engines: the MMA warp issues both
-  static constexpr int kPvWarp = NT == 1 ? kSoftmaxWarps + 2 : -1;
-  static constexpr int kWarps = NT == 1 ? 8 : 10;
+  // the PV products are issued by their own thread (warp 6 of the single-plane engines, warp 10
+  // of the wide ones), the S products by the MMA warp.  Wide engines: 11 warps put three on one
+  // scheduler, whose 16K registers then allow at most 168 per thread (the kernel uses 160)
+  static constexpr int kPvWarp = kSoftmaxWarps + 2;
+  static constexpr int kWarps = NT == 1 ? 8 : 11;
   static constexpr int kThreads = 32 * kWarps;
   static constexpr int kSoftmaxThreads = 32 * kSoftmaxWarps;
 };
@@ -726,53 +727,25 @@ __global__ void __launch_bounds__(Roles<NT>::kThreads, NT == 1 ? kMaxCtasPerSm :
     }
   } else if (fits && warp == kMmaWarp) {
     // ============================================================ MMA issuer (lane 0)
-    // tile j: S_j into S buffer j%2; on the wide engines then PV_{j-1} (or PV_j at once when j
-    // ends its item), accumulated into O (an item's first tile starts it afresh).  On the
-    // single-plane engines the PV products have their own issuing thread (warp 6): an MMA
-    // costs its issuing thread about 100 cycles, and these products are small (N = 16), so one
-    // thread issuing both paced the whole pipeline.  The two threads' products touch disjoint
-    // state (S buffers; P in shared memory and O), and each thread's commits track its own.
+    // tile j: S_j into S buffer j%2.  The PV products have their own issuing thread (kPvWarp):
+    // an MMA costs its issuing thread about 100 cycles and these products are small (N = 16 per
+    // plane), so one thread issuing both paced the tile loop.  The two threads' products touch
+    // disjoint state (S buffers; P in shared memory and O), and each thread's commits track its
+    // own products.
     if (lane == 0) {
       const uint32_t idesc_s = tc::idesc_e4m3(128, N, false, false);
-      const uint32_t idesc_pv = tc::idesc_e4m3(128, 16, true, true);
       int stage = 0, j = 0;
       uint32_t phase = 0;
       int qcount[2] = {0, 0};
-      bool pend = false;  // a tile whose PV is still to be issued
-      int pend_stage = 0, pend_first = 0, pend_ob = 0;
-      int items = 0;  // items started: O buffer of an item = its parity
-      auto issue_pv = [&](int st, int tile, int fresh, int ob) -> bool {
-        const int b = tile & 1;
-        if (!mbar_wait(&sm.p_full[b], (tile >> 1) & 1, p.ctrl)) return false;
-        tc::fence_after_sync();
-        const uint32_t va = smem_u32(&sm.v[st][0]);
-#pragma unroll
-        for (int plane = 0; plane < NT; ++plane) {
-          const uint32_t pa = smem_u32(&sm.p2[b][plane][0]);
-#pragma unroll
-          for (int ks = 0; ks < 4; ++ks) {
-            const uint64_t ad = tc::smem_desc(va + ks * 32 * 128, 0, 1024, tc::kSw128);
-            const uint64_t bd = tc::smem_desc(pa + ks * 32 * 16, 128, 2048, tc::kSwNone);
-            tc::mma_f8(tmem + (2 + ob) * N + 16 * plane, ad, bd, idesc_pv, (ks > 0 || !fresh) ? 1u : 0u);
-          }
-        }
-        tc::commit(&sm.kv_empty[st]);
-        tc::commit(&sm.pv_done[b]);
-        return true;
-      };
       while (true) {
         if (!mbar_wait(&sm.kv_full[stage], phase, p.ctrl)) break;
         if (sm.hdr[stage][kHdrItem] < 0) break;
         const int hflags = sm.hdr[stage][kHdrFlags];
-        const int first = hflags & kFirst;
-        const int last = hflags & kLast;
         const int slot = hflags >> 4;
-        if (first) {
+        if (hflags & kFirst) {
           if (!mbar_wait(&sm.q_full[slot], qcount[slot] & 1, p.ctrl)) break;
           qcount[slot]++;
-          ++items;
         }
-        const int ob = (items - 1) & 1;
         const int sb = j & 1;
         if (!mbar_wait(&sm.s_empty[sb], ((j >> 1) & 1) ^ 1, p.ctrl)) break;
         tc::fence_after_sync();
@@ -785,27 +758,15 @@ __global__ void __launch_bounds__(Roles<NT>::kThreads, NT == 1 ? kMaxCtasPerSm :
           tc::mma_f8(tmem + sb * N, ad, bd, idesc_s, ks > 0 ? 1u : 0u);
         }
         tc::commit(&sm.s_full[sb]);
-        if constexpr (NT > 1) {
-          if (pend && !issue_pv(pend_stage, j - 1, pend_first, pend_ob)) break;
-          pend = true;
-          pend_stage = stage;
-          pend_first = first;
-          pend_ob = ob;
-          if (last) {  // the item's epilogue waits on this PV: issue it now, not after the next S
-            if (!issue_pv(stage, j, first, ob)) break;
-            pend = false;
-          }
-        }
         ++j;
         if (++stage == kStages) { stage = 0; phase ^= 1; }
       }
-      if (pend) issue_pv(pend_stage, j - 1, pend_first, pend_ob);
     }
     __syncwarp();
   } else if (fits && warp == kPvWarp) {
     // ============================================================ PV issuer (lane 0)
-    // single-plane engines: PV_j as soon as P_j is written, accumulated into the O buffer of the
-    // item's parity (an item's first tile starts it afresh); its commit releases the stage
+    // PV_j as soon as P_j is written, accumulated into the O buffer of the item's parity (an
+    // item's first tile starts it afresh); its commit releases the stage
     if (lane == 0) {
       const uint32_t idesc_pv = tc::idesc_e4m3(128, 16, true, true);
       int stage = 0, j = 0;
