@@ -768,7 +768,9 @@ __global__ void __launch_bounds__(Roles<NT>::kThreads, NT == 1 ? kMaxCtasPerSm :
     // PV_j as soon as P_j is written, accumulated into the O buffer of the item's parity (an
     // item's first tile starts it afresh); its commit releases the stage
     if (lane == 0) {
-      const uint32_t idesc_pv = tc::idesc_e4m3(128, 16, true, true);
+      // P^T's NT planes of 16 columns lie 2 KB apart, the descriptor's stride between 16-column
+      // blocks (SBO): one MMA of N = 16 NT per 32-key step covers them all
+      const uint32_t idesc_pv = tc::idesc_e4m3(128, 16 * NT, true, true);
       int stage = 0, j = 0;
       uint32_t phase = 0;
       int items = 0;
@@ -782,15 +784,13 @@ __global__ void __launch_bounds__(Roles<NT>::kThreads, NT == 1 ? kMaxCtasPerSm :
         tc::fence_after_sync();
         const uint32_t va = smem_u32(&sm.v[stage][0]);
         const int ob = (items - 1) & 1;
+        const uint32_t pa = smem_u32(&sm.p2[b][0][0]);
+        static_assert(sizeof(sm.p2[0][0]) == 2048, "plane stride = SBO");
 #pragma unroll
-        for (int plane = 0; plane < NT; ++plane) {
-          const uint32_t pa = smem_u32(&sm.p2[b][plane][0]);
-#pragma unroll
-          for (int ks = 0; ks < 4; ++ks) {
-            const uint64_t ad = tc::smem_desc(va + ks * 32 * 128, 0, 1024, tc::kSw128);
-            const uint64_t bd = tc::smem_desc(pa + ks * 32 * 16, 128, 2048, tc::kSwNone);
-            tc::mma_f8(tmem + (2 + ob) * N + 16 * plane, ad, bd, idesc_pv, (ks > 0 || !first) ? 1u : 0u);
-          }
+        for (int ks = 0; ks < 4; ++ks) {
+          const uint64_t ad = tc::smem_desc(va + ks * 32 * 128, 0, 1024, tc::kSw128);
+          const uint64_t bd = tc::smem_desc(pa + ks * 32 * 16, 128, 2048, tc::kSwNone);
+          tc::mma_f8(tmem + (2 + ob) * N, ad, bd, idesc_pv, (ks > 0 || !first) ? 1u : 0u);
         }
         tc::commit(&sm.kv_empty[stage]);
         tc::commit(&sm.pv_done[b]);
