@@ -140,37 +140,45 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
       for (int g = 0; g < NG && ok; ++g) ok = mbar_wait(&sm.q_full[g], 0, p.err);
       int stage = 0, prev_stage = 0;
       uint32_t phase = 0;
+      // operand descriptors, built once: a K step moves an operand by a multiple of 16 bytes,
+      // i.e. adds to the start-address field (bits 0-13, address >> 4), which no operand here
+      // carries past its 14 bits
+      const uint64_t dk0 = tc::smem_desc(smem_u32(&sm.k[0][0]), 16, 1024, tc::kSw128);
+      const uint64_t dk1 = tc::smem_desc(smem_u32(&sm.k[kStages - 1][0]), 16, 1024, tc::kSw128);
+      const uint64_t dv0 = tc::smem_desc(smem_u32(&sm.vh[0][0]), kBN * 128, 1024, tc::kSw128);
+      const uint64_t dv1 = tc::smem_desc(smem_u32(&sm.vh[kStages - 1][0]), kBN * 128, 1024, tc::kSw128);
+      static_assert(kStages == 2, "two descriptor bases per ring");
       // O_g += P_g . V over tile jt (stage st): kind::f16, K = 16 keys per MMA, P_g (f16 pairs)
       // from S_g's columns, V as f16 (both groups converted their shares: vh_full)
       auto issue_pv = [&](int g, int jt, int st) -> bool {
         if (!mbar_wait(&sm.p_full[g], jt & 1, p.err)) return false;
         if (g == 0 && !mbar_wait(&sm.vh_full[st], (jt / kStages) & 1, p.err)) return false;
         tc::fence_after_sync();
-        const uint32_t vb = smem_u32(&sm.vh[st][0]);
+        const uint64_t dv = st ? dv1 : dv0;
         const uint32_t pt = tmem + 256 * g;
 #pragma unroll
         for (int ks = 0; ks < kBN / 16; ++ks) {
-          // V rows 16 ks .. + 15: two 64-dim blocks kBN * 128 bytes apart, 8-row groups 1 KB apart
-          const uint64_t bd = tc::smem_desc(vb + ks * 16 * 128, kBN * 128, 1024, tc::kSw128);
-          tc::mma_f16_ts(tmem + 256 * g + 128, pt + p_col(16 * ks & ~31) + ((16 * ks) & 16) / 2, bd,
-                         idesc_pv, (jt > 0 || ks > 0) ? 1u : 0u);
+          // V rows 16 ks .. + 15 (2 KB further per step): two 64-dim blocks kBN * 128 bytes
+          // apart, 8-row groups 1 KB apart
+          tc::mma_f16_ts(tmem + 256 * g + 128, pt + p_col(16 * ks & ~31) + ((16 * ks) & 16) / 2,
+                         dv + static_cast<uint64_t>(ks * (16 * 128 >> 4)), idesc_pv,
+                         (jt > 0 || ks > 0) ? 1u : 0u);
         }
         return true;
       };
       for (int j = 0; ok && j < ntiles; ++j) {
-        const uint32_t ka = smem_u32(&sm.k[stage][0]);
+        const uint64_t dk = stage ? dk1 : dk0;
         for (int g = 0; g < NG && ok; ++g) {
           if (j > 0 && !issue_pv(g, j - 1, prev_stage)) { ok = false; break; }
           if (g == 0 && !mbar_wait(&sm.kv_full[stage], phase, p.err)) { ok = false; break; }
-          const uint32_t qh = smem_u32(&sm.qhi[g][0]), ql = smem_u32(&sm.qlo[g][0]);
+          const uint64_t dqh = tc::smem_desc(smem_u32(&sm.qhi[g][0]), 16, 1024, tc::kSw128);
+          const uint64_t dql = tc::smem_desc(smem_u32(&sm.qlo[g][0]), 16, 1024, tc::kSw128);
 #pragma unroll
           for (int plane = 0; plane < 2; ++plane)
 #pragma unroll
-            for (int ks = 0; ks < 4; ++ks) {
-              const uint64_t ad = tc::smem_desc((plane ? ql : qh) + ks * 32, 16, 1024, tc::kSw128);
-              const uint64_t bd = tc::smem_desc(ka + ks * 32, 16, 1024, tc::kSw128);
-              tc::mma_f8(tmem + 256 * g, ad, bd, idesc_s, (plane > 0 || ks > 0) ? 1u : 0u);
-            }
+            for (int ks = 0; ks < 4; ++ks)  // 32 bytes further per step
+              tc::mma_f8(tmem + 256 * g, (plane ? dql : dqh) + static_cast<uint64_t>(2 * ks),
+                         dk + static_cast<uint64_t>(2 * ks), idesc_s, (plane > 0 || ks > 0) ? 1u : 0u);
           tc::commit(&sm.s_full[g]);
         }
         if (!ok) break;
