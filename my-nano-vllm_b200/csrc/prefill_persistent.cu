@@ -198,10 +198,10 @@ __global__ void __launch_bounds__(PrefillCfg<NG>::kThreads, 1)
     const int nbox = kBN / box_rows;
     int stage = 0;
     uint32_t phase = 0;
-    // The next item is claimed while the last tile of this one waits for its stage, so it is
-    // claimed only a ring's depth before this CTA's consumers run dry: claiming a whole item
-    // ahead would let a busy CTA hold a long item that an idle one could run (a tail of up to one
-    // item on batches of few long items).
+    // The next item is claimed two tiles before this one's last (its seq lookup and first block
+    // table loads then overlap the last tiles), i.e. a few tiles before this CTA's consumers run
+    // dry: claiming a whole item ahead would let a busy CTA hold a long item that an idle one
+    // could run (a tail of up to one item on batches of few long items).
     int next = lane == 0 ? atomicAdd(p.err + 1, 1) : 0;
     while (true) {
       const int item = __shfl_sync(0xffffffffu, next, 0);
