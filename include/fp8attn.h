@@ -196,6 +196,39 @@ FP8ATTN_API int fp8attn_read_error(const void* workspace, int32_t* dst, int clea
 FP8ATTN_API int fp8attn_set_decode_min_chunk(int tokens);
 
 /*
+ * FP8 block-scaled linear layer (replaces fp8_block_linear, nanovllm/kernels/fp8_linear.py:93-139,
+ * called by nanovllm/layers/linear.py:58 for checkpoints quantised in 128 x 128 weight blocks).
+ * Types: x and out bf16, xq and w e4m3 (one byte), x_scale and w_scale bf16.  Shapes: x [M, K],
+ * w [N, K] (contiguous), w_scale [N / 128, K / 128] (contiguous), out [M, N]; N and K positive
+ * multiples of 128, M >= 0 (M = 0 is a no-op).  Row strides are in elements of each tensor.
+ *   fp8attn_fp8_dyn_quant (fp8_dyn_quant_kernel, :11-31): per token m and 128-column group g,
+ *     s = max|x[m, g]| / 448 (1 for an all-zero group), xq = e4m3(clamp(x / s, -448, 448)),
+ *     x_scale[m, g] = bf16(s).  xq [M, K] (row stride a multiple of 4), x_scale [M, K / 128]
+ *     (contiguous).  x 16-byte aligned, its row stride a multiple of 8.
+ *   fp8attn_fp8_block_gemm (fp8_block_gemm_kernel, :34-71): out[m, n] = bf16(sum over groups g,
+ *     in order, of (xq[m, g] . w[n, g]) * (x_scale[m, g] * w_scale[n / 128, g])), each group's
+ *     dot exact (fp32 tensor-core accumulation of e4m3 products) and the sum kept in fp32.
+ *     xq and w 16-byte aligned, xq's row stride a multiple of 16.  workspace: at least
+ *     fp8attn_fp8_gemm_workspace_bytes(M, N, K) bytes, 16-byte aligned; its first int32 is the
+ *     device error word (fp8attn_read_error reads it), the rest holds split-K partial sums.
+ *   fp8attn_fp8_block_linear: both, with xq and x_scale placed in the workspace after the GEMM's
+ *     part; workspace of fp8attn_fp8_linear_workspace_bytes(M, N, K) bytes.
+ * The workspace sizes depend on the current device's SM count (split-K ranges); they return -1
+ * for invalid sizes.  Errors: FP8ATTN_EINVAL for shapes, strides, alignment and null pointers,
+ * FP8ATTN_EWORKSPACE for a missing or small workspace.  Launches are asynchronous on `stream`.
+ */
+FP8ATTN_API int64_t fp8attn_fp8_gemm_workspace_bytes(int64_t M, int N, int K);
+FP8ATTN_API int64_t fp8attn_fp8_linear_workspace_bytes(int64_t M, int N, int K);
+FP8ATTN_API int fp8attn_fp8_dyn_quant(const void* x, int64_t x_row_stride, void* xq,
+                   int64_t xq_row_stride, void* x_scale, int64_t M, int K, void* stream);
+FP8ATTN_API int fp8attn_fp8_block_gemm(const void* xq, int64_t xq_row_stride, const void* x_scale,
+                   const void* w, const void* w_scale, void* out, int64_t out_row_stride,
+                   int64_t M, int N, int K, void* workspace, int64_t workspace_bytes, void* stream);
+FP8ATTN_API int fp8attn_fp8_block_linear(const void* x, int64_t x_row_stride, const void* w,
+                   const void* w_scale, void* out, int64_t out_row_stride, int64_t M, int N, int K,
+                   void* workspace, int64_t workspace_bytes, void* stream);
+
+/*
  * Self-checks of device-side mechanisms (no counterpart in the reference; used by the tests).
  *   fp8attn_diag_wait_timeout: num_ctas CTAs each claim one work item from the control block at
  *     `workspace` (ints: [0] error word, [1] next item, [2] CTAs finished, zeroed by the caller)

@@ -539,3 +539,150 @@ int fp8attn_noalloc_read_error(int32_t* dst, int clear, void* stream) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------- FP8 block-scaled linear
+namespace {
+
+int64_t round16(int64_t v) { return (v + 15) & ~int64_t{15}; }
+
+int device_sms() {
+  static int sms[kMaxDevices] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 148;
+  if (sms[dev] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    sms[dev] = n > 0 ? n : 148;
+  }
+  return sms[dev];
+}
+
+bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+int check_linear_sizes(int64_t M, int N, int K) {
+  if (M < 0 || N <= 0 || K <= 0 || N % 128 != 0 || K % 128 != 0)
+    return fail(FP8ATTN_EINVAL, "fp8 linear needs M >= 0 and N, K positive multiples of 128 "
+                "(got M=%lld N=%d K=%d)", static_cast<long long>(M), N, K);
+  if ((M + fp8attn::kFp8GemmTokens - 1) / fp8attn::kFp8GemmTokens > 65535)
+    return fail(FP8ATTN_EINVAL, "fp8 linear: M=%lld exceeds %d rows", static_cast<long long>(M),
+                65535 * fp8attn::kFp8GemmTokens);
+  return FP8ATTN_OK;
+}
+
+int run_quant(const void* x, int64_t x_row_stride, void* xq, int64_t xq_row_stride,
+              void* x_scale, int64_t M, int K, cudaStream_t st) {
+  if (M == 0) return FP8ATTN_OK;
+  if (x == nullptr || xq == nullptr || x_scale == nullptr)
+    return fail(FP8ATTN_EINVAL, "fp8 quant: null pointer argument");
+  if (!aligned(x, 16) || x_row_stride < K || x_row_stride % 8 != 0)
+    return fail(FP8ATTN_EINVAL, "fp8 quant: x must be 16-byte aligned with a row stride >= K "
+                "that is a multiple of 8 elements");
+  if (!aligned(xq, 4) || xq_row_stride < K || xq_row_stride % 4 != 0)
+    return fail(FP8ATTN_EINVAL, "fp8 quant: xq must be 4-byte aligned with a row stride >= K "
+                "that is a multiple of 4 bytes");
+  if (!aligned(x_scale, 2)) return fail(FP8ATTN_EINVAL, "fp8 quant: x_scale must be 2-byte aligned");
+  fp8attn::Fp8QuantParams p;
+  p.x = static_cast<const uint16_t*>(x);
+  p.x_row_stride = x_row_stride;
+  p.xq = static_cast<uint8_t*>(xq);
+  p.xq_row_stride = xq_row_stride;
+  p.x_scale = static_cast<uint16_t*>(x_scale);
+  p.M = M;
+  p.K = K;
+  const cudaError_t e = fp8attn::launch_fp8_dyn_quant(p, st);
+  return e == cudaSuccess ? FP8ATTN_OK : cuda_fail(e, "fp8 quant launch");
+}
+
+int run_gemm(const void* xq, int64_t xq_row_stride, const void* x_scale, const void* w,
+             const void* w_scale, void* out, int64_t out_row_stride, int64_t M, int N, int K,
+             void* workspace, int64_t workspace_bytes, cudaStream_t st) {
+  if (M == 0) return FP8ATTN_OK;
+  if (xq == nullptr || x_scale == nullptr || w == nullptr || w_scale == nullptr || out == nullptr)
+    return fail(FP8ATTN_EINVAL, "fp8 gemm: null pointer argument");
+  if (!aligned(xq, 16) || !aligned(w, 16) || xq_row_stride < K || xq_row_stride % 16 != 0)
+    return fail(FP8ATTN_EINVAL, "fp8 gemm: xq and w must be 16-byte aligned, xq's row stride "
+                ">= K and a multiple of 16 bytes");
+  if (!aligned(x_scale, 2) || !aligned(w_scale, 2) || !aligned(out, 2) || out_row_stride < N)
+    return fail(FP8ATTN_EINVAL, "fp8 gemm: scales and out must be 2-byte aligned, out's row "
+                "stride >= N");
+  const int sms = device_sms();
+  const int64_t need = fp8attn::fp8_gemm_workspace_bytes(M, N, K, sms);
+  if (workspace == nullptr || workspace_bytes < need || !aligned(workspace, 16))
+    return fail(FP8ATTN_EWORKSPACE, "fp8 gemm: workspace of %lld bytes (16-byte aligned) needed, "
+                "got %lld", static_cast<long long>(need), static_cast<long long>(workspace_bytes));
+  fp8attn::Fp8GemmParams p;
+  p.xq = static_cast<const uint8_t*>(xq);
+  p.xq_row_stride = xq_row_stride;
+  p.x_scale = static_cast<const uint16_t*>(x_scale);
+  p.w = static_cast<const uint8_t*>(w);
+  p.w_scale = static_cast<const uint16_t*>(w_scale);
+  p.out = static_cast<uint16_t*>(out);
+  p.out_row_stride = out_row_stride;
+  p.err = static_cast<int*>(workspace);
+  p.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + fp8attn::kCtrlInts * 4);
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.splits = fp8attn::fp8_gemm_splits(M, N, K, sms);
+  const cudaError_t e = fp8attn::launch_fp8_block_gemm(p, st);
+  if (e == cudaErrorInvalidValue) return fail(FP8ATTN_EINVAL, "fp8 gemm: tensor map rejected");
+  return e == cudaSuccess ? FP8ATTN_OK : cuda_fail(e, "fp8 gemm launch");
+}
+
+}  // namespace
+
+extern "C" {
+
+int64_t fp8attn_fp8_gemm_workspace_bytes(int64_t M, int N, int K) {
+  if (M < 0 || N <= 0 || K <= 0) return -1;
+  return fp8attn::fp8_gemm_workspace_bytes(M, N, K, device_sms());
+}
+
+int64_t fp8attn_fp8_linear_workspace_bytes(int64_t M, int N, int K) {
+  if (M < 0 || N <= 0 || K <= 0) return -1;
+  return round16(fp8attn_fp8_gemm_workspace_bytes(M, N, K)) + round16(M * K) +
+         round16(M * (K / 128) * 2);
+}
+
+int fp8attn_fp8_dyn_quant(const void* x, int64_t x_row_stride, void* xq, int64_t xq_row_stride,
+                          void* x_scale, int64_t M, int K, void* stream) {
+  if (M < 0 || K <= 0 || K % 128 != 0)
+    return fail(FP8ATTN_EINVAL, "fp8 quant needs M >= 0 and K a positive multiple of 128 "
+                "(got M=%lld K=%d)", static_cast<long long>(M), K);
+  return run_quant(x, x_row_stride, xq, xq_row_stride, x_scale, M, K,
+                   static_cast<cudaStream_t>(stream));
+}
+
+int fp8attn_fp8_block_gemm(const void* xq, int64_t xq_row_stride, const void* x_scale,
+                           const void* w, const void* w_scale, void* out, int64_t out_row_stride,
+                           int64_t M, int N, int K, void* workspace, int64_t workspace_bytes,
+                           void* stream) {
+  const int rc = check_linear_sizes(M, N, K);
+  if (rc) return rc;
+  return run_gemm(xq, xq_row_stride, x_scale, w, w_scale, out, out_row_stride, M, N, K, workspace,
+                  workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int fp8attn_fp8_block_linear(const void* x, int64_t x_row_stride, const void* w,
+                             const void* w_scale, void* out, int64_t out_row_stride, int64_t M,
+                             int N, int K, void* workspace, int64_t workspace_bytes,
+                             void* stream) {
+  int rc = check_linear_sizes(M, N, K);
+  if (rc) return rc;
+  if (M == 0) return FP8ATTN_OK;
+  const int64_t need = fp8attn_fp8_linear_workspace_bytes(M, N, K);
+  if (workspace == nullptr || workspace_bytes < need || !aligned(workspace, 16))
+    return fail(FP8ATTN_EWORKSPACE, "fp8 linear: workspace of %lld bytes (16-byte aligned) "
+                "needed, got %lld", static_cast<long long>(need),
+                static_cast<long long>(workspace_bytes));
+  const int64_t gemm_ws = round16(fp8attn_fp8_gemm_workspace_bytes(M, N, K));
+  uint8_t* base = static_cast<uint8_t*>(workspace);
+  uint8_t* xq = base + gemm_ws;
+  uint8_t* xs = xq + round16(M * K);
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  rc = run_quant(x, x_row_stride, xq, K, xs, M, K, st);
+  if (rc) return rc;
+  return run_gemm(xq, K, xs, w, w_scale, out, out_row_stride, M, N, K, workspace, gemm_ws, st);
+}
+
+}  // extern "C"

@@ -1,0 +1,363 @@
+// FP8 block-scaled linear layer on the sm_100a tensor cores: y = x . w^T with e4m3 weights in
+// 128 x 128 blocks (one bf16 scale each) and activations quantised per token and 128-column group.
+//
+// Replaces fp8_block_linear (nanovllm/kernels/fp8_linear.py:93-139) and its two Triton kernels:
+//   fp8_dyn_quant_kernel (:11-31): per (token, 128-column group) scale = amax / 448 (1 for an
+//     all-zero group), xq = e4m3(clamp(x / scale, +-448)), the scale stored as bf16 (bytes equal
+//     to the reference's on the GPU: the same approximate fp32 division);
+//   fp8_block_gemm_kernel (:34-71): per 128-column block kb, the fp32 dot of the block times
+//     (x_scale[m, kb] * w_scale[n / 128, kb]) accumulated in fp32, the sum rounded once to the
+//     output dtype.
+//
+// The GEMM is computed transposed (out^T = w . xq^T), so that the weight rows fill the MMA's 128
+// rows and the few tokens of a decode batch are its N (64 per CTA): one CTA owns a 128-row block of
+// the output features and 64 tokens, over a range of K blocks (split-K, so that thin decode GEMMs
+// still put a CTA on every SM; the ranges' fp32 partial sums are added by a second kernel in split
+// order).  Warps:
+//   warp 4  producer: per K block, TMA loads of the weight tile (128 rows x 128 bytes) and the
+//           token tile (64 rows x 128 bytes, 128B swizzle, rows past M read as zeros) into a
+//           6-stage ring, and the block's scales (64 token scales, one weight scale) as fp32;
+//   warp 5  MMA issuer (one thread): D = w_kb . xq_kb^T, four kind::f8f6f4 products of K = 32
+//           into one of two 64-column tensor-memory buffers;
+//   warps 0-3  promotion: thread t = output feature n0 + t (tensor-memory lane t) reads its 64
+//           values of D and accumulates acc[j] += D[t, j] * (x_scale[j] * w_scale) in fp32
+//           registers (the reference's per-block scaling, which the tensor cores cannot apply:
+//           the scales are arbitrary fp32, not powers of two); at the end it writes its column of
+//           the output (or of its range's partial sum).
+#include "common.cuh"
+#include "kernels.h"
+#include "tcgen05.cuh"
+
+namespace fp8attn {
+namespace {
+
+constexpr int kBlk = 128;                 // K block (bytes of e4m3) and weight rows per CTA
+constexpr int kTok = kFp8GemmTokens;      // tokens per CTA
+constexpr int kGemmStages = 6;
+constexpr int kGemmThreads = 6 * 32;
+constexpr int kProducerWarp = 4;
+constexpr int kMmaWarp = 5;
+
+// ------------------------------------------------------------------ dynamic quantisation
+// a / b as the reference computes it: Triton's `/` on fp32 tensors is the full-range approximate
+// division (div.full.f32), not the IEEE one.  With it the quantised bytes equal the reference's;
+// with IEEE division about 0.1 % of them differed by one step (quotients that are exact e4m3
+// rounding midpoints, e.g. 0.816406 / 0.00537109 = 152 between 144 and 160, are common with bf16
+// inputs and scales).
+__device__ __forceinline__ float div_like_reference(float a, float b) {
+  float y;
+  asm("div.full.f32 %0, %1, %2;" : "=f"(y) : "f"(a), "f"(b));
+  return y;
+}
+
+// One warp per (token, 128-column group): lane l takes columns 4l .. 4l + 3.
+__global__ void __launch_bounds__(256) fp8_dyn_quant_kernel(const Fp8QuantParams p) {
+  const int64_t groups = p.M * (p.K / kBlk);
+  const int64_t w = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (w >= groups) return;  // uniform per warp
+  const int kc = p.K / kBlk;
+  const int64_t m = w / kc;
+  const int g = static_cast<int>(w - m * kc);
+  const uint2 raw = *reinterpret_cast<const uint2*>(p.x + m * p.x_row_stride + g * kBlk + 4 * lane);
+  float x[4] = {__uint_as_float(raw.x << 16), __uint_as_float(raw.x & 0xFFFF0000u),
+                __uint_as_float(raw.y << 16), __uint_as_float(raw.y & 0xFFFF0000u)};
+  float amax = fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3])));
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+  float scale = div_like_reference(amax, 448.0f);
+  if (!(scale > 0.f)) scale = 1.0f;  // an all-zero group
+#pragma unroll
+  for (int i = 0; i < 4; ++i) x[i] = fminf(fmaxf(div_like_reference(x[i], scale), -448.0f), 448.0f);
+  const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(x[0], x[1]), __NV_SATFINITE, __NV_E4M3);
+  const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(x[2], x[3]), __NV_SATFINITE, __NV_E4M3);
+  *reinterpret_cast<uint32_t*>(p.xq + m * p.xq_row_stride + g * kBlk + 4 * lane) = lo | (hi << 16);
+  if (lane == 0) {
+    const __nv_bfloat16 s = __float2bfloat16_rn(scale);
+    p.x_scale[m * kc + g] = *reinterpret_cast<const uint16_t*>(&s);
+  }
+}
+
+// ------------------------------------------------------------------ block-scaled GEMM
+struct __align__(1024) GemmSmem {
+  uint8_t w[kGemmStages][kBlk * kBlk];  // weight tiles: 128 rows x 128 bytes, 128B swizzle
+  uint8_t x[kGemmStages][kTok * kBlk];  // token tiles: 64 rows x 128 bytes, 128B swizzle
+  float xs[kGemmStages][kTok];          // the K block's token scales
+  float ws[kGemmStages];                // the K block's weight scale
+  uint64_t full[kGemmStages];           // tiles landed and scales written
+  uint64_t empty[kGemmStages];          // the MMA's commit and every promotion thread
+  uint64_t d_full[2];                   // D buffer complete
+  uint64_t d_empty[2];                  // D buffer read by every promotion thread
+  uint32_t tmem_base;
+};
+static_assert(sizeof(GemmSmem) + 1024 <= 227 * 1024, "smem");
+
+__device__ __forceinline__ float bf16_to_f32(uint16_t b) {
+  return __uint_as_float(static_cast<uint32_t>(b) << 16);
+}
+
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    fp8_block_gemm_kernel(const __grid_constant__ CUtensorMap tmx,
+                          const __grid_constant__ CUtensorMap tmw, const Fp8GemmParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  GemmSmem& sm = *reinterpret_cast<GemmSmem*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int nb = blockIdx.x;                                   // 128 output features
+  const int64_t m0 = static_cast<int64_t>(blockIdx.y) * kTok;  // 64 tokens
+  const int split = blockIdx.z;
+  const int kc = p.K / kBlk;
+  const int per = (kc + p.splits - 1) / p.splits;
+  const int kb0 = split * per;
+  const int nk = max(0, min(kc, kb0 + per) - kb0);  // K blocks of this CTA
+
+  if (tid == 0) {
+    for (int i = 0; i < kGemmStages; ++i) {
+      mbar_init(&sm.full[i], 1);
+      mbar_init(&sm.empty[i], 1 + 128);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&sm.d_full[b], 1);
+      mbar_init(&sm.d_empty[b], 128);
+    }
+    fence_mbar_init();
+  }
+  if (warp == kProducerWarp && lane == 0) {
+    prefetch_tensormap(&tmx);
+    prefetch_tensormap(&tmw);
+  }
+  if (warp == kMmaWarp) {
+    tc::tmem_alloc(&sm.tmem_base, 2 * kTok);
+    tc::tmem_relinquish();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = sm.tmem_base;
+  // launched as a programmatic dependent of the quantisation kernel: nothing it writes is read
+  // before it has finished
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+
+  if (warp == kProducerWarp) {
+    // ============================================================ producer
+    for (int i = 0; i < nk; ++i) {
+      const int stage = i % kGemmStages;
+      const uint32_t phase = (i / kGemmStages) & 1;
+      const int kb = kb0 + i;
+      if (!mbar_wait(&sm.empty[stage], phase ^ 1, p.err)) break;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {  // token scales of rows m0 + lane and m0 + 32 + lane
+        const int64_t m = m0 + lane + 32 * h;
+        sm.xs[stage][lane + 32 * h] = m < p.M ? bf16_to_f32(__ldg(p.x_scale + m * kc + kb)) : 0.f;
+      }
+      if (lane == 0) sm.ws[stage] = bf16_to_f32(__ldg(p.w_scale + static_cast<int64_t>(nb) * kc + kb));
+      __syncwarp();  // the scales are written before the arrive below releases them
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&sm.full[stage], kBlk * kBlk + kTok * kBlk);
+        tma_load_2d(&sm.w[stage][0], &tmw, &sm.full[stage], kb * kBlk, nb * kBlk);
+        tma_load_2d(&sm.x[stage][0], &tmx, &sm.full[stage], kb * kBlk, static_cast<int>(m0));
+      }
+      __syncwarp();
+    }
+  } else if (warp == kMmaWarp) {
+    // ============================================================ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = tc::idesc_e4m3(128, kTok, false, false);
+      for (int i = 0; i < nk; ++i) {
+        const int stage = i % kGemmStages;
+        const uint32_t phase = (i / kGemmStages) & 1;
+        const int buf = i & 1;
+        if (!mbar_wait(&sm.full[stage], phase, p.err)) break;
+        if (!mbar_wait(&sm.d_empty[buf], ((i >> 1) & 1) ^ 1, p.err)) break;
+        tc::fence_after_sync();
+        // K steps of 32 bytes add 2 to the start-address field (address >> 4)
+        const uint64_t wd = tc::smem_desc(smem_u32(&sm.w[stage][0]), 16, 1024, tc::kSw128);
+        const uint64_t xd = tc::smem_desc(smem_u32(&sm.x[stage][0]), 16, 1024, tc::kSw128);
+#pragma unroll
+        for (int ks = 0; ks < kBlk / 32; ++ks)
+          tc::mma_f8(tmem + buf * kTok, wd + static_cast<uint64_t>(2 * ks),
+                     xd + static_cast<uint64_t>(2 * ks), idesc, ks > 0 ? 1u : 0u);
+        tc::commit(&sm.d_full[buf]);
+        tc::commit(&sm.empty[stage]);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ============================================================ promotion, thread = feature
+    const uint32_t lane_base = static_cast<uint32_t>(32 * warp) << 16;
+    float acc[kTok];
+#pragma unroll
+    for (int j = 0; j < kTok; ++j) acc[j] = 0.f;
+    bool ok = true;
+    for (int i = 0; i < nk && ok; ++i) {
+      const int stage = i % kGemmStages;
+      const uint32_t phase = (i / kGemmStages) & 1;
+      const int buf = i & 1;
+      // the block's scales (written before full's arrive) and its D
+      if (!mbar_wait(&sm.full[stage], phase, p.err)) { ok = false; break; }
+      if (!mbar_wait(&sm.d_full[buf], (i >> 1) & 1, p.err)) { ok = false; break; }
+      tc::fence_after_sync();
+      const float sw = sm.ws[stage];
+#pragma unroll
+      for (int h = 0; h < kTok / 32; ++h) {
+        float d0[16], d1[16];
+        tc::ld16(tmem + lane_base + buf * kTok + 32 * h, d0);
+        tc::ld16(tmem + lane_base + buf * kTok + 32 * h + 16, d1);
+        tc::wait_ld();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          acc[32 * h + j] = fmaf(d0[j], sm.xs[stage][32 * h + j] * sw, acc[32 * h + j]);
+          acc[32 * h + 16 + j] = fmaf(d1[j], sm.xs[stage][32 * h + 16 + j] * sw, acc[32 * h + 16 + j]);
+        }
+      }
+      tc::fence_before_sync();
+      mbar_arrive(&sm.d_empty[buf]);
+      mbar_arrive(&sm.empty[stage]);
+    }
+    if (ok) {
+      const int n = nb * kBlk + tid;
+      for (int j = 0; j < kTok; ++j) {
+        const int64_t m = m0 + j;
+        if (m >= p.M) break;
+        if (p.splits == 1) {
+          const __nv_bfloat16 v = __float2bfloat16_rn(acc[j]);
+          p.out[m * p.out_row_stride + n] = *reinterpret_cast<const uint16_t*>(&v);
+        } else {
+          p.partials[(static_cast<int64_t>(split) * p.M + m) * p.N + n] = acc[j];
+        }
+      }
+    }
+  }
+
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  if (warp == kMmaWarp) tc::tmem_dealloc(tmem, 2 * kTok);
+}
+
+// out[m, n] = bf16(sum over the splits, in order, of partials[s, m, n]); four values a thread.
+__global__ void __launch_bounds__(256) fp8_split_reduce_kernel(const Fp8GemmParams p) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int64_t quads = p.M * (p.N / 4);
+  const int64_t q = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;
+  if (q >= quads) return;
+  const int64_t m = q / (p.N / 4);
+  const int n = static_cast<int>(q - m * (p.N / 4)) * 4;
+  float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int k = 0; k < p.splits; ++k) {
+    const float4 v = *reinterpret_cast<const float4*>(p.partials + (static_cast<int64_t>(k) * p.M + m) * p.N + n);
+    s.x += v.x;
+    s.y += v.y;
+    s.z += v.z;
+    s.w += v.w;
+  }
+  uint16_t* dst = p.out + m * p.out_row_stride + n;
+  const __nv_bfloat16 a = __float2bfloat16_rn(s.x), b = __float2bfloat16_rn(s.y);
+  const __nv_bfloat16 c = __float2bfloat16_rn(s.z), d = __float2bfloat16_rn(s.w);
+  dst[0] = *reinterpret_cast<const uint16_t*>(&a);
+  dst[1] = *reinterpret_cast<const uint16_t*>(&b);
+  dst[2] = *reinterpret_cast<const uint16_t*>(&c);
+  dst[3] = *reinterpret_cast<const uint16_t*>(&d);
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (fn == nullptr) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
+
+// [rows, row_bytes] e4m3 (row stride `stride` bytes) in boxes of 128 bytes x box_rows rows, 128B
+// swizzle; rows past the end read as zeros.
+bool make_rows_map(CUtensorMap* map, const void* base, int64_t rows, int64_t row_bytes,
+                   int64_t stride, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return false;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(row_bytes), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(stride)};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kBlk), static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+cudaError_t launch_fp8_dyn_quant(const Fp8QuantParams& p, cudaStream_t stream) {
+  const int64_t groups = p.M * (p.K / kBlk);
+  if (groups == 0) return cudaSuccess;
+  const int64_t blocks = (groups + 7) / 8;
+  fp8_dyn_quant_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(p);
+  return cudaGetLastError();
+}
+
+// Split-K: enough K ranges that the grid covers every SM once, each range at least 4 K blocks
+// (the ring's fill), at most 16 ranges; then as few ranges as that range length needs.
+int fp8_gemm_splits(int64_t M, int N, int K, int num_sms) {
+  const int64_t base = static_cast<int64_t>(N / kBlk) * ((M + kTok - 1) / kTok);
+  const int kc = K / kBlk;
+  if (base <= 0 || kc <= 0 || base >= num_sms) return 1;
+  int s = static_cast<int>((num_sms + base - 1) / base);
+  s = s < kc / 4 ? s : kc / 4;
+  s = s < 16 ? s : 16;
+  if (s < 2) return 1;
+  const int per = (kc + s - 1) / s;
+  return (kc + per - 1) / per;
+}
+
+int64_t fp8_gemm_workspace_bytes(int64_t M, int N, int K, int num_sms) {
+  const int s = fp8_gemm_splits(M, N, K, num_sms);
+  return kCtrlInts * 4 + (s > 1 ? static_cast<int64_t>(s) * M * N * 4 : 0);
+}
+
+cudaError_t launch_fp8_block_gemm(const Fp8GemmParams& p, cudaStream_t stream) {
+  if (p.M == 0) return cudaSuccess;
+  CUtensorMap tmx, tmw;
+  if (!make_rows_map(&tmx, p.xq, p.M, p.K, p.xq_row_stride, kTok) ||
+      !make_rows_map(&tmw, p.w, p.N, p.K, p.K, kBlk))
+    return cudaErrorInvalidValue;
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const size_t smem = sizeof(GemmSmem) + 1024;
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    cudaFuncSetAttribute(fp8_block_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(smem));
+    configured[dev] = true;
+  }
+  // both kernels are programmatic dependents of the kernel before them on the stream
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(p.N / kBlk), static_cast<unsigned>((p.M + kTok - 1) / kTok),
+                     static_cast<unsigned>(p.splits));
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, fp8_block_gemm_kernel, tmx, tmw, p);
+  if (e != cudaSuccess || p.splits == 1) return e;
+  const int64_t quads = p.M * (p.N / 4);
+  cudaLaunchConfig_t rcfg = {};
+  rcfg.gridDim = dim3(static_cast<unsigned>((quads + 255) / 256));
+  rcfg.blockDim = dim3(256);
+  rcfg.stream = stream;
+  rcfg.attrs = attr;
+  rcfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&rcfg, fp8_split_reduce_kernel, p);
+}
+
+}  // namespace fp8attn

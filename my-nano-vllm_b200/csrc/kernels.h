@@ -50,6 +50,41 @@ struct QkNormParams {
 };
 cudaError_t launch_qk_norm_rope_store(const QkNormParams& p, cudaStream_t stream);
 
+// ------------------------------------------------------------------ FP8 block-scaled linear
+// Dynamic quantisation of the activations: per token and 128-column group, scale = amax / 448
+// (1 for an all-zero group), e4m3 = RNE(clamp(x / scale, +-448)), the scale stored as bf16.
+struct Fp8QuantParams {
+  const uint16_t* x;  // bf16 [M, K], rows x_row_stride elements apart
+  int64_t x_row_stride;
+  uint8_t* xq;        // e4m3 [M, K], rows xq_row_stride bytes apart
+  int64_t xq_row_stride;
+  uint16_t* x_scale;  // bf16 [M, K / 128]
+  int64_t M;
+  int K;
+};
+cudaError_t launch_fp8_dyn_quant(const Fp8QuantParams& p, cudaStream_t stream);
+
+// out[M, N] = sum over 128-column blocks kb of (xq[:, kb] . w[:, kb]^T) * x_scale[m, kb] *
+// w_scale[n / 128, kb], in fp32, rounded once to bf16.
+struct Fp8GemmParams {
+  const uint8_t* xq;        // e4m3 [M, K], rows xq_row_stride bytes apart (multiple of 16)
+  int64_t xq_row_stride;
+  const uint16_t* x_scale;  // bf16 [M, K / 128]
+  const uint8_t* w;         // e4m3 [N, K], contiguous
+  const uint16_t* w_scale;  // bf16 [N / 128, K / 128]
+  uint16_t* out;            // bf16 [M, N], rows out_row_stride elements apart
+  int64_t out_row_stride;
+  float* partials;          // fp32 [splits, M, N] (split-K), from the workspace
+  int* err;                 // device error word (workspace head)
+  int64_t M;
+  int N, K;
+  int splits;               // K blocks are divided into this many ranges (one CTA each)
+};
+constexpr int kFp8GemmTokens = 64;  // tokens per CTA (the MMA's N)
+int fp8_gemm_splits(int64_t M, int N, int K, int num_sms);
+int64_t fp8_gemm_workspace_bytes(int64_t M, int N, int K, int num_sms);
+cudaError_t launch_fp8_block_gemm(const Fp8GemmParams& p, cudaStream_t stream);
+
 // ------------------------------------------------------------------ decode engine
 // Control block at the head of the decode workspace (ints):
 //   [0] sticky device error code, [1] next work item, [2] CTAs finished.

@@ -52,6 +52,16 @@ def _load() -> ctypes.CDLL:
     lib.fp8attn_read_error.argtypes = [vp, vp, i32, vp]
     lib.fp8attn_noalloc_read_error.restype = i32
     lib.fp8attn_noalloc_read_error.argtypes = [vp, i32, vp]
+    lib.fp8attn_fp8_gemm_workspace_bytes.restype = i64
+    lib.fp8attn_fp8_gemm_workspace_bytes.argtypes = [i64, i32, i32]
+    lib.fp8attn_fp8_linear_workspace_bytes.restype = i64
+    lib.fp8attn_fp8_linear_workspace_bytes.argtypes = [i64, i32, i32]
+    lib.fp8attn_fp8_dyn_quant.restype = i32
+    lib.fp8attn_fp8_dyn_quant.argtypes = [vp, i64, vp, i64, vp, i64, i32, vp]
+    lib.fp8attn_fp8_block_gemm.restype = i32
+    lib.fp8attn_fp8_block_gemm.argtypes = [vp, i64, vp, vp, vp, vp, i64, i64, i32, i32, vp, i64, vp]
+    lib.fp8attn_fp8_block_linear.restype = i32
+    lib.fp8attn_fp8_block_linear.argtypes = [vp, i64, vp, vp, vp, i64, i64, i32, i32, vp, i64, vp]
     lib.fp8attn_diag_wait_timeout.restype = i32
     lib.fp8attn_diag_wait_timeout.argtypes = [vp, i64, i32, vp]
     lib.fp8attn_diag_exp2.restype = i32

@@ -21,7 +21,7 @@ INCLUDE = os.path.join(os.path.dirname(ROOT), "include")
 LIB_PATH = os.path.join(PKG_DIR, "libfp8attn.so")
 
 SOURCES = ["capi.cu", "store.cu", "decode.cu", "prefill.cu", "prefill_persistent.cu", "diag.cu",
-           "qknorm.cu"]
+           "qknorm.cu", "fp8linear.cu"]
 HEADERS = ["common.cuh", "kernels.h", "tcgen05.cuh", "prefill_common.cuh"]
 
 NVCC_FLAGS = [

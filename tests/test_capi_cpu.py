@@ -84,3 +84,39 @@ def test_prefill_rejects_bad_arguments():
     bad = list(args)
     bad[13] = 0                                    # no sequences: nothing to do
     assert f(*bad) == _lib.OK
+
+
+def test_fp8_linear_rejects_bad_arguments():
+    lib = _lib.lib
+    assert lib.fp8attn_fp8_gemm_workspace_bytes(4, 0, 128) == -1
+    assert lib.fp8attn_fp8_linear_workspace_bytes(-1, 128, 128) == -1
+    # a grid that covers the SMs without split-K: only the control words
+    assert lib.fp8attn_fp8_gemm_workspace_bytes(1024, 4096, 1024) == 256
+    assert lib.fp8attn_fp8_linear_workspace_bytes(1024, 4096, 1024) == \
+        256 + 1024 * 1024 + 1024 * 8 * 2
+    split = lib.fp8attn_fp8_gemm_workspace_bytes(4, 256, 4096)       # thin: split-K partials
+    assert split > 256 and (split - 256) % (4 * 256 * 4) == 0
+    q = lib.fp8attn_fp8_dyn_quant
+    assert q(4096, 1024, 4096, 1024, 4096, 4, 100, None) == _lib.EINVAL     # K not a multiple of 128
+    assert q(4098, 1024, 4096, 1024, 4096, 4, 1024, None) == _lib.EINVAL    # x misaligned
+    assert q(4096, 1020, 4096, 1024, 4096, 4, 1024, None) == _lib.EINVAL    # x stride < K
+    assert q(None, 1024, 4096, 1024, 4096, 4, 1024, None) == _lib.EINVAL
+    assert q(4096, 1024, 4096, 1024, 4096, 0, 1024, None) == _lib.OK        # empty batch
+    g = lib.fp8attn_fp8_block_gemm
+    args = [4096, 1024, 4096, 4096, 4096, 4096, 256, 4, 256, 1024, 4096, 1 << 20, None]
+    bad = list(args)
+    bad[8] = 200                                   # N not a multiple of 128
+    assert g(*bad) == _lib.EINVAL
+    bad = list(args)
+    bad[1] = 1032                                  # xq row stride not a multiple of 16
+    assert g(*bad) == _lib.EINVAL
+    bad = list(args)
+    bad[11] = 16                                   # workspace too small
+    assert g(*bad) == _lib.EWORKSPACE
+    bad = list(args)
+    bad[7] = 0                                     # empty batch: nothing to do
+    assert g(*bad) == _lib.OK
+    lin = lib.fp8attn_fp8_block_linear
+    assert lin(4096, 1024, 4096, 4096, 4096, 256, 4, 256, 1000, 4096, 1 << 20, None) == _lib.EINVAL
+    assert lin(4096, 1024, 4096, 4096, 4096, 256, 4, 256, 1024, 4096, 64, None) == _lib.EWORKSPACE
+    assert "workspace" in lib.fp8attn_last_error().decode()

@@ -124,3 +124,31 @@ def test_qk_epilogue_oracle_matches_reference_outputs(golden):
     got = kc.reshape(-1, kvh, 128)[s[keep]]
     exp = g["k_cache"].reshape(-1, kvh, 128)[s[keep]]
     assert np.array_equal(got[same[keep]], exp[same[keep]])
+
+
+def test_fp8_linear_oracle_matches_reference_fixture(golden):
+    """oracle/fp8_linear.py against the reference's fp8_dyn_quant_kernel and fp8_block_linear run
+    on a GPU (tests/golden/make_golden_fp8linear.py).  Quantisation: scales identical, bytes
+    identical except where the quotient x / s lies within a few ulp of an e4m3 rounding midpoint
+    (the reference divides with the GPU's approximate fp32 division; the restatement's quotient is
+    the IEEE one), and there the neighbouring code.  GEMM, on the reference's own quantised bytes:
+    within one bf16 step of the reference plus 1e-3 of the output's largest magnitude (fp32
+    accumulation order), nearly all identical."""
+    from oracle import fp8_linear as ofl
+    g = golden("fp8_linear")
+    for i, (m, k, n) in enumerate(g["shapes"].tolist()):
+        x, w, ws = g[f"x_{i}"], g[f"w_{i}"], g[f"ws_{i}"]
+        xq, xs = ofl.dyn_quant(x)
+        assert np.array_equal(xs, g[f"xs_{i}"]), i
+        differ = xq != g[f"xq_{i}"]
+        assert bool(ofl.near_midpoint(x, ulps=4)[differ].all()), (i, int(differ.sum()))
+        a, b = xq[differ].astype(np.int16), g[f"xq_{i}"][differ].astype(np.int16)
+        assert bool((np.abs((a & 0x7F) - (b & 0x7F)) == 1).all()) and bool(((a ^ b) & 0x80 == 0).all())
+        if i == 0:
+            assert int(xs[0, 0]) == 0x3F80                 # the all-zero group: scale 1
+        y = ofl.block_gemm_f32(g[f"xq_{i}"], g[f"xs_{i}"], w, ws)
+        r = ofl.bf16_bits_to_f32(g[f"y_{i}"])
+        err = np.abs(ofl.bf16_bits_to_f32(ofl.f32_to_bf16_bits(y)).astype(np.float64) - r)
+        bound = 2.0 ** -7 * np.abs(r) + 1e-3 * float(np.abs(r).max())
+        assert bool((err <= bound).all()), (i, float(err.max()))
+        assert (ofl.f32_to_bf16_bits(y) == g[f"y_{i}"]).mean() >= 0.97, i
