@@ -563,9 +563,9 @@ int check_linear_sizes(int64_t M, int N, int K) {
   if (M < 0 || N <= 0 || K <= 0 || N % 128 != 0 || K % 128 != 0)
     return fail(FP8ATTN_EINVAL, "fp8 linear needs M >= 0 and N, K positive multiples of 128 "
                 "(got M=%lld N=%d K=%d)", static_cast<long long>(M), N, K);
-  if ((M + fp8attn::kFp8GemmTokens - 1) / fp8attn::kFp8GemmTokens > 65535)
-    return fail(FP8ATTN_EINVAL, "fp8 linear: M=%lld exceeds %d rows", static_cast<long long>(M),
-                65535 * fp8attn::kFp8GemmTokens);
+  if ((M + fp8attn::kFp8GemmTokens - 1) / fp8attn::kFp8GemmTokens * (N / 128) > (1LL << 26))
+    return fail(FP8ATTN_EINVAL, "fp8 linear: M=%lld x N=%d is more than 2^26 output tiles",
+                static_cast<long long>(M), N);
   return FP8ATTN_OK;
 }
 
@@ -624,7 +624,7 @@ int run_gemm(const void* xq, int64_t xq_row_stride, const void* x_scale, const v
   p.N = N;
   p.K = K;
   p.splits = fp8attn::fp8_gemm_splits(M, N, K, sms);
-  const cudaError_t e = fp8attn::launch_fp8_block_gemm(p, st);
+  const cudaError_t e = fp8attn::launch_fp8_block_gemm(p, sms, st);
   if (e == cudaErrorInvalidValue) return fail(FP8ATTN_EINVAL, "fp8 gemm: tensor map rejected");
   return e == cudaSuccess ? FP8ATTN_OK : cuda_fail(e, "fp8 gemm launch");
 }

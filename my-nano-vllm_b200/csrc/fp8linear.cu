@@ -10,20 +10,25 @@
 //     output dtype.
 //
 // The GEMM is computed transposed (out^T = w . xq^T), so that the weight rows fill the MMA's 128
-// rows and the few tokens of a decode batch are its N (64 per CTA): one CTA owns a 128-row block of
-// the output features and 64 tokens, over a range of K blocks (split-K, so that thin decode GEMMs
-// still put a CTA on every SM; the ranges' fp32 partial sums are added by a second kernel in split
-// order).  Warps:
-//   warp 4  producer: per K block, TMA loads of the weight tile (128 rows x 128 bytes) and the
-//           token tile (64 rows x 128 bytes, 128B swizzle, rows past M read as zeros) into a
-//           6-stage ring, and the block's scales (64 token scales, one weight scale) as fp32;
-//   warp 5  MMA issuer (one thread): D = w_kb . xq_kb^T, four kind::f8f6f4 products of K = 32
-//           into one of two 64-column tensor-memory buffers;
-//   warps 0-3  promotion: thread t = output feature n0 + t (tensor-memory lane t) reads its 64
-//           values of D and accumulates acc[j] += D[t, j] * (x_scale[j] * w_scale) in fp32
-//           registers (the reference's per-block scaling, which the tensor cores cannot apply:
-//           the scales are arbitrary fp32, not powers of two); at the end it writes its column of
-//           the output (or of its range's partial sum).
+// rows and the tokens are its N.  A work unit is one 128-row block of output features x 128
+// tokens x a range of K blocks (split-K, so that thin decode GEMMs still occupy every SM; the
+// ranges' fp32 partial sums are added by a second kernel in split order).  The grid is persistent:
+// one CTA per SM walks units u = blockIdx.x, + gridDim.x, ..., and its pipelines run on across
+// unit boundaries.  Warps:
+//   warp 8   producer: per K block, TMA loads of the weight tile (128 rows x 128 bytes) and the
+//            token tile (128 rows x 128 bytes; 128B swizzle, rows past M read as zeros) into a
+//            5-stage ring;
+//   warp 10  scales: per K block, x_scale[m, kb] * w_scale[nb, kb] in fp32 for the unit's 128
+//            tokens into the stage's slot, the loads of 4 blocks in flight together (they are
+//            strided 2-byte reads, off the producer's path);
+//   warp 9   MMA issuer (one thread): D = w_kb . xq_kb^T, four kind::f8f6f4 products of K = 32
+//            into one of four 128-column tensor-memory buffers (all 512 columns), so the tensor
+//            cores run up to four blocks ahead of the promotion;
+//   warps 0-7  promotion: warp w reads tensor-memory lanes 32 (w % 4) .. + 31 (output features)
+//            and tokens 64 (w / 4) .. + 63 of D and accumulates acc += D * scale product in fp32
+//            registers, block by block in K order (the reference's per-block scaling, which the
+//            tensor cores cannot apply: the scales are arbitrary fp32, not powers of two); at a
+//            unit's end it writes its outputs (or its range's partial sums).
 #include "common.cuh"
 #include "kernels.h"
 #include "tcgen05.cuh"
@@ -31,12 +36,16 @@
 namespace fp8attn {
 namespace {
 
-constexpr int kBlk = 128;                 // K block (bytes of e4m3) and weight rows per CTA
-constexpr int kTok = kFp8GemmTokens;      // tokens per CTA
-constexpr int kGemmStages = 6;
-constexpr int kGemmThreads = 6 * 32;
-constexpr int kProducerWarp = 4;
-constexpr int kMmaWarp = 5;
+constexpr int kBlk = 128;                 // K block (bytes of e4m3) and weight rows per unit
+constexpr int kTok = kFp8GemmTokens;      // tokens per unit (the MMA's N)
+constexpr int kGemmStages = 5;
+constexpr int kDBufs = 4;                 // D buffers of kTok columns: all 512 of tensor memory
+constexpr int kPromoThreads = 256;        // warps 0-7
+constexpr int kProducerWarp = 8;
+constexpr int kMmaWarp = 9;
+constexpr int kScaleWarp = 10;
+constexpr int kGemmThreads = 11 * 32;
+constexpr int kScaleBatch = 4;            // K blocks whose scale loads are in flight together
 
 // ------------------------------------------------------------------ dynamic quantisation
 // a / b as the reference computes it: Triton's `/` on fp32 tensors is the full-range approximate
@@ -81,19 +90,39 @@ __global__ void __launch_bounds__(256) fp8_dyn_quant_kernel(const Fp8QuantParams
 // ------------------------------------------------------------------ block-scaled GEMM
 struct __align__(1024) GemmSmem {
   uint8_t w[kGemmStages][kBlk * kBlk];  // weight tiles: 128 rows x 128 bytes, 128B swizzle
-  uint8_t x[kGemmStages][kTok * kBlk];  // token tiles: 64 rows x 128 bytes, 128B swizzle
-  float xs[kGemmStages][kTok];          // the K block's token scales
-  float ws[kGemmStages];                // the K block's weight scale
-  uint64_t full[kGemmStages];           // tiles landed and scales written
+  uint8_t x[kGemmStages][kTok * kBlk];  // token tiles: 128 rows x 128 bytes, 128B swizzle
+  float ss[kGemmStages][kTok];          // x_scale[m, kb] * w_scale[nb, kb] of the stage's block
+  uint64_t full[kGemmStages];           // tiles landed
+  uint64_t ss_full[kGemmStages];        // the stage's scale products written (32 lanes)
   uint64_t empty[kGemmStages];          // the MMA's commit and every promotion thread
-  uint64_t d_full[2];                   // D buffer complete
-  uint64_t d_empty[2];                  // D buffer read by every promotion thread
+  uint64_t d_full[kDBufs];              // D buffer complete
+  uint64_t d_empty[kDBufs];             // D buffer read by every promotion thread
   uint32_t tmem_base;
 };
 static_assert(sizeof(GemmSmem) + 1024 <= 227 * 1024, "smem");
+static_assert(sizeof(GemmSmem) > 114 * 1024, "one CTA per SM: the D ring takes all of TMEM");
 
 __device__ __forceinline__ float bf16_to_f32(uint16_t b) {
   return __uint_as_float(static_cast<uint32_t>(b) << 16);
+}
+
+// Work unit u -> (feature block nb, token tile mt, K range split); feature blocks vary fastest.
+struct GemmUnit {
+  int nb, split, kb0, nk;
+  int64_t m0;
+};
+__device__ __forceinline__ GemmUnit gemm_unit(const Fp8GemmParams& p, int64_t u) {
+  const int tiles_n = p.N / kBlk;
+  const int kc = p.K / kBlk;
+  const int per = (kc + p.splits - 1) / p.splits;
+  GemmUnit g;
+  g.nb = static_cast<int>(u % tiles_n);
+  const int64_t rest = u / tiles_n;
+  g.split = static_cast<int>(rest % p.splits);
+  g.m0 = (rest / p.splits) * kTok;
+  g.kb0 = g.split * per;
+  g.nk = max(0, min(kc, g.kb0 + per) - g.kb0);
+  return g;
 }
 
 __global__ void __launch_bounds__(kGemmThreads, 1)
@@ -103,22 +132,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   GemmSmem& sm = *reinterpret_cast<GemmSmem*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int nb = blockIdx.x;                                   // 128 output features
-  const int64_t m0 = static_cast<int64_t>(blockIdx.y) * kTok;  // 64 tokens
-  const int split = blockIdx.z;
   const int kc = p.K / kBlk;
-  const int per = (kc + p.splits - 1) / p.splits;
-  const int kb0 = split * per;
-  const int nk = max(0, min(kc, kb0 + per) - kb0);  // K blocks of this CTA
+  const int64_t units = ((p.M + kTok - 1) / kTok) * (p.N / kBlk) * p.splits;
 
   if (tid == 0) {
     for (int i = 0; i < kGemmStages; ++i) {
       mbar_init(&sm.full[i], 1);
-      mbar_init(&sm.empty[i], 1 + 128);
+      mbar_init(&sm.ss_full[i], 32);
+      mbar_init(&sm.empty[i], 1 + kPromoThreads);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < kDBufs; ++b) {
       mbar_init(&sm.d_full[b], 1);
-      mbar_init(&sm.d_empty[b], 128);
+      mbar_init(&sm.d_empty[b], kPromoThreads);
     }
     fence_mbar_init();
   }
@@ -127,7 +152,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     prefetch_tensormap(&tmw);
   }
   if (warp == kMmaWarp) {
-    tc::tmem_alloc(&sm.tmem_base, 2 * kTok);
+    tc::tmem_alloc(&sm.tmem_base, kDBufs * kTok);
     tc::tmem_relinquish();
   }
   tc::fence_before_sync();
@@ -138,92 +163,145 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   // before it has finished
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
+  // Every role walks the same units and K blocks; r counts this CTA's K blocks (ring position).
   if (warp == kProducerWarp) {
-    // ============================================================ producer
-    for (int i = 0; i < nk; ++i) {
-      const int stage = i % kGemmStages;
-      const uint32_t phase = (i / kGemmStages) & 1;
-      const int kb = kb0 + i;
-      if (!mbar_wait(&sm.empty[stage], phase ^ 1, p.err)) break;
+    // ============================================================ producer (TMA)
+    if (lane == 0) {
+      uint32_t r = 0;
+      bool ok = true;
+      for (int64_t u = blockIdx.x; u < units && ok; u += gridDim.x) {
+        const GemmUnit g = gemm_unit(p, u);
+        for (int i = 0; i < g.nk; ++i, ++r) {
+          const int stage = r % kGemmStages;
+          if (!mbar_wait(&sm.empty[stage], ((r / kGemmStages) & 1) ^ 1, p.err)) { ok = false; break; }
+          mbar_arrive_expect_tx(&sm.full[stage], kBlk * kBlk + kTok * kBlk);
+          tma_load_2d(&sm.w[stage][0], &tmw, &sm.full[stage], (g.kb0 + i) * kBlk, g.nb * kBlk);
+          tma_load_2d(&sm.x[stage][0], &tmx, &sm.full[stage], (g.kb0 + i) * kBlk,
+                      static_cast<int>(g.m0));
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == kScaleWarp) {
+    // ============================================================ scale products
+    // ss[m] = x_scale[m0 + m, kb] * w_scale[nb, kb] in fp32 (the reference's s_act * s_w).  The
+    // loads of kScaleBatch blocks are issued together, before the waits for their stages, so
+    // their latency overlaps.
+    uint32_t r = 0;
+    bool ok = true;
+    for (int64_t u = blockIdx.x; u < units && ok; u += gridDim.x) {
+      const GemmUnit g = gemm_unit(p, u);
+      for (int i0 = 0; i0 < g.nk && ok; i0 += kScaleBatch) {
+        float xv[kScaleBatch][kTok / 32], sw[kScaleBatch];
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {  // token scales of rows m0 + lane and m0 + 32 + lane
-        const int64_t m = m0 + lane + 32 * h;
-        sm.xs[stage][lane + 32 * h] = m < p.M ? bf16_to_f32(__ldg(p.x_scale + m * kc + kb)) : 0.f;
+        for (int t = 0; t < kScaleBatch; ++t) {
+          const int kb = g.kb0 + min(i0 + t, g.nk - 1);
+          sw[t] = bf16_to_f32(__ldg(p.w_scale + static_cast<int64_t>(g.nb) * kc + kb));
+#pragma unroll
+          for (int e = 0; e < kTok / 32; ++e) {
+            const int64_t m = g.m0 + lane + 32 * e;
+            xv[t][e] = m < p.M ? bf16_to_f32(__ldg(p.x_scale + m * kc + kb)) : 0.f;
+          }
+        }
+#pragma unroll
+        for (int t = 0; t < kScaleBatch; ++t) {
+          if (i0 + t >= g.nk) break;
+          const uint32_t rr = r + i0 + t;
+          const int stage = rr % kGemmStages;
+          if (!mbar_wait(&sm.empty[stage], ((rr / kGemmStages) & 1) ^ 1, p.err)) { ok = false; break; }
+#pragma unroll
+          for (int e = 0; e < kTok / 32; ++e) sm.ss[stage][lane + 32 * e] = xv[t][e] * sw[t];
+          mbar_arrive(&sm.ss_full[stage]);
+        }
       }
-      if (lane == 0) sm.ws[stage] = bf16_to_f32(__ldg(p.w_scale + static_cast<int64_t>(nb) * kc + kb));
-      __syncwarp();  // the scales are written before the arrive below releases them
-      if (lane == 0) {
-        mbar_arrive_expect_tx(&sm.full[stage], kBlk * kBlk + kTok * kBlk);
-        tma_load_2d(&sm.w[stage][0], &tmw, &sm.full[stage], kb * kBlk, nb * kBlk);
-        tma_load_2d(&sm.x[stage][0], &tmx, &sm.full[stage], kb * kBlk, static_cast<int>(m0));
-      }
-      __syncwarp();
+      r += g.nk;
     }
   } else if (warp == kMmaWarp) {
     // ============================================================ MMA issuer
     if (lane == 0) {
       const uint32_t idesc = tc::idesc_e4m3(128, kTok, false, false);
-      for (int i = 0; i < nk; ++i) {
-        const int stage = i % kGemmStages;
-        const uint32_t phase = (i / kGemmStages) & 1;
-        const int buf = i & 1;
-        if (!mbar_wait(&sm.full[stage], phase, p.err)) break;
-        if (!mbar_wait(&sm.d_empty[buf], ((i >> 1) & 1) ^ 1, p.err)) break;
-        tc::fence_after_sync();
-        // K steps of 32 bytes add 2 to the start-address field (address >> 4)
-        const uint64_t wd = tc::smem_desc(smem_u32(&sm.w[stage][0]), 16, 1024, tc::kSw128);
-        const uint64_t xd = tc::smem_desc(smem_u32(&sm.x[stage][0]), 16, 1024, tc::kSw128);
+      uint32_t r = 0;
+      bool ok = true;
+      for (int64_t u = blockIdx.x; u < units && ok; u += gridDim.x) {
+        const GemmUnit g = gemm_unit(p, u);
+        for (int i = 0; i < g.nk; ++i, ++r) {
+          const int stage = r % kGemmStages;
+          const int buf = r % kDBufs;
+          if (!mbar_wait(&sm.full[stage], (r / kGemmStages) & 1, p.err) ||
+              !mbar_wait(&sm.d_empty[buf], ((r / kDBufs) & 1) ^ 1, p.err)) {
+            ok = false;
+            break;
+          }
+          tc::fence_after_sync();
+          // K steps of 32 bytes add 2 to the start-address field (address >> 4)
+          const uint64_t wd = tc::smem_desc(smem_u32(&sm.w[stage][0]), 16, 1024, tc::kSw128);
+          const uint64_t xd = tc::smem_desc(smem_u32(&sm.x[stage][0]), 16, 1024, tc::kSw128);
 #pragma unroll
-        for (int ks = 0; ks < kBlk / 32; ++ks)
-          tc::mma_f8(tmem + buf * kTok, wd + static_cast<uint64_t>(2 * ks),
-                     xd + static_cast<uint64_t>(2 * ks), idesc, ks > 0 ? 1u : 0u);
-        tc::commit(&sm.d_full[buf]);
-        tc::commit(&sm.empty[stage]);
+          for (int ks = 0; ks < kBlk / 32; ++ks)
+            tc::mma_f8(tmem + buf * kTok, wd + static_cast<uint64_t>(2 * ks),
+                       xd + static_cast<uint64_t>(2 * ks), idesc, ks > 0 ? 1u : 0u);
+          tc::commit(&sm.d_full[buf]);
+          tc::commit(&sm.empty[stage]);
+        }
       }
     }
     __syncwarp();
   } else {
-    // ============================================================ promotion, thread = feature
-    const uint32_t lane_base = static_cast<uint32_t>(32 * warp) << 16;
-    float acc[kTok];
-#pragma unroll
-    for (int j = 0; j < kTok; ++j) acc[j] = 0.f;
+    // ============================================================ promotion
+    // warp w: tensor-memory lanes 32 (w % 4) .. + 31 = output features nb * 128 + 32 (w % 4) +
+    // lane, and tokens 64 (w / 4) .. + 63 of the tile (D columns).
+    const int quad = warp & 3, half = warp >> 2;
+    const uint32_t lane_base = static_cast<uint32_t>(32 * quad) << 16;
+    uint32_t r = 0;
     bool ok = true;
-    for (int i = 0; i < nk && ok; ++i) {
-      const int stage = i % kGemmStages;
-      const uint32_t phase = (i / kGemmStages) & 1;
-      const int buf = i & 1;
-      // the block's scales (written before full's arrive) and its D
-      if (!mbar_wait(&sm.full[stage], phase, p.err)) { ok = false; break; }
-      if (!mbar_wait(&sm.d_full[buf], (i >> 1) & 1, p.err)) { ok = false; break; }
-      tc::fence_after_sync();
-      const float sw = sm.ws[stage];
+    for (int64_t u = blockIdx.x; u < units && ok; u += gridDim.x) {
+      const GemmUnit g = gemm_unit(p, u);
+      const int64_t t0 = g.m0 + 64 * half;  // first token of this warp
+      const bool active = t0 < p.M;         // warp-uniform
+      float acc[64];
 #pragma unroll
-      for (int h = 0; h < kTok / 32; ++h) {
-        float d0[16], d1[16];
-        tc::ld16(tmem + lane_base + buf * kTok + 32 * h, d0);
-        tc::ld16(tmem + lane_base + buf * kTok + 32 * h + 16, d1);
-        tc::wait_ld();
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          acc[32 * h + j] = fmaf(d0[j], sm.xs[stage][32 * h + j] * sw, acc[32 * h + j]);
-          acc[32 * h + 16 + j] = fmaf(d1[j], sm.xs[stage][32 * h + 16 + j] * sw, acc[32 * h + 16 + j]);
+      for (int j = 0; j < 64; ++j) acc[j] = 0.f;
+      for (int i = 0; i < g.nk; ++i, ++r) {
+        const int stage = r % kGemmStages;
+        const int buf = r % kDBufs;
+        if (!mbar_wait(&sm.ss_full[stage], (r / kGemmStages) & 1, p.err) ||
+            !mbar_wait(&sm.d_full[buf], (r / kDBufs) & 1, p.err)) {
+          ok = false;
+          break;
         }
+        tc::fence_after_sync();
+        if (active) {
+          const float* s = &sm.ss[stage][64 * half];
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            float d0[16], d1[16];
+            tc::ld16(tmem + lane_base + buf * kTok + 64 * half + 32 * h, d0);
+            tc::ld16(tmem + lane_base + buf * kTok + 64 * half + 32 * h + 16, d1);
+            tc::wait_ld();
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              acc[32 * h + j] = fmaf(d0[j], s[32 * h + j], acc[32 * h + j]);
+              acc[32 * h + 16 + j] = fmaf(d1[j], s[32 * h + 16 + j], acc[32 * h + 16 + j]);
+            }
+          }
+        }
+        tc::fence_before_sync();
+        mbar_arrive(&sm.d_empty[buf]);
+        mbar_arrive(&sm.empty[stage]);
       }
-      tc::fence_before_sync();
-      mbar_arrive(&sm.d_empty[buf]);
-      mbar_arrive(&sm.empty[stage]);
-    }
-    if (ok) {
-      const int n = nb * kBlk + tid;
-      for (int j = 0; j < kTok; ++j) {
-        const int64_t m = m0 + j;
-        if (m >= p.M) break;
-        if (p.splits == 1) {
-          const __nv_bfloat16 v = __float2bfloat16_rn(acc[j]);
-          p.out[m * p.out_row_stride + n] = *reinterpret_cast<const uint16_t*>(&v);
-        } else {
-          p.partials[(static_cast<int64_t>(split) * p.M + m) * p.N + n] = acc[j];
+      if (ok && active) {
+        const int n = g.nb * kBlk + 32 * quad + lane;
+#pragma unroll
+        for (int j = 0; j < 64; ++j) {
+          const int64_t m = t0 + j;
+          if (m < p.M) {
+            if (p.splits == 1) {
+              const __nv_bfloat16 v = __float2bfloat16_rn(acc[j]);
+              p.out[m * p.out_row_stride + n] = *reinterpret_cast<const uint16_t*>(&v);
+            } else {
+              p.partials[(static_cast<int64_t>(g.split) * p.M + m) * p.N + n] = acc[j];
+            }
+          }
         }
       }
     }
@@ -232,7 +310,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
-  if (warp == kMmaWarp) tc::tmem_dealloc(tmem, 2 * kTok);
+  if (warp == kMmaWarp) tc::tmem_dealloc(tmem, kDBufs * kTok);
 }
 
 // out[m, n] = bf16(sum over the splits, in order, of partials[s, m, n]); four values a thread.
@@ -302,18 +380,26 @@ cudaError_t launch_fp8_dyn_quant(const Fp8QuantParams& p, cudaStream_t stream) {
   return cudaGetLastError();
 }
 
-// Split-K: enough K ranges that the grid covers every SM once, each range at least 4 K blocks
-// (the ring's fill), at most 16 ranges; then as few ranges as that range length needs.
+// Split-K, only when there are fewer output tiles than SMs (else its partial sums cost more
+// traffic than the last wave's imbalance): the number of K ranges s (1 .. 16) that minimises the
+// persistent grid's time in K-block steps, ceil(units(s) / num_sms) * ceil(kc / s), the smaller s
+// on ties.
 int fp8_gemm_splits(int64_t M, int N, int K, int num_sms) {
   const int64_t base = static_cast<int64_t>(N / kBlk) * ((M + kTok - 1) / kTok);
   const int kc = K / kBlk;
-  if (base <= 0 || kc <= 0 || base >= num_sms) return 1;
-  int s = static_cast<int>((num_sms + base - 1) / base);
-  s = s < kc / 4 ? s : kc / 4;
-  s = s < 16 ? s : 16;
-  if (s < 2) return 1;
-  const int per = (kc + s - 1) / s;
-  return (kc + per - 1) / per;
+  if (base <= 0 || kc <= 0 || num_sms <= 0 || base >= num_sms) return 1;
+  int best = 1;
+  int64_t best_cost = ((base + num_sms - 1) / num_sms) * kc;
+  for (int s = 2; s <= 16 && s <= kc; ++s) {
+    const int per = (kc + s - 1) / s;
+    if ((kc + per - 1) / per != s) continue;  // s ranges of `per` blocks, none empty
+    const int64_t cost = ((base * s + num_sms - 1) / num_sms) * per;
+    if (cost < best_cost) {
+      best = s;
+      best_cost = cost;
+    }
+  }
+  return best;
 }
 
 int64_t fp8_gemm_workspace_bytes(int64_t M, int N, int K, int num_sms) {
@@ -321,7 +407,7 @@ int64_t fp8_gemm_workspace_bytes(int64_t M, int N, int K, int num_sms) {
   return kCtrlInts * 4 + (s > 1 ? static_cast<int64_t>(s) * M * N * 4 : 0);
 }
 
-cudaError_t launch_fp8_block_gemm(const Fp8GemmParams& p, cudaStream_t stream) {
+cudaError_t launch_fp8_block_gemm(const Fp8GemmParams& p, int num_sms, cudaStream_t stream) {
   if (p.M == 0) return cudaSuccess;
   CUtensorMap tmx, tmw;
   if (!make_rows_map(&tmx, p.xq, p.M, p.K, p.xq_row_stride, kTok) ||
@@ -336,13 +422,14 @@ cudaError_t launch_fp8_block_gemm(const Fp8GemmParams& p, cudaStream_t stream) {
                          static_cast<int>(smem));
     configured[dev] = true;
   }
+  const int64_t units = ((p.M + kTok - 1) / kTok) * (p.N / kBlk) * p.splits;
+  const int64_t ctas = units < num_sms ? units : num_sms;
   // both kernels are programmatic dependents of the kernel before them on the stream
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(p.N / kBlk), static_cast<unsigned>((p.M + kTok - 1) / kTok),
-                     static_cast<unsigned>(p.splits));
+  cfg.gridDim = dim3(static_cast<unsigned>(ctas));
   cfg.blockDim = dim3(kGemmThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;

@@ -78,12 +78,12 @@ struct Fp8GemmParams {
   int* err;                 // device error word (workspace head)
   int64_t M;
   int N, K;
-  int splits;               // K blocks are divided into this many ranges (one CTA each)
+  int splits;               // K blocks are divided into this many ranges (one unit each)
 };
-constexpr int kFp8GemmTokens = 64;  // tokens per CTA (the MMA's N)
+constexpr int kFp8GemmTokens = 128;  // tokens per work unit (the MMA's N)
 int fp8_gemm_splits(int64_t M, int N, int K, int num_sms);
 int64_t fp8_gemm_workspace_bytes(int64_t M, int N, int K, int num_sms);
-cudaError_t launch_fp8_block_gemm(const Fp8GemmParams& p, cudaStream_t stream);
+cudaError_t launch_fp8_block_gemm(const Fp8GemmParams& p, int num_sms, cudaStream_t stream);
 
 // ------------------------------------------------------------------ decode engine
 // Control block at the head of the decode workspace (ints):

@@ -96,7 +96,8 @@ def test_quant_matches_oracle(m, k):
     (4, 4096, 256),       # thin decode GEMM: split-K
     (37, 2048, 1024),     # partial token tile, split-K
     (130, 1024, 512),     # three token tiles, the last partial
-    (512, 1024, 4096),    # grid covers the SMs: no split
+    (512, 1024, 4096),    # 128 units, no split
+    (1000, 1024, 4096),   # 256 units on the persistent grid: CTAs run two, the last tile partial
 ])
 def test_gemm_matches_oracle(m, k, n):
     from nanovllm_b200.fp8_linear import fp8_block_gemm, fp8_dyn_quant
