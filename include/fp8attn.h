@@ -208,7 +208,8 @@ FP8ATTN_API int fp8attn_set_decode_min_chunk(int tokens);
  *   fp8attn_fp8_block_gemm (fp8_block_gemm_kernel, :34-71): out[m, n] = bf16(sum over groups g,
  *     in order, of (xq[m, g] . w[n, g]) * (x_scale[m, g] * w_scale[n / 128, g])), each group's
  *     dot exact (fp32 tensor-core accumulation of e4m3 products) and the sum kept in fp32.
- *     xq and w 16-byte aligned, xq's row stride a multiple of 16.  workspace: at least
+ *     xq, w and out 16-byte aligned, xq's row stride a multiple of 16 and out's a multiple of
+ *     8.  workspace: at least
  *     fp8attn_fp8_gemm_workspace_bytes(M, N, K) bytes, 16-byte aligned; its first int32 is the
  *     device error word (fp8attn_read_error reads it), the rest holds split-K partial sums.
  *   fp8attn_fp8_block_linear: both, with xq and x_scale placed in the workspace after the GEMM's

@@ -602,9 +602,10 @@ int run_gemm(const void* xq, int64_t xq_row_stride, const void* x_scale, const v
   if (!aligned(xq, 16) || !aligned(w, 16) || xq_row_stride < K || xq_row_stride % 16 != 0)
     return fail(FP8ATTN_EINVAL, "fp8 gemm: xq and w must be 16-byte aligned, xq's row stride "
                 ">= K and a multiple of 16 bytes");
-  if (!aligned(x_scale, 2) || !aligned(w_scale, 2) || !aligned(out, 2) || out_row_stride < N)
-    return fail(FP8ATTN_EINVAL, "fp8 gemm: scales and out must be 2-byte aligned, out's row "
-                "stride >= N");
+  if (!aligned(x_scale, 2) || !aligned(w_scale, 2) || !aligned(out, 16) || out_row_stride < N ||
+      out_row_stride % 8 != 0)
+    return fail(FP8ATTN_EINVAL, "fp8 gemm: scales must be 2-byte aligned, out 16-byte aligned "
+                "with a row stride >= N that is a multiple of 8");
   const int sms = device_sms();
   const int64_t need = fp8attn::fp8_gemm_workspace_bytes(M, N, K, sms);
   if (workspace == nullptr || workspace_bytes < need || !aligned(workspace, 16))

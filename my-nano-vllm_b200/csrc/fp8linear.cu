@@ -21,14 +21,17 @@
 //   warp 10  scales: per K block, x_scale[m, kb] * w_scale[nb, kb] in fp32 for the unit's 128
 //            tokens into the stage's slot, the loads of 4 blocks in flight together (they are
 //            strided 2-byte reads, off the producer's path);
-//   warp 9   MMA issuer (one thread): D = w_kb . xq_kb^T, four kind::f8f6f4 products of K = 32
-//            into one of four 128-column tensor-memory buffers (all 512 columns), so the tensor
-//            cores run up to four blocks ahead of the promotion;
-//   warps 0-7  promotion: warp w reads tensor-memory lanes 32 (w % 4) .. + 31 (output features)
-//            and tokens 64 (w / 4) .. + 63 of D and accumulates acc += D * scale product in fp32
-//            registers, block by block in K order (the reference's per-block scaling, which the
-//            tensor cores cannot apply: the scales are arbitrary fp32, not powers of two); at a
-//            unit's end it writes its outputs (or its range's partial sums).
+//   warp 9   MMA issuer (one thread): D = xq_kb . w_kb^T (tokens are the MMA's 128 rows, the
+//            128 features its N), four kind::f8f6f4 products of K = 32 into one of four
+//            128-column tensor-memory buffers (all 512 columns), so the tensor cores run up to
+//            four blocks ahead of the promotion;
+//   warps 0-7  promotion: warp w reads tensor-memory lanes 32 (w % 4) .. + 31 (tokens) and
+//            columns 64 (w / 4) .. + 63 (features) of D, so a thread owns 64 consecutive outputs
+//            of one token row and one scale product per K block, and accumulates
+//            acc += D * scale product in fp32 registers (packed fp32x2 fused multiply-adds),
+//            block by block in K order (the reference's per-block scaling, which the tensor cores
+//            cannot apply: the scales are arbitrary fp32, not powers of two); at a unit's end it
+//            writes its 64 outputs (or its range's partial sums) as 16-byte stores.
 #include "common.cuh"
 #include "kernels.h"
 #include "tcgen05.cuh"
@@ -40,7 +43,7 @@ constexpr int kBlk = 128;                 // K block (bytes of e4m3) and weight 
 constexpr int kTok = kFp8GemmTokens;      // tokens per unit (the MMA's N)
 constexpr int kGemmStages = 5;
 constexpr int kDBufs = 4;                 // D buffers of kTok columns: all 512 of tensor memory
-constexpr int kPromoThreads = 256;        // warps 0-7
+constexpr int kPromoWarps = 8;            // warps 0-7
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
 constexpr int kScaleWarp = 10;
@@ -94,13 +97,26 @@ struct __align__(1024) GemmSmem {
   float ss[kGemmStages][kTok];          // x_scale[m, kb] * w_scale[nb, kb] of the stage's block
   uint64_t full[kGemmStages];           // tiles landed
   uint64_t ss_full[kGemmStages];        // the stage's scale products written (32 lanes)
-  uint64_t empty[kGemmStages];          // the MMA's commit and every promotion thread
+  uint64_t empty[kGemmStages];          // the MMA's commit and every promotion warp
   uint64_t d_full[kDBufs];              // D buffer complete
-  uint64_t d_empty[kDBufs];             // D buffer read by every promotion thread
+  uint64_t d_empty[kDBufs];             // D buffer read by every promotion warp
   uint32_t tmem_base;
 };
 static_assert(sizeof(GemmSmem) + 1024 <= 227 * 1024, "smem");
 static_assert(sizeof(GemmSmem) > 114 * 1024, "one CTA per SM: the D ring takes all of TMEM");
+
+// a0 = fma(d0, s, a0), a1 = fma(d1, s, a1): one packed fp32x2 instruction, each half an IEEE
+// fused multiply-add.
+__device__ __forceinline__ void fma2(float& a0, float& a1, float d0, float d1, float s) {
+  asm("{\n\t.reg .b64 a, d, s;\n\t"
+      "mov.b64 a, {%0, %1};\n\t"
+      "mov.b64 d, {%2, %3};\n\t"
+      "mov.b64 s, {%4, %4};\n\t"
+      "fma.rn.f32x2 a, d, s, a;\n\t"
+      "mov.b64 {%0, %1}, a;\n\t}"
+      : "+f"(a0), "+f"(a1)
+      : "f"(d0), "f"(d1), "f"(s));
+}
 
 __device__ __forceinline__ float bf16_to_f32(uint16_t b) {
   return __uint_as_float(static_cast<uint32_t>(b) << 16);
@@ -139,11 +155,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     for (int i = 0; i < kGemmStages; ++i) {
       mbar_init(&sm.full[i], 1);
       mbar_init(&sm.ss_full[i], 32);
-      mbar_init(&sm.empty[i], 1 + kPromoThreads);
+      mbar_init(&sm.empty[i], 1 + kPromoWarps);
     }
     for (int b = 0; b < kDBufs; ++b) {
       mbar_init(&sm.d_full[b], 1);
-      mbar_init(&sm.d_empty[b], kPromoThreads);
+      mbar_init(&sm.d_empty[b], kPromoWarps);
     }
     fence_mbar_init();
   }
@@ -219,7 +235,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else if (warp == kMmaWarp) {
     // ============================================================ MMA issuer
     if (lane == 0) {
-      const uint32_t idesc = tc::idesc_e4m3(128, kTok, false, false);
+      const uint32_t idesc = tc::idesc_e4m3(kTok, kBlk, false, false);
       uint32_t r = 0;
       bool ok = true;
       for (int64_t u = blockIdx.x; u < units && ok; u += gridDim.x) {
@@ -234,12 +250,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
           tc::fence_after_sync();
           // K steps of 32 bytes add 2 to the start-address field (address >> 4)
-          const uint64_t wd = tc::smem_desc(smem_u32(&sm.w[stage][0]), 16, 1024, tc::kSw128);
           const uint64_t xd = tc::smem_desc(smem_u32(&sm.x[stage][0]), 16, 1024, tc::kSw128);
+          const uint64_t wd = tc::smem_desc(smem_u32(&sm.w[stage][0]), 16, 1024, tc::kSw128);
 #pragma unroll
           for (int ks = 0; ks < kBlk / 32; ++ks)
-            tc::mma_f8(tmem + buf * kTok, wd + static_cast<uint64_t>(2 * ks),
-                       xd + static_cast<uint64_t>(2 * ks), idesc, ks > 0 ? 1u : 0u);
+            tc::mma_f8_plain(tmem + buf * kBlk, xd + static_cast<uint64_t>(2 * ks),
+                             wd + static_cast<uint64_t>(2 * ks), idesc, ks > 0 ? 1u : 0u);
           tc::commit(&sm.d_full[buf]);
           tc::commit(&sm.empty[stage]);
         }
@@ -248,16 +264,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     __syncwarp();
   } else {
     // ============================================================ promotion
-    // warp w: tensor-memory lanes 32 (w % 4) .. + 31 = output features nb * 128 + 32 (w % 4) +
-    // lane, and tokens 64 (w / 4) .. + 63 of the tile (D columns).
+    // warp w: tensor-memory lanes 32 (w % 4) .. + 31 = tokens m0 + 32 (w % 4) + lane, and D
+    // columns 64 (w / 4) .. + 63 = output features nb * 128 + 64 (w / 4) + c: a thread owns 64
+    // consecutive outputs of one token row, and one scale product per K block.
     const int quad = warp & 3, half = warp >> 2;
     const uint32_t lane_base = static_cast<uint32_t>(32 * quad) << 16;
     uint32_t r = 0;
     bool ok = true;
     for (int64_t u = blockIdx.x; u < units && ok; u += gridDim.x) {
       const GemmUnit g = gemm_unit(p, u);
-      const int64_t t0 = g.m0 + 64 * half;  // first token of this warp
-      const bool active = t0 < p.M;         // warp-uniform
+      const int64_t m = g.m0 + 32 * quad + lane;
+      const bool active = g.m0 + 32 * quad < p.M;  // warp-uniform: some row of the warp is real
       float acc[64];
 #pragma unroll
       for (int j = 0; j < 64; ++j) acc[j] = 0.f;
@@ -271,37 +288,44 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         tc::fence_after_sync();
         if (active) {
-          const float* s = &sm.ss[stage][64 * half];
+          const float sc = sm.ss[stage][32 * quad + lane];
+          float d[4][16];
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            float d0[16], d1[16];
-            tc::ld16(tmem + lane_base + buf * kTok + 64 * half + 32 * h, d0);
-            tc::ld16(tmem + lane_base + buf * kTok + 64 * half + 32 * h + 16, d1);
-            tc::wait_ld();
+          for (int c = 0; c < 4; ++c) tc::ld16(tmem + lane_base + buf * kBlk + 64 * half + 16 * c, d[c]);
+          tc::wait_ld();
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              acc[32 * h + j] = fmaf(d0[j], s[32 * h + j], acc[32 * h + j]);
-              acc[32 * h + 16 + j] = fmaf(d1[j], s[32 * h + 16 + j], acc[32 * h + 16 + j]);
-            }
-          }
+          for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int j = 0; j < 16; j += 2)
+              fma2(acc[16 * c + j], acc[16 * c + j + 1], d[c][j], d[c][j + 1], sc);
         }
         tc::fence_before_sync();
-        mbar_arrive(&sm.d_empty[buf]);
-        mbar_arrive(&sm.empty[stage]);
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&sm.d_empty[buf]);
+          mbar_arrive(&sm.empty[stage]);
+        }
       }
-      if (ok && active) {
-        const int n = g.nb * kBlk + 32 * quad + lane;
+      if (ok && m < p.M) {
+        const int n0 = g.nb * kBlk + 64 * half;
+        if (p.splits == 1) {
+          uint4* dst = reinterpret_cast<uint4*>(p.out + m * p.out_row_stride + n0);
 #pragma unroll
-        for (int j = 0; j < 64; ++j) {
-          const int64_t m = t0 + j;
-          if (m < p.M) {
-            if (p.splits == 1) {
-              const __nv_bfloat16 v = __float2bfloat16_rn(acc[j]);
-              p.out[m * p.out_row_stride + n] = *reinterpret_cast<const uint16_t*>(&v);
-            } else {
-              p.partials[(static_cast<int64_t>(g.split) * p.M + m) * p.N + n] = acc[j];
+          for (int v = 0; v < 8; ++v) {
+            uint32_t w4[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const __nv_bfloat162 h2 = __floats2bfloat162_rn(acc[8 * v + 2 * e], acc[8 * v + 2 * e + 1]);
+              w4[e] = *reinterpret_cast<const uint32_t*>(&h2);
             }
+            dst[v] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
           }
+        } else {
+          float4* dst = reinterpret_cast<float4*>(
+              p.partials + (static_cast<int64_t>(g.split) * p.M + m) * p.N + n0);
+#pragma unroll
+          for (int v = 0; v < 16; ++v)
+            dst[v] = make_float4(acc[4 * v], acc[4 * v + 1], acc[4 * v + 2], acc[4 * v + 3]);
         }
       }
     }
