@@ -21,7 +21,7 @@
 //   warp 10  scales: per K block, x_scale[m, kb] * w_scale[nb, kb] in fp32 for the unit's 128
 //            tokens into the stage's slot, the loads of 4 blocks in flight together (they are
 //            strided 2-byte reads, off the producer's path);
-//   warp 9   MMA issuer (one thread): D = xq_kb . w_kb^T (tokens are the MMA's 128 rows, the
+//   warps 9, 11  MMA issuers (one thread each, alternate K blocks): D = xq_kb . w_kb^T (tokens are the MMA's 128 rows, the
 //            128 features its N), four kind::f8f6f4 products of K = 32 into one of four
 //            128-column tensor-memory buffers (all 512 columns), so the tensor cores run up to
 //            four blocks ahead of the promotion;
@@ -47,7 +47,8 @@ constexpr int kPromoWarps = 8;            // warps 0-7
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
 constexpr int kScaleWarp = 10;
-constexpr int kGemmThreads = 11 * 32;
+constexpr int kMmaWarp2 = 11;             // second MMA issuer: odd K-block positions
+constexpr int kGemmThreads = 12 * 32;
 constexpr int kScaleBatch = 4;            // K blocks whose scale loads are in flight together
 
 // ------------------------------------------------------------------ dynamic quantisation
@@ -232,15 +233,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       r += g.nk;
     }
-  } else if (warp == kMmaWarp) {
-    // ============================================================ MMA issuer
+  } else if (warp == kMmaWarp || warp == kMmaWarp2) {
+    // ============================================================ MMA issuers
+    // Two threads in warps on different schedulers take alternate K-block positions: an MMA
+    // instruction holds its issuing thread for about 100 cycles, more than the tensor core
+    // needs for it, so one issuer cannot keep the tensor core busy.  Their blocks go to distinct
+    // D buffers, and each thread's commits track its own MMAs only.
     if (lane == 0) {
       const uint32_t idesc = tc::idesc_e4m3(kTok, kBlk, false, false);
+      const uint32_t mine = warp == kMmaWarp2 ? 1u : 0u;
       uint32_t r = 0;
       bool ok = true;
       for (int64_t u = blockIdx.x; u < units && ok; u += gridDim.x) {
         const GemmUnit g = gemm_unit(p, u);
         for (int i = 0; i < g.nk; ++i, ++r) {
+          if ((r & 1u) != mine) continue;
           const int stage = r % kGemmStages;
           const int buf = r % kDBufs;
           if (!mbar_wait(&sm.full[stage], (r / kGemmStages) & 1, p.err) ||
