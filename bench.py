@@ -313,6 +313,8 @@ def _maxdiff(a, b):
 
 
 PARTS = ("config2", "config1", "config3", "store", "config4", "epilogue", "fp8linear")
+# half of a part, for profile captures that want one launch shape only
+SUBPARTS = ("fp8linear_decode", "fp8linear_prefill")
 
 
 def _store_sets(c, nsets, dev):
@@ -378,7 +380,9 @@ def secondary(dev, peaks, with_reference: bool, only=None):
             refgpu[name] = {"unavailable": f"{type(e).__name__}: {e}"}
 
     fp8_peak, fp8_kind = None, "measured e4m3 GEMM (torch._scaled_mm)"
-    if parts & {"config3", "fp8linear"}:
+    lin_decode = bool(parts & {"fp8linear", "fp8linear_decode"})
+    lin_prefill = bool(parts & {"fp8linear", "fp8linear_prefill"})
+    if "config3" in parts or lin_prefill:
         fp8_peak = _fp8_peak(dev)
     if fp8_peak is None:
         fp8_peak, fp8_kind = 2 * bf16_peak, "2 x measured bf16 GEMM"
@@ -544,46 +548,51 @@ def secondary(dev, peaks, with_reference: bool, only=None):
         torch.cuda.empty_cache()
     # ---- FP8 block-scaled linear: Qwen3-8B's QKV projection (K 4096 -> N 6144) at config 2's
     # decode batch (256 tokens, weight-streaming) and at the 8192-token prefill budget (tensor)
-    if "fp8linear" in parts:
+    if lin_decode or lin_prefill:
         from nanovllm_b200.fp8_linear import fp8_block_linear
         K, N = 4096, 6144
         g = torch.Generator(device=dev).manual_seed(91)
         sets = []
-        for _ in range(8):
+        for _ in range(8 if lin_decode else 1):
             w = (torch.randn(N, K, generator=g, device=dev) * 0.5).to(torch.float8_e4m3fn)
             ws = (torch.rand(N // 128, K // 128, generator=g, device=dev) * 0.02 + 0.001).to(
                 torch.bfloat16)
             x = torch.randn(256, K, generator=g, device=dev).to(torch.bfloat16)
             sets.append((x, w, ws))
-        d_ms = _time_graph_calls(lambda: [fp8_block_linear(*a) for a in sets], len(sets))
-        d_bytes = N * K + (N // 128) * (K // 128) * 2 + 256 * K * 2 + 256 * N * 2
-        d_gbs = d_bytes / (d_ms * 1e-3) / 1e9
-        xp = torch.randn(8192, K, generator=g, device=dev).to(torch.bfloat16)
-        w0, ws0 = sets[0][1], sets[0][2]
-        p_ms = _time_calls(lambda: fp8_block_linear(xp, w0, ws0), iters=10, warm=3, flush=flush)
-        p_flops = 2 * 8192 * N * K
-        p_tf = p_flops / (p_ms * 1e-3) / 1e12
-        out["fp8linear_qkv"] = {
+        lin = out["fp8linear_qkv"] = {
             "workload": "y = x . w^T, e4m3 weight 6144 x 4096 in 128 x 128 blocks (Qwen3-8B QKV "
-                        "projection), bf16 x quantised per token and 128-column group",
-            "decode_m256": {
+                        "projection), bf16 x quantised per token and 128-column group"}
+        if lin_decode:
+            d_ms = _time_graph_calls(lambda: [fp8_block_linear(*a) for a in sets], len(sets))
+            d_bytes = N * K + (N // 128) * (K // 128) * 2 + 256 * K * 2 + 256 * N * 2
+            d_gbs = d_bytes / (d_ms * 1e-3) / 1e9
+            lin["decode_m256"] = {
                 "ms": d_ms, "bytes": d_bytes, "tokens_per_s": 256 / (d_ms * 1e-3),
                 "timing": "CUDA graph of 8 back-to-back calls on 8 independent weight and input "
                           "sets (200 MB, more than L2), per call; quantise + GEMM",
                 "roofline": {"bound": "hbm", "achieved": d_gbs, "peak": hbm_peak, "unit": "GB/s",
-                             "frac": d_gbs / hbm_peak}},
-            "prefill_m8192": {
+                             "frac": d_gbs / hbm_peak}}
+            if ref is not None and "linear" in ref:
+                ref_time("fp8linear_decode_m256", lambda: [ref["linear"](*a) for a in sets],
+                         d_ms, ncalls=len(sets))
+        if lin_prefill:
+            xp = torch.randn(8192, K, generator=g, device=dev).to(torch.bfloat16)
+            w0, ws0 = sets[0][1], sets[0][2]
+            p_ms = _time_calls(lambda: fp8_block_linear(xp, w0, ws0), iters=10, warm=3,
+                               flush=flush)
+            p_flops = 2 * 8192 * N * K
+            p_tf = p_flops / (p_ms * 1e-3) / 1e12
+            lin["prefill_m8192"] = {
                 "ms": p_ms, "flops": p_flops, "tokens_per_s": 8192 / (p_ms * 1e-3),
                 "l2": "flushed before each call",
                 "roofline": {"bound": "tensor", "achieved": p_tf, "peak": fp8_peak,
-                             "unit": "TFLOP/s", "frac": p_tf / fp8_peak, "peak_kind": fp8_kind}}}
-        if ref is not None and "linear" in ref:
-            ours = fp8_block_linear(xp, w0, ws0)
-            ref_time("fp8linear_decode_m256", lambda: [ref["linear"](*a) for a in sets], d_ms,
-                     ncalls=len(sets))
-            ref_time("fp8linear_prefill_m8192", lambda: ref["linear"](xp, w0, ws0), p_ms, ours,
-                     iters=5, warm=2, flush_l2=flush)
-        del sets, xp
+                             "unit": "TFLOP/s", "frac": p_tf / fp8_peak, "peak_kind": fp8_kind}}
+            if ref is not None and "linear" in ref:
+                ours = fp8_block_linear(xp, w0, ws0)
+                ref_time("fp8linear_prefill_m8192", lambda: ref["linear"](xp, w0, ws0), p_ms,
+                         ours, iters=5, warm=2, flush_l2=flush)
+            del xp
+        del sets
         torch.cuda.empty_cache()
     return out, refgpu
 
@@ -770,7 +779,7 @@ def main():
                          "which then skip the secondary figures)")
     ap.add_argument("--only", default=None,
                     help="comma-separated secondary parts (%s) to run alone on one GPU, "
-                         "without the headline (profile captures)" % ",".join(PARTS))
+                         "without the headline (profile captures)" % ",".join(PARTS + SUBPARTS))
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world, rank, local = _dist_init() if args.impl == "ours" else (
@@ -782,7 +791,7 @@ def main():
             import torch
             from nanovllm_b200.fp8_attention import device_error
             only = args.only.split(",")
-            assert set(only) <= set(PARTS), only
+            assert set(only) <= set(PARTS) | set(SUBPARTS), only
             torch.cuda.set_device(0)
             sec, _ = secondary(torch.device("cuda", 0), _peaks(), False, only)
             sec["device_error"] = device_error()
