@@ -597,6 +597,87 @@ def secondary(dev, peaks, with_reference: bool, only=None):
     return out, refgpu
 
 
+def tp_linear_bench(world, rank, local, with_reference=True):
+    """Row-parallel FP8 o_proj with its all-reduce (one rank per GPU, N > 1; `--only tp_linear`
+    under torchrun): Qwen3-32B's o_proj (64 heads x 128 = 8,192 in, 5,120 out), each rank its
+    8,192 / N input columns, at 256 tokens (decode) and 8,192 tokens (prefill budget).  Three ways:
+    the fused kernel (fp8attn_fp8_tp_linear), this library's fp8_block_linear + NCCL all_reduce,
+    and the reference's Triton fp8_block_linear + NCCL all_reduce (RowParallelLinear.forward).
+    Each timed with CUDA events after a barrier, median of 10, max over ranks."""
+    import torch
+    import torch.distributed as dist
+    from nanovllm_b200.fp8_attention import device_error
+    from nanovllm_b200.fp8_linear import fp8_block_linear
+    from nanovllm_b200.tp_linear import TpLinearBuffers, fp8_row_parallel_linear
+    dev = torch.device("cuda", local)
+    ref, ref_err = _reference_module() if with_reference else (None, "not requested")
+    K, N = 8192, 5120
+    kl = K // world
+    fp8_peak = _fp8_peak(dev) or 2 * _peaks()[1]
+    g = torch.Generator(device=dev).manual_seed(100 + rank)
+    w = (torch.randn(N, kl, generator=g, device=dev) * 0.5).to(torch.float8_e4m3fn)
+    ws = (torch.rand(N // 128, kl // 128, generator=g, device=dev) * 0.02 + 0.001).to(
+        torch.bfloat16)
+    bufs = TpLinearBuffers(8192, N, device=dev)
+
+    def timed(fn, iters=10, warm=3):
+        for _ in range(warm):
+            fn()
+        ts = []
+        for _ in range(iters):
+            dist.barrier()
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            b.synchronize()
+            ts.append(a.elapsed_time(b))
+        return _reduce(statistics.median(ts), world, "max")
+
+    line = {"metric": "row-parallel FP8 o_proj + all-reduce", "n_gpus": world,
+            "workload": "Qwen3-32B o_proj, 8192 -> 5120, K split over the ranks, block-quantised "
+                        "e4m3 weight, bf16 activations; synthetic"}
+    for m in (256, 8192):
+        x = torch.randn(m, kl, generator=g, device=dev).to(torch.bfloat16)
+
+        def fused():
+            return fp8_row_parallel_linear(x, w, ws, bufs)
+
+        def nccl():
+            y = fp8_block_linear(x, w, ws)
+            dist.all_reduce(y)
+            return y
+
+        entry = {"fused_ms": timed(fused), "ours_gemm_plus_nccl_ms": timed(nccl)}
+        flops = 2 * m * N * K / world                    # per rank
+        link = 2 * m * N * 2 * (world - 1) / world       # bytes each rank sends over NVLink
+        target_ms = max(flops / (fp8_peak * 1e12), link / 770e9) * 1e3
+        entry["roofline"] = {"target_ms": target_ms, "frac": target_ms / entry["fused_ms"],
+                             "flops_per_rank": flops, "nvlink_bytes_per_rank": link,
+                             "fp8_peak_tflops": fp8_peak, "link_gbs": 770}
+        if ref is not None and "linear" in ref:
+            def refn():
+                y = ref["linear"](x, w, ws)
+                dist.all_reduce(y)
+                return y
+            entry["reference_ms"] = timed(refn)
+            entry["speedup_vs_reference"] = entry["reference_ms"] / entry["fused_ms"]
+            d = (fused().float() - refn().float()).abs().max()
+            dist.all_reduce(d, op=dist.ReduceOp.MAX)
+            entry["max_abs_diff_vs_reference"] = float(d)
+        line[f"m{m}"] = entry
+    if ref is None:
+        line["reference"] = ref_err
+    torch.cuda.synchronize()
+    err = torch.tensor([float(device_error(dev))], device=dev)
+    dist.all_reduce(err, op=dist.ReduceOp.MAX)
+    line["device_error"] = int(err.item())
+    del bufs
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def _e2e(case, steps, warmup, world, stream):
     """The headline call through the public API with host buffers: every step copies its inputs
     (q, block tables, lengths) from pinned host memory and its output back.  The copies run on a
@@ -779,7 +860,8 @@ def main():
                          "which then skip the secondary figures)")
     ap.add_argument("--only", default=None,
                     help="comma-separated secondary parts (%s) to run alone on one GPU, "
-                         "without the headline (profile captures)" % ",".join(PARTS + SUBPARTS))
+                         "without the headline (profile captures); or tp_linear under torchrun "
+                         "with N > 1 (the fused row-parallel o_proj)" % ",".join(PARTS + SUBPARTS))
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world, rank, local = _dist_init() if args.impl == "ours" else (
@@ -787,6 +869,9 @@ def main():
     try:
         if args.impl == "reference":
             run_reference(args, world, rank)
+        elif args.only == "tp_linear":
+            assert world > 1, "tp_linear runs under torchrun with N > 1"
+            tp_linear_bench(world, rank, local, not args.no_reference_gpu)
         elif args.only:
             import torch
             from nanovllm_b200.fp8_attention import device_error

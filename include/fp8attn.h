@@ -230,6 +230,36 @@ FP8ATTN_API int fp8attn_fp8_block_linear(const void* x, int64_t x_row_stride, co
                    void* workspace, int64_t workspace_bytes, void* stream);
 
 /*
+ * Row-parallel FP8 linear with its tensor-parallel all-reduce in one launch (replaces
+ * RowParallelLinear.forward, nanovllm/layers/linear.py:235-239, for block-quantised weights:
+ * y = fp8_block_linear(x_r, w_r, w_scale_r) on each rank, then dist.all_reduce(y)).
+ *   Rank r passes its K slice: x [M, K] bf16 (K = in_features / world), w [N, K] e4m3 and
+ *   w_scale [N / 128, K / 128] bf16 (the slices RowParallelLinear's loaders keep).  Each rank's
+ *   output rows of a 128 x 128 tile are rounded to bf16 (the reference's local result), written
+ *   over NVLink into the tile owner's receive buffer (owner = tile % world) and stamped; the owner
+ *   adds the world partials in rank order in fp32, rounds to bf16 and writes the tile into every
+ *   rank's output.  No host synchronisation and no collective library call.
+ *   buffers[r]: rank r's buffer of fp8attn_tp_linear_layout(max_tokens, N, world) bytes, as
+ *   mapped in this process (peer-accessible, e.g. torch symmetric memory), 256-byte aligned,
+ *   zero-filled before the first call; the same allocation on every rank.  The result is at
+ *   buffers[rank] + *out_offset, bf16 [M, N] rows N apart, complete when the launch ends and
+ *   valid until this rank's next call on the buffers.
+ *   epoch: this call's stamp, the same on every rank and larger than any earlier call's on the
+ *   buffers (1, 2, 3, ...).  Every rank must make the same calls in the same order; a rank whose
+ *   peers do not arrive gives up after 5 s and records 1 (wait timed out) in the workspace's
+ *   error word (fp8attn_read_error).
+ *   workspace: fp8attn_fp8_tp_linear_workspace_bytes(M, K) bytes, 16-byte aligned.
+ *   Sizes: N and K multiples of 128, 0 <= M <= max_tokens, 1 <= world <= 8.
+ */
+FP8ATTN_API int64_t fp8attn_tp_linear_layout(int64_t max_tokens, int N, int world,
+                   int64_t* out_offset, int64_t* recv_offset);
+FP8ATTN_API int64_t fp8attn_fp8_tp_linear_workspace_bytes(int64_t M, int K);
+FP8ATTN_API int fp8attn_fp8_tp_linear(const void* x, int64_t x_row_stride, const void* w,
+                   const void* w_scale, void* const* buffers, int rank, int world, uint64_t epoch,
+                   int64_t max_tokens, int64_t M, int N, int K, void* workspace,
+                   int64_t workspace_bytes, void* stream);
+
+/*
  * Self-checks of device-side mechanisms (no counterpart in the reference; used by the tests).
  *   fp8attn_diag_wait_timeout: num_ctas CTAs each claim one work item from the control block at
  *     `workspace` (ints: [0] error word, [1] next item, [2] CTAs finished, zeroed by the caller)

@@ -687,3 +687,106 @@ int fp8attn_fp8_block_linear(const void* x, int64_t x_row_stride, const void* w,
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------- row-parallel FP8 linear
+namespace {
+int64_t round256(int64_t v) { return (v + 255) & ~int64_t{255}; }
+
+struct TpLayout {
+  int64_t tiles_cap, flags_bytes, out_offset, recv_offset, total;
+};
+bool tp_layout(int64_t max_tokens, int N, int world, TpLayout* l) {
+  if (max_tokens <= 0 || N <= 0 || N % 128 != 0 || world < 1 || world > fp8attn::kMaxTpRanks)
+    return false;
+  l->tiles_cap = (max_tokens + fp8attn::kFp8GemmTokens - 1) / fp8attn::kFp8GemmTokens * (N / 128);
+  l->flags_bytes = round256(static_cast<int64_t>(world + 1) * l->tiles_cap * 8);
+  l->out_offset = l->flags_bytes;
+  l->recv_offset = l->out_offset + round256(max_tokens * N * 2);
+  l->total = l->recv_offset + round256(static_cast<int64_t>(world) * max_tokens * N * 2);
+  return true;
+}
+}  // namespace
+
+extern "C" {
+
+int64_t fp8attn_tp_linear_layout(int64_t max_tokens, int N, int world, int64_t* out_offset,
+                                 int64_t* recv_offset) {
+  TpLayout l;
+  if (!tp_layout(max_tokens, N, world, &l)) return -1;
+  if (out_offset) *out_offset = l.out_offset;
+  if (recv_offset) *recv_offset = l.recv_offset;
+  return l.total;
+}
+
+int64_t fp8attn_fp8_tp_linear_workspace_bytes(int64_t M, int K) {
+  if (M < 0 || K <= 0 || K % 128 != 0) return -1;
+  return round16(fp8attn::kCtrlInts * 4) + round16(M * K) + round16(M * (K / 128) * 2);
+}
+
+int fp8attn_fp8_tp_linear(const void* x, int64_t x_row_stride, const void* w, const void* w_scale,
+                          void* const* buffers, int rank, int world, uint64_t epoch,
+                          int64_t max_tokens, int64_t M, int N, int K, void* workspace,
+                          int64_t workspace_bytes, void* stream) {
+  int rc = check_linear_sizes(M, N, K);
+  if (rc) return rc;
+  TpLayout l;
+  if (!tp_layout(max_tokens, N, world, &l))
+    return fail(FP8ATTN_EINVAL, "tp linear: world must be 1..%d and max_tokens positive (got "
+                "world=%d max_tokens=%lld)", fp8attn::kMaxTpRanks, world,
+                static_cast<long long>(max_tokens));
+  if (rank < 0 || rank >= world)
+    return fail(FP8ATTN_EINVAL, "tp linear: rank %d outside 0..%d", rank, world - 1);
+  if (M > max_tokens)
+    return fail(FP8ATTN_EINVAL, "tp linear: M=%lld exceeds the buffers' max_tokens=%lld",
+                static_cast<long long>(M), static_cast<long long>(max_tokens));
+  if (epoch == 0) return fail(FP8ATTN_EINVAL, "tp linear: epoch must be >= 1");
+  if (buffers == nullptr) return fail(FP8ATTN_EINVAL, "tp linear: null buffer table");
+  for (int r = 0; r < world; ++r)
+    if (buffers[r] == nullptr || !aligned(buffers[r], 256))
+      return fail(FP8ATTN_EINVAL, "tp linear: buffer of rank %d is null or not 256-byte aligned",
+                  r);
+  if (M == 0) return FP8ATTN_OK;
+  const int64_t need = fp8attn_fp8_tp_linear_workspace_bytes(M, K);
+  if (workspace == nullptr || workspace_bytes < need || !aligned(workspace, 16))
+    return fail(FP8ATTN_EWORKSPACE, "tp linear: workspace of %lld bytes (16-byte aligned) "
+                "needed, got %lld", static_cast<long long>(need),
+                static_cast<long long>(workspace_bytes));
+  if (w == nullptr || w_scale == nullptr || !aligned(w, 16) || !aligned(w_scale, 2))
+    return fail(FP8ATTN_EINVAL, "tp linear: w (16-byte aligned) and w_scale must be given");
+  uint8_t* base = static_cast<uint8_t*>(workspace);
+  uint8_t* xq = base + round16(fp8attn::kCtrlInts * 4);
+  uint8_t* xs = xq + round16(M * K);
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  rc = run_quant(x, x_row_stride, xq, K, xs, M, K, st);
+  if (rc) return rc;
+  fp8attn::Fp8GemmParams p;
+  p.xq = xq;
+  p.xq_row_stride = K;
+  p.x_scale = reinterpret_cast<const uint16_t*>(xs);
+  p.w = static_cast<const uint8_t*>(w);
+  p.w_scale = static_cast<const uint16_t*>(w_scale);
+  p.out = nullptr;
+  p.out_row_stride = N;
+  p.err = static_cast<int*>(workspace);
+  p.partials = nullptr;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.splits = 1;
+  fp8attn::Fp8TpParams tp = {};
+  for (int r = 0; r < world; ++r) {
+    uint8_t* b = static_cast<uint8_t*>(buffers[r]);
+    tp.flags[r] = reinterpret_cast<unsigned long long*>(b);
+    tp.out[r] = reinterpret_cast<uint16_t*>(b + l.out_offset);
+    tp.recv[r] = reinterpret_cast<uint16_t*>(b + l.recv_offset);
+  }
+  tp.epoch = epoch;
+  tp.tiles_cap = l.tiles_cap;
+  tp.rank = rank;
+  tp.world = world;
+  const cudaError_t e = fp8attn::launch_fp8_tp_gemm(p, tp, device_sms(), st);
+  if (e == cudaErrorInvalidValue) return fail(FP8ATTN_EINVAL, "tp linear: tensor map rejected");
+  return e == cudaSuccess ? FP8ATTN_OK : cuda_fail(e, "tp linear launch");
+}
+
+}  // extern "C"

@@ -142,9 +142,116 @@ __device__ __forceinline__ GemmUnit gemm_unit(const Fp8GemmParams& p, int64_t u)
   return g;
 }
 
+// 64 fp32 values -> 64 bf16 at dst (16-byte aligned), as eight 16-byte stores.
+__device__ __forceinline__ void store_bf16x64(uint16_t* dst, const float (&v)[64]) {
+  uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    uint32_t w4[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const __nv_bfloat162 h2 = __floats2bfloat162_rn(v[8 * q + 2 * e], v[8 * q + 2 * e + 1]);
+      w4[e] = *reinterpret_cast<const uint32_t*>(&h2);
+    }
+    d[q] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+  }
+}
+
+// ---- cross-GPU stamps (peer memory; system scope)
+constexpr unsigned long long kPeerWaitLimitNs = 5000000000ull;  // 5 s: ranks launch at skewed times
+
+__device__ __forceinline__ void stamp_release(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long stamp_acquire(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+// Wait until *p >= epoch; gives up after kPeerWaitLimitNs, recording kDevErrWaitTimeout.
+__device__ __forceinline__ bool wait_stamp(const unsigned long long* p, unsigned long long epoch,
+                                           int* err) {
+  unsigned long long t0 = 0;
+  for (uint32_t polls = 0;; ++polls) {
+    if (stamp_acquire(p) >= epoch) return true;
+    if ((polls & 63u) == 63u) {
+      const unsigned long long now = globaltimer_ns();
+      if (t0 == 0) {
+        t0 = now;
+      } else if (now - t0 > kPeerWaitLimitNs) {
+        if (err) atomicExch(err, kDevErrWaitTimeout);
+        return false;
+      }
+    }
+    __nanosleep(128);
+  }
+}
+// Barrier of the 256 promotion threads (warps 0-7) only.
+__device__ __forceinline__ void promo_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+
+// Phases 2 and 3 of the row-parallel launch, run by the promotion threads after the GEMM units.
+// Phase 2: for each tile this rank owns (tiles rank, rank + world, ...; spread over the CTAs),
+// wait for every source's stamp, sum the world bf16 partials in rank order in fp32 (what an
+// all-reduce of the ranks' bf16 outputs computes), round to bf16, write the row to every rank's
+// `out` and stamp the tile final there.  Phase 3: wait until every tile of this rank's `out` is
+// stamped final, so the output is complete when the launch ends.
+__device__ void tp_reduce_gather(const Fp8GemmParams& p, const Fp8TpParams& tp, int tid) {
+  const int tiles_n = p.N / kBlk;
+  const int64_t tiles = ((p.M + kTok - 1) / kTok) * tiles_n;
+  const int row = tid >> 1, colh = tid & 1;  // thread: one row, 64 of the tile's 128 columns
+  // after one wait has given up, later waits of the same thread are skipped (the error word is
+  // set; the output is not valid), so a missing peer costs one limit, not one per tile
+  bool alive = true;
+  for (int64_t j = blockIdx.x;; j += gridDim.x) {
+    const int64_t t = tp.rank + j * tp.world;
+    if (t >= tiles) break;
+    if (tid == 0)
+      for (int s = 0; s < tp.world && alive; ++s)
+        alive = wait_stamp(tp.flags[tp.rank] + s * tp.tiles_cap + t, tp.epoch, p.err);
+    promo_sync();
+    const int64_t m = (t / tiles_n) * kTok + row;
+    const int n0 = static_cast<int>(t % tiles_n) * kBlk + 64 * colh;
+    if (m < p.M) {
+      float acc[64];
+#pragma unroll
+      for (int e = 0; e < 64; ++e) acc[e] = 0.f;
+      for (int s = 0; s < tp.world; ++s) {
+        // peers wrote these rows: read them from L2 (ld.global.cg), not from a stale L1 line
+        const uint4* src = reinterpret_cast<const uint4*>(
+            tp.recv[tp.rank] + (static_cast<int64_t>(s) * p.M + m) * p.N + n0);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const uint4 w = __ldcg(src + q);
+          const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            acc[8 * q + 2 * e] += __uint_as_float(ws[e] << 16);
+            acc[8 * q + 2 * e + 1] += __uint_as_float(ws[e] & 0xFFFF0000u);
+          }
+        }
+      }
+      for (int r = 0; r < tp.world; ++r) store_bf16x64(tp.out[r] + m * p.N + n0, acc);
+    }
+    __threadfence_system();
+    promo_sync();
+    if (tid == 0)
+      for (int r = 0; r < tp.world; ++r)
+        stamp_release(tp.flags[r] + static_cast<int64_t>(tp.world) * tp.tiles_cap + t, tp.epoch);
+  }
+  alive = true;
+  for (int64_t t = static_cast<int64_t>(blockIdx.x) * 256 + tid; t < tiles && alive;
+       t += static_cast<int64_t>(gridDim.x) * 256)
+    alive = wait_stamp(tp.flags[tp.rank] + static_cast<int64_t>(tp.world) * tp.tiles_cap + t,
+                       tp.epoch, p.err);
+}
+
+// kTP = false: the block-scaled GEMM.  kTP = true: the row-parallel launch -- each unit's bf16
+// tile goes to its owner's receive buffer and is stamped there, then tp_reduce_gather.
+template <bool kTP>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     fp8_block_gemm_kernel(const __grid_constant__ CUtensorMap tmx,
-                          const __grid_constant__ CUtensorMap tmw, const Fp8GemmParams p) {
+                          const __grid_constant__ CUtensorMap tmw, const Fp8GemmParams p,
+                          const Fp8TpParams tp) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   GemmSmem& sm = *reinterpret_cast<GemmSmem*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -278,14 +385,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const uint32_t lane_base = static_cast<uint32_t>(32 * quad) << 16;
     uint32_t r = 0;
     bool ok = true;
-    for (int64_t u = blockIdx.x; u < units && ok; u += gridDim.x) {
+    // In the row-parallel launch every promotion thread walks every unit, also after a failed
+    // wait, so that the per-unit barriers below always see all 256 threads.
+    for (int64_t u = blockIdx.x; u < units && (kTP || ok); u += gridDim.x) {
       const GemmUnit g = gemm_unit(p, u);
       const int64_t m = g.m0 + 32 * quad + lane;
       const bool active = g.m0 + 32 * quad < p.M;  // warp-uniform: some row of the warp is real
       float acc[64];
 #pragma unroll
       for (int j = 0; j < 64; ++j) acc[j] = 0.f;
-      for (int i = 0; i < g.nk; ++i, ++r) {
+      for (int i = 0; i < g.nk && ok; ++i, ++r) {
         const int stage = r % kGemmStages;
         const int buf = r % kDBufs;
         if (!mbar_wait(&sm.ss_full[stage], (r / kGemmStages) & 1, p.err) ||
@@ -313,29 +422,32 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           mbar_arrive(&sm.empty[stage]);
         }
       }
-      if (ok && m < p.M) {
-        const int n0 = g.nb * kBlk + 64 * half;
-        if (p.splits == 1) {
-          uint4* dst = reinterpret_cast<uint4*>(p.out + m * p.out_row_stride + n0);
+      const int n0 = g.nb * kBlk + 64 * half;
+      if constexpr (!kTP) {
+        if (ok && m < p.M) {
+          if (p.splits == 1) {
+            store_bf16x64(p.out + m * p.out_row_stride + n0, acc);
+          } else {
+            float4* dst = reinterpret_cast<float4*>(
+                p.partials + (static_cast<int64_t>(g.split) * p.M + m) * p.N + n0);
 #pragma unroll
-          for (int v = 0; v < 8; ++v) {
-            uint32_t w4[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const __nv_bfloat162 h2 = __floats2bfloat162_rn(acc[8 * v + 2 * e], acc[8 * v + 2 * e + 1]);
-              w4[e] = *reinterpret_cast<const uint32_t*>(&h2);
-            }
-            dst[v] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+            for (int v = 0; v < 16; ++v)
+              dst[v] = make_float4(acc[4 * v], acc[4 * v + 1], acc[4 * v + 2], acc[4 * v + 3]);
           }
-        } else {
-          float4* dst = reinterpret_cast<float4*>(
-              p.partials + (static_cast<int64_t>(g.split) * p.M + m) * p.N + n0);
-#pragma unroll
-          for (int v = 0; v < 16; ++v)
-            dst[v] = make_float4(acc[4 * v], acc[4 * v + 1], acc[4 * v + 2], acc[4 * v + 3]);
         }
+      } else {
+        // this rank's bf16 tile (the reference's local output) into the owner's receive buffer
+        const int64_t t = (g.m0 / kTok) * (p.N / kBlk) + g.nb;
+        const int owner = static_cast<int>(t % tp.world);
+        if (ok && m < p.M)
+          store_bf16x64(tp.recv[owner] + (static_cast<int64_t>(tp.rank) * p.M + m) * p.N + n0, acc);
+        __threadfence_system();
+        promo_sync();
+        if (tid == 0 && ok)
+          stamp_release(tp.flags[owner] + static_cast<int64_t>(tp.rank) * tp.tiles_cap + t, tp.epoch);
       }
     }
+    if constexpr (kTP) tp_reduce_gather(p, tp, tid);
   }
 
   tc::fence_before_sync();
@@ -438,8 +550,10 @@ int64_t fp8_gemm_workspace_bytes(int64_t M, int N, int K, int num_sms) {
   return kCtrlInts * 4 + (s > 1 ? static_cast<int64_t>(s) * M * N * 4 : 0);
 }
 
-cudaError_t launch_fp8_block_gemm(const Fp8GemmParams& p, int num_sms, cudaStream_t stream) {
-  if (p.M == 0) return cudaSuccess;
+namespace {
+template <bool kTP>
+cudaError_t launch_gemm_impl(const Fp8GemmParams& p, const Fp8TpParams& tp, int num_sms,
+                             cudaStream_t stream) {
   CUtensorMap tmx, tmw;
   if (!make_rows_map(&tmx, p.xq, p.M, p.K, p.xq_row_stride, kTok) ||
       !make_rows_map(&tmw, p.w, p.N, p.K, p.K, kBlk))
@@ -449,7 +563,7 @@ cudaError_t launch_fp8_block_gemm(const Fp8GemmParams& p, int num_sms, cudaStrea
   cudaGetDevice(&dev);
   const size_t smem = sizeof(GemmSmem) + 1024;
   if (dev >= 0 && dev < 64 && !configured[dev]) {
-    cudaFuncSetAttribute(fp8_block_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaFuncSetAttribute(fp8_block_gemm_kernel<kTP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          static_cast<int>(smem));
     configured[dev] = true;
   }
@@ -466,7 +580,7 @@ cudaError_t launch_fp8_block_gemm(const Fp8GemmParams& p, int num_sms, cudaStrea
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, fp8_block_gemm_kernel, tmx, tmw, p);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, fp8_block_gemm_kernel<kTP>, tmx, tmw, p, tp);
   if (e != cudaSuccess || p.splits == 1) return e;
   const int64_t quads = p.M * (p.N / 4);
   cudaLaunchConfig_t rcfg = {};
@@ -476,6 +590,19 @@ cudaError_t launch_fp8_block_gemm(const Fp8GemmParams& p, int num_sms, cudaStrea
   rcfg.attrs = attr;
   rcfg.numAttrs = 1;
   return cudaLaunchKernelEx(&rcfg, fp8_split_reduce_kernel, p);
+}
+}  // namespace
+
+cudaError_t launch_fp8_block_gemm(const Fp8GemmParams& p, int num_sms, cudaStream_t stream) {
+  if (p.M == 0) return cudaSuccess;
+  return launch_gemm_impl<false>(p, Fp8TpParams{}, num_sms, stream);
+}
+
+cudaError_t launch_fp8_tp_gemm(const Fp8GemmParams& p, const Fp8TpParams& tp, int num_sms,
+                               cudaStream_t stream) {
+  if (p.M == 0) return cudaSuccess;
+  if (p.splits != 1 || tp.world < 1 || tp.world > kMaxTpRanks) return cudaErrorInvalidValue;
+  return launch_gemm_impl<true>(p, tp, num_sms, stream);
 }
 
 }  // namespace fp8attn

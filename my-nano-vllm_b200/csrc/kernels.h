@@ -85,6 +85,26 @@ int fp8_gemm_splits(int64_t M, int N, int K, int num_sms);
 int64_t fp8_gemm_workspace_bytes(int64_t M, int N, int K, int num_sms);
 cudaError_t launch_fp8_block_gemm(const Fp8GemmParams& p, int num_sms, cudaStream_t stream);
 
+// Row-parallel FP8 linear with the tensor-parallel all-reduce over peer memory (one kernel).
+// Every rank computes y_r = x_r . w_r^T on its K slice; output tile t (128 tokens x 128 features,
+// t = token tile * N/128 + feature block) belongs to rank t % world.  Pointers are each rank's
+// buffers as mapped in this process (index = rank).  Per rank:
+//   recv  bf16 [world][M][N]: the partial tile of source s at rows s * M + m;
+//   out   bf16 [M][N]: the all-reduced output;
+//   flags u64 [world + 1][tiles_cap]: row s < world = the call's stamp once source s's partial of
+//         tile t has landed here; row world = the stamp once tile t's final values are in `out`.
+constexpr int kMaxTpRanks = 8;
+struct Fp8TpParams {
+  uint16_t* recv[kMaxTpRanks];
+  uint16_t* out[kMaxTpRanks];
+  unsigned long long* flags[kMaxTpRanks];
+  unsigned long long epoch;  // this call's stamp: larger than every earlier call's on the buffers
+  int64_t tiles_cap;         // flags per row
+  int rank, world;
+};
+cudaError_t launch_fp8_tp_gemm(const Fp8GemmParams& p, const Fp8TpParams& tp, int num_sms,
+                               cudaStream_t stream);
+
 // ------------------------------------------------------------------ decode engine
 // Control block at the head of the decode workspace (ints):
 //   [0] sticky device error code, [1] next work item, [2] CTAs finished.

@@ -60,6 +60,13 @@ def _load() -> ctypes.CDLL:
     lib.fp8attn_fp8_dyn_quant.argtypes = [vp, i64, vp, i64, vp, i64, i32, vp]
     lib.fp8attn_fp8_block_gemm.restype = i32
     lib.fp8attn_fp8_block_gemm.argtypes = [vp, i64, vp, vp, vp, vp, i64, i64, i32, i32, vp, i64, vp]
+    lib.fp8attn_tp_linear_layout.restype = i64
+    lib.fp8attn_tp_linear_layout.argtypes = [i64, i32, i32, vp, vp]
+    lib.fp8attn_fp8_tp_linear_workspace_bytes.restype = i64
+    lib.fp8attn_fp8_tp_linear_workspace_bytes.argtypes = [i64, i32]
+    lib.fp8attn_fp8_tp_linear.restype = i32
+    lib.fp8attn_fp8_tp_linear.argtypes = [vp, i64, vp, vp, vp, i32, i32, ctypes.c_uint64, i64,
+                                          i64, i32, i32, vp, i64, vp]
     lib.fp8attn_fp8_block_linear.restype = i32
     lib.fp8attn_fp8_block_linear.argtypes = [vp, i64, vp, vp, vp, i64, i64, i32, i32, vp, i64, vp]
     lib.fp8attn_diag_wait_timeout.restype = i32

@@ -114,3 +114,27 @@ def block_linear(x_bits: np.ndarray, w: np.ndarray, ws_bits: np.ndarray) -> np.n
     """y bf16 bits [M, N] of fp8_block_linear: quantise x, then the block-scaled GEMM."""
     xq, xs = dyn_quant(x_bits)
     return block_gemm(xq, xs, w, ws_bits)
+
+
+def rank_slices(x_bits: np.ndarray, w: np.ndarray, ws_bits: np.ndarray, rank: int, world: int):
+    """Rank ``rank``'s share of a row-parallel layer, as RowParallelLinear keeps it
+    (nanovllm/layers/linear.py:215-232): columns [r K/world, (r+1) K/world) of the activation and
+    the weight, and the matching block columns of the weight scale (dim 1)."""
+    k = x_bits.shape[1]
+    kl = k // world
+    return (np.ascontiguousarray(x_bits[:, rank * kl:(rank + 1) * kl]),
+            np.ascontiguousarray(w[:, rank * kl:(rank + 1) * kl]),
+            np.ascontiguousarray(ws_bits[:, rank * kl // BLOCK:(rank + 1) * kl // BLOCK]))
+
+
+def row_parallel_linear(x_bits: np.ndarray, w: np.ndarray, ws_bits: np.ndarray,
+                        world: int) -> np.ndarray:
+    """RowParallelLinear.forward over ``world`` ranks (nanovllm/layers/linear.py:235-239): each
+    rank's fp8_block_linear of its slice (bf16), then the all-reduce: the ranks' bf16 values added
+    in rank order in fp32 and rounded to bf16 (for two ranks this is what NCCL's sum gives; with
+    more, NCCL's order and intermediate rounding may differ by a bf16 step)."""
+    acc = None
+    for r in range(world):
+        part = bf16_bits_to_f32(block_linear(*rank_slices(x_bits, w, ws_bits, r, world)))
+        acc = part if acc is None else (acc + part).astype(np.float32)
+    return f32_to_bf16_bits(acc)

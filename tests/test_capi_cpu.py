@@ -120,3 +120,33 @@ def test_fp8_linear_rejects_bad_arguments():
     assert lin(4096, 1024, 4096, 4096, 4096, 256, 4, 256, 1000, 4096, 1 << 20, None) == _lib.EINVAL
     assert lin(4096, 1024, 4096, 4096, 4096, 256, 4, 256, 1024, 4096, 64, None) == _lib.EWORKSPACE
     assert "workspace" in lib.fp8attn_last_error().decode()
+
+
+def test_tp_linear_layout_and_rejects_bad_arguments():
+    lib = _lib.lib
+    out_off, recv_off = ctypes.c_int64(), ctypes.c_int64()
+    total = lib.fp8attn_tp_linear_layout(1000, 1024, 2, ctypes.byref(out_off),
+                                         ctypes.byref(recv_off))
+    tiles = 8 * 8                                   # ceil(1000 / 128) token tiles x 1024 / 128
+    assert out_off.value == (3 * tiles * 8 + 255) // 256 * 256
+    assert recv_off.value == out_off.value + 1000 * 1024 * 2
+    assert total == recv_off.value + 2 * 1000 * 1024 * 2
+    assert lib.fp8attn_tp_linear_layout(1000, 1000, 2, None, None) == -1
+    assert lib.fp8attn_tp_linear_layout(1000, 1024, 0, None, None) == -1
+    assert lib.fp8attn_fp8_tp_linear_workspace_bytes(10, 100) == -1
+    table = (ctypes.c_void_p * 2)(4096, 8192)
+    f = lib.fp8attn_fp8_tp_linear
+    args = [4096, 1024, 4096, 4096, table, 0, 2, 1, 256, 64, 1024, 1024, 4096, 1 << 20, None]
+    for i, v in ((5, 2), (6, 9), (7, 0), (8, 32), (10, 1000)):   # rank, world, epoch, max, N
+        bad = list(args)
+        bad[i] = v
+        assert f(*bad) == _lib.EINVAL, (i, v)
+    bad = list(args)
+    bad[4] = (ctypes.c_void_p * 2)(4096, 8200)       # a buffer not 256-byte aligned
+    assert f(*bad) == _lib.EINVAL
+    bad = list(args)
+    bad[13] = 64                                      # workspace too small
+    assert f(*bad) == _lib.EWORKSPACE
+    bad = list(args)
+    bad[9] = 0                                        # no rows: nothing to do
+    assert f(*bad) == _lib.OK

@@ -90,3 +90,55 @@ def test_config5_shards_are_slices_of_the_unsharded_batch():
                                full.k_cache.view(torch.uint8)[:, :, k0:k1])
             assert torch.equal(part.v_cache.view(torch.uint8),
                                full.v_cache.view(torch.uint8)[:, :, k0:k1])
+
+
+def _tp_linear_rank(rank, world, port, results):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from oracle import fp8_linear as ofl
+        x, w, ws = _tp_linear_inputs()
+        part = ofl.block_linear(*ofl.rank_slices(x, w, ws, rank, world))  # this rank's bf16 y_r
+        y = torch.from_numpy(ofl.bf16_bits_to_f32(part).copy())
+        dist.all_reduce(y)                                                 # linear.py:238
+        if rank == 0:
+            results.put(ofl.f32_to_bf16_bits(y.numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+def _tp_linear_inputs():
+    import numpy as np
+    g = torch.Generator().manual_seed(23)
+    x = (torch.randn(9, 512, generator=g) * 2).to(torch.bfloat16)
+    w = (torch.randn(256, 512, generator=g) * 0.5).to(torch.float8_e4m3fn)
+    ws = (torch.rand(2, 4, generator=g) * 0.02 + 0.001).to(torch.bfloat16)
+    return (x.view(torch.int16).numpy().view(np.uint16), w.view(torch.uint8).numpy(),
+            ws.view(torch.int16).numpy().view(np.uint16))
+
+
+def test_row_parallel_linear_shards_and_all_reduce():
+    """RowParallelLinear over two gloo ranks (nanovllm/layers/linear.py:215-239): each rank keeps
+    its K slice of x, w and the scale's block columns, computes its bf16 partial, and the sum over
+    ranks equals the restatement the fused kernel follows (oracle.fp8_linear.row_parallel_linear)
+    exactly, and the unsharded layer within the rounding of the partials."""
+    import numpy as np
+    from oracle import fp8_linear as ofl
+    world = 2
+    ctx = mp.get_context("spawn")
+    results = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_tp_linear_rank, args=(r, world, port, results))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    got = results.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    x, w, ws = _tp_linear_inputs()
+    assert np.array_equal(got, ofl.row_parallel_linear(x, w, ws, world))
+    full = ofl.bf16_bits_to_f32(ofl.block_linear(x, w, ws)).astype(np.float64)
+    err = np.abs(ofl.bf16_bits_to_f32(got) - full)
+    assert bool((err <= 2.0 ** -6 * np.abs(full) + 2e-3 * np.abs(full).max()).all()), err.max()
