@@ -101,6 +101,10 @@ struct __align__(1024) GemmSmem {
   uint64_t empty[kGemmStages];          // the MMA's commit and every promotion warp
   uint64_t d_full[kDBufs];              // D buffer complete
   uint64_t d_empty[kDBufs];             // D buffer read by every promotion warp
+  // the row-parallel launch's bf16 output tile, 128 rows x 16 chunks of 16 bytes, chunk c of row
+  // r at r * 16 + (c ^ (r & 15)) (spread over the banks); lets the copy to the owner run as
+  // whole rows
+  uint4 stage[kTok * 16];
   uint32_t tmem_base;
 };
 static_assert(sizeof(GemmSmem) + 1024 <= 227 * 1024, "smem");
@@ -189,16 +193,26 @@ __device__ __forceinline__ bool wait_stamp(const unsigned long long* p, unsigned
 // Barrier of the 256 promotion threads (warps 0-7) only.
 __device__ __forceinline__ void promo_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
+// Before a stamp that publishes the promotion threads' stores to other GPUs: one system-scope
+// fence per warp, by lane 0 after the warp's lanes have synchronised; the barrier that follows
+// and the stamping thread's release carry them on (the fences are cumulative).  A fence in every
+// thread cost ~20 us per tile: system-scope fences of an SM's threads run one after another.
+__device__ __forceinline__ void publish_fence(int lane) {
+  __syncwarp();
+  if (lane == 0) __threadfence_system();
+}
+
 // Phases 2 and 3 of the row-parallel launch, run by the promotion threads after the GEMM units.
 // Phase 2: for each tile this rank owns (tiles rank, rank + world, ...; spread over the CTAs),
 // wait for every source's stamp, sum the world bf16 partials in rank order in fp32 (what an
-// all-reduce of the ranks' bf16 outputs computes), round to bf16, write the row to every rank's
-// `out` and stamp the tile final there.  Phase 3: wait until every tile of this rank's `out` is
-// stamped final, so the output is complete when the launch ends.
+// all-reduce of the ranks' bf16 outputs computes), round to bf16 and write the rows to every
+// rank's `out`; then, once for all of the CTA's tiles, fence and stamp them final on every rank
+// (a fence waits for the remote writes' acknowledgements: one per tile cost ~30 us each).
+// Phase 3: wait until every tile of this rank's `out` is stamped final, so the output is complete
+// when the launch ends.
 __device__ void tp_reduce_gather(const Fp8GemmParams& p, const Fp8TpParams& tp, int tid) {
   const int tiles_n = p.N / kBlk;
   const int64_t tiles = ((p.M + kTok - 1) / kTok) * tiles_n;
-  const int row = tid >> 1, colh = tid & 1;  // thread: one row, 64 of the tile's 128 columns
   // after one wait has given up, later waits of the same thread are skipped (the error word is
   // set; the output is not valid), so a missing peer costs one limit, not one per tile
   bool alive = true;
@@ -209,34 +223,47 @@ __device__ void tp_reduce_gather(const Fp8GemmParams& p, const Fp8TpParams& tp, 
       for (int s = 0; s < tp.world && alive; ++s)
         alive = wait_stamp(tp.flags[tp.rank] + s * tp.tiles_cap + t, tp.epoch, p.err);
     promo_sync();
-    const int64_t m = (t / tiles_n) * kTok + row;
-    const int n0 = static_cast<int>(t % tiles_n) * kBlk + 64 * colh;
-    if (m < p.M) {
-      float acc[64];
-#pragma unroll
-      for (int e = 0; e < 64; ++e) acc[e] = 0.f;
+    // thread: 16-byte chunks tid, tid + 256, ... of the tile (row = chunk / 16), so a warp reads
+    // and writes two whole 256-byte rows per instruction
+    const int64_t m0 = (t / tiles_n) * kTok;
+    const int nbase = static_cast<int>(t % tiles_n) * kBlk;
+#pragma unroll 2
+    for (int i = 0; i < 8; ++i) {
+      const int c = tid + 256 * i, r16 = c >> 4, col = c & 15;
+      const int64_t m = m0 + r16;
+      if (m >= p.M) continue;
+      float a8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
       for (int s = 0; s < tp.world; ++s) {
         // peers wrote these rows: read them from L2 (ld.global.cg), not from a stale L1 line
-        const uint4* src = reinterpret_cast<const uint4*>(
-            tp.recv[tp.rank] + (static_cast<int64_t>(s) * p.M + m) * p.N + n0);
+        const uint4 w = __ldcg(reinterpret_cast<const uint4*>(
+            tp.recv[tp.rank] + (static_cast<int64_t>(s) * p.M + m) * p.N + nbase + 8 * col));
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const uint4 w = __ldcg(src + q);
-          const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            acc[8 * q + 2 * e] += __uint_as_float(ws[e] << 16);
-            acc[8 * q + 2 * e + 1] += __uint_as_float(ws[e] & 0xFFFF0000u);
-          }
+        for (int e = 0; e < 4; ++e) {
+          a8[2 * e] += __uint_as_float(ws[e] << 16);
+          a8[2 * e + 1] += __uint_as_float(ws[e] & 0xFFFF0000u);
         }
       }
-      for (int r = 0; r < tp.world; ++r) store_bf16x64(tp.out[r] + m * p.N + n0, acc);
-    }
-    __threadfence_system();
-    promo_sync();
-    if (tid == 0)
+      uint32_t v[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const __nv_bfloat162 h2 = __floats2bfloat162_rn(a8[2 * e], a8[2 * e + 1]);
+        v[e] = *reinterpret_cast<const uint32_t*>(&h2);
+      }
       for (int r = 0; r < tp.world; ++r)
-        stamp_release(tp.flags[r] + static_cast<int64_t>(tp.world) * tp.tiles_cap + t, tp.epoch);
+        *reinterpret_cast<uint4*>(tp.out[r] + m * p.N + nbase + 8 * col) =
+            make_uint4(v[0], v[1], v[2], v[3]);
+    }
+    promo_sync();  // before tid 0 waits for the next tile
+  }
+  // publish the owned tiles' final rows: one fence per warp, then the stamps on every rank
+  publish_fence(tid & 31);
+  promo_sync();
+  for (int64_t j = blockIdx.x + static_cast<int64_t>(tid) * gridDim.x;; j += 256LL * gridDim.x) {
+    const int64_t t = tp.rank + j * tp.world;
+    if (t >= tiles) break;
+    for (int r = 0; r < tp.world; ++r)
+      stamp_release(tp.flags[r] + static_cast<int64_t>(tp.world) * tp.tiles_cap + t, tp.epoch);
   }
   alive = true;
   for (int64_t t = static_cast<int64_t>(blockIdx.x) * 256 + tid; t < tiles && alive;
@@ -439,15 +466,50 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         // this rank's bf16 tile (the reference's local output) into the owner's receive buffer
         const int64_t t = (g.m0 / kTok) * (p.N / kBlk) + g.nb;
         const int owner = static_cast<int>(t % tp.world);
-        if (ok && m < p.M)
-          store_bf16x64(tp.recv[owner] + (static_cast<int64_t>(tp.rank) * p.M + m) * p.N + n0, acc);
-        __threadfence_system();
+        // through shared memory, so that the copy to the owner (often over NVLink) runs as whole
+        // 256-byte rows: a thread's row-wise 16-byte stores would each be a separate small write
+        const int row = 32 * quad + lane;
+        if (ok) {
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            uint32_t w4[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const __nv_bfloat162 h2 =
+                  __floats2bfloat162_rn(acc[8 * q + 2 * e], acc[8 * q + 2 * e + 1]);
+              w4[e] = *reinterpret_cast<const uint32_t*>(&h2);
+            }
+            sm.stage[row * 16 + ((8 * half + q) ^ (row & 15))] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+          }
+        }
         promo_sync();
-        if (tid == 0 && ok)
-          stamp_release(tp.flags[owner] + static_cast<int64_t>(tp.rank) * tp.tiles_cap + t, tp.epoch);
+        uint16_t* dst = tp.recv[owner] + (static_cast<int64_t>(tp.rank) * p.M + g.m0) * p.N +
+                        g.nb * kBlk;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int c = tid + 256 * i, r16 = c >> 4, col = c & 15;
+          if (ok && g.m0 + r16 < p.M)
+            *reinterpret_cast<uint4*>(dst + static_cast<int64_t>(r16) * p.N + 8 * col) =
+                sm.stage[r16 * 16 + (col ^ (r16 & 15))];
+        }
+        promo_sync();  // the stage is rewritten by the next unit
       }
     }
-    if constexpr (kTP) tp_reduce_gather(p, tp, tid);
+    if constexpr (kTP) {
+      // publish this CTA's tiles: one fence per warp, then the stamps, one thread a unit
+      publish_fence(lane);
+      promo_sync();
+      if (ok) {
+        for (int64_t u = blockIdx.x + static_cast<int64_t>(tid) * gridDim.x; u < units;
+             u += static_cast<int64_t>(256) * gridDim.x) {
+          const GemmUnit g = gemm_unit(p, u);
+          const int64_t t = (g.m0 / kTok) * (p.N / kBlk) + g.nb;
+          stamp_release(tp.flags[t % tp.world] + static_cast<int64_t>(tp.rank) * tp.tiles_cap + t,
+                        tp.epoch);
+        }
+      }
+      tp_reduce_gather(p, tp, tid);
+    }
   }
 
   tc::fence_before_sync();
