@@ -224,30 +224,47 @@ __device__ void tp_reduce_gather(const Fp8GemmParams& p, const Fp8TpParams& tp, 
         alive = wait_stamp(tp.flags[tp.rank] + s * tp.tiles_cap + t, tp.epoch, p.err);
     promo_sync();
     // thread: 16-byte chunks tid, tid + 256, ... of the tile (row = chunk / 16), so a warp reads
-    // and writes two whole 256-byte rows per instruction
+    // and writes two whole 256-byte rows per instruction; sources outermost, so that the eight
+    // chunks' loads of one source are in flight together (each element still sums the sources
+    // in rank order)
     const int64_t m0 = (t / tiles_n) * kTok;
     const int nbase = static_cast<int>(t % tiles_n) * kBlk;
-#pragma unroll 2
+    float a8[8][8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) a8[i][e] = 0.f;
+    for (int s = 0; s < tp.world; ++s) {
+      uint4 w[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int c = tid + 256 * i, r16 = c >> 4, col = c & 15;
+        const int64_t m = m0 + r16;
+        // peers wrote these rows: read them from L2 (ld.global.cg), not from a stale L1 line
+        w[i] = m < p.M ? __ldcg(reinterpret_cast<const uint4*>(
+                             tp.recv[tp.rank] + (static_cast<int64_t>(s) * p.M + m) * p.N + nbase +
+                             8 * col))
+                       : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const uint32_t ws[4] = {w[i].x, w[i].y, w[i].z, w[i].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          a8[i][2 * e] += __uint_as_float(ws[e] << 16);
+          a8[i][2 * e + 1] += __uint_as_float(ws[e] & 0xFFFF0000u);
+        }
+      }
+    }
+#pragma unroll
     for (int i = 0; i < 8; ++i) {
       const int c = tid + 256 * i, r16 = c >> 4, col = c & 15;
       const int64_t m = m0 + r16;
       if (m >= p.M) continue;
-      float a8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      for (int s = 0; s < tp.world; ++s) {
-        // peers wrote these rows: read them from L2 (ld.global.cg), not from a stale L1 line
-        const uint4 w = __ldcg(reinterpret_cast<const uint4*>(
-            tp.recv[tp.rank] + (static_cast<int64_t>(s) * p.M + m) * p.N + nbase + 8 * col));
-        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          a8[2 * e] += __uint_as_float(ws[e] << 16);
-          a8[2 * e + 1] += __uint_as_float(ws[e] & 0xFFFF0000u);
-        }
-      }
       uint32_t v[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const __nv_bfloat162 h2 = __floats2bfloat162_rn(a8[2 * e], a8[2 * e + 1]);
+        const __nv_bfloat162 h2 = __floats2bfloat162_rn(a8[i][2 * e], a8[i][2 * e + 1]);
         v[e] = *reinterpret_cast<const uint32_t*>(&h2);
       }
       for (int r = 0; r < tp.world; ++r)
