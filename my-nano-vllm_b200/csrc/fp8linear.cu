@@ -31,7 +31,11 @@
 //            acc += D * scale product in fp32 registers (packed fp32x2 fused multiply-adds),
 //            block by block in K order (the reference's per-block scaling, which the tensor cores
 //            cannot apply: the scales are arbitrary fp32, not powers of two); at a unit's end it
-//            writes its 64 outputs (or its range's partial sums) as 16-byte stores.
+//            writes its 64 bf16 outputs as 16-byte stores, or, with split-K, its range's fp32
+//            partial sums through a shared-memory stage that the 256 threads copy out as whole
+//            rows.
+// The row-parallel form (kTP) sends each bf16 tile through the same stage to the rank that owns
+// it and adds the ranks' tiles there (tp_reduce_gather).
 #include "common.cuh"
 #include "kernels.h"
 #include "tcgen05.cuh"
