@@ -150,3 +150,36 @@ def test_tp_linear_layout_and_rejects_bad_arguments():
     bad = list(args)
     bad[9] = 0                                        # no rows: nothing to do
     assert f(*bad) == _lib.OK
+
+
+def _splits(m, n, k, sms=148):
+    """The GEMM's split-K rule: only with fewer output tiles (128 tokens x 128 features) than SMs,
+    the number of K ranges s minimising ceil(units / SMs) * ceil(blocks / s), the smaller on ties,
+    with every range non-empty."""
+    base = (n // 128) * ((m + 127) // 128)
+    kc = k // 128
+    if base >= sms:
+        return 1
+    best, best_cost = 1, -(-base // sms) * kc
+    for s in range(2, min(16, kc) + 1):
+        per = -(-kc // s)
+        if -(-kc // per) != s:
+            continue
+        cost = -(-(base * s) // sms) * per
+        if cost < best_cost:
+            best, best_cost = s, cost
+    return best
+
+
+def test_fp8_gemm_split_policy_and_workspace_sizes():
+    """Without a GPU the library assumes 148 SMs (a B200).  Without split-K the output equals the
+    reference's Triton kernel bit for bit; with it, within the accumulation-order bound."""
+    lib = _lib.lib
+    for m in (1, 37, 128, 256, 1000, 8192):
+        for n in (1024, 4096, 6144):
+            for k in (1024, 4096, 12288):
+                s = _splits(m, n, k)
+                want = 256 + (s * m * n * 4 if s > 1 else 0)
+                assert lib.fp8attn_fp8_gemm_workspace_bytes(m, n, k) == want, (m, n, k, s)
+    assert _splits(8192, 6144, 4096) == 1      # the prefill-size QKV projection: no split
+    assert _splits(256, 6144, 4096) == 3       # the decode-size one: three K ranges
